@@ -1,0 +1,868 @@
+// CUDA kernels of the decode path (sm_100a) and their launchers.
+//
+// Every kernel reproduces the reference's IEEE operation order (see
+// mi_device.cuh); the comment above each names the reference code it
+// replaces.
+#include <algorithm>
+#include <cstdio>
+
+#include "mi_device.cuh"
+
+namespace mi {
+
+namespace {
+
+constexpr unsigned FULL = 0xffffffffu;
+
+// Shared-memory map of the GEMV kernel, computed identically on host and
+// device: [0,64) mbarriers, [64,128) broadcast scalars, activation quants,
+// activation scales, per-row results, F32 input staging (norm prologues),
+// then n_stages weight stages of stage_rows rows each (quants, then scales).
+struct GemvSmem {
+  size_t act_qs, act_d, res, xs, stages, stage_bytes, total;
+};
+
+__host__ __device__ inline GemvSmem gemv_smem(int64_t K, int32_t rows_per_cta, int32_t stage_rows,
+                                              int32_t n_stages, int32_t pro) {
+  GemvSmem L;
+  size_t off = 128;
+  L.act_qs = off;
+  off += (size_t)((K + 15) / 16 * 16);
+  L.act_d = off;
+  off += (size_t)((K / 32 * 4 + 15) / 16 * 16);
+  L.res = off;
+  off += (size_t)(((int64_t)rows_per_cta * 4 + 15) / 16 * 16);
+  L.xs = off;
+  if (pro >= PRO_NORM_QUANT) off += (size_t)(K * 4);
+  off = (off + 127) / 128 * 128;
+  L.stages = off;
+  L.stage_bytes = (size_t)(((int64_t)stage_rows * K + (int64_t)stage_rows * (K / 32) * 2 + 127) / 128 * 128);
+  off += (size_t)n_stages * L.stage_bytes;
+  L.total = off;
+  return L;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Q8_0 GEMV: out[r] = dot(W row r, act) for the CTA's contiguous rows.
+//
+// Replaces mi_compute_mul_mat's Q8_0 branch (ref src/ops_cpu.cpp:226-237) and
+// the quantize node in front of it (src/ops_cpu.cpp:462-479). Per row, eight
+// lanes each keep the AVX2 kernel's accumulator chain (ref
+// src/quant_avx2.cpp:170-181): lane j of block i adds the int32 dot of bytes
+// 4j..4j+3 (one dp4a, exactly the maddubs+madd lane partial) times
+// fp16(w.d)*a.d with one FMA, blocks in order; the row result is the hsum_ps
+// order ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7)) (src/quant_avx2.cpp:74-83).
+//
+// Data flow: thread 0 issues bulk async copies of the CTA's weight rows into
+// shared-memory stages before waiting on the previous kernel (programmatic
+// dependent launch), so weight streaming overlaps the predecessor; then the
+// prologue builds the quantized activation in shared memory (optionally after
+// the embedding lookup and rms_norm), the warps consume the stages, and the
+// epilogue applies bias / residual / SiLU*up / argmax.
+// ---------------------------------------------------------------------------
+template <int NT>
+__global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int NW = NT / 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t K = p.K;
+  const int nb = (int)(K >> 5);
+  const GemvSmem L = gemv_smem(K, p.rows_per_cta, p.stage_rows, p.n_stages, p.pro);
+  uint64_t* bars = (uint64_t*)smem;
+  float* misc = (float*)(smem + 64);
+  int8_t* aq = (int8_t*)(smem + L.act_qs);
+  float* ad = (float*)(smem + L.act_d);
+  float* res = (float*)(smem + L.res);
+  float* xs = (float*)(smem + L.xs);
+  uint8_t* stages = smem + L.stages;
+
+  const int64_t r0 = (int64_t)blockIdx.x * p.rows_per_cta;
+  const int64_t r1 = min(r0 + (int64_t)p.rows_per_cta, p.n_pad);
+  const int nrows = (int)(r1 - r0);
+  const int n_tiles = (nrows + p.stage_rows - 1) / p.stage_rows;
+  const uint8_t* wq = p.w;
+  const uint8_t* wd = p.w + p.n_pad * K;
+
+  auto issue = [&](int t) {
+    const int s = t % p.n_stages;
+    const int64_t tr0 = r0 + (int64_t)t * p.stage_rows;
+    const int rows = (int)min((int64_t)p.stage_rows, r1 - tr0);
+    const uint32_t qb = (uint32_t)(rows * K), db = (uint32_t)(rows * nb * 2);
+    uint8_t* st = stages + (size_t)s * L.stage_bytes;
+    mbar_arrive_expect_tx(&bars[s], qb + db);
+    bulk_load(st, wq + tr0 * K, qb, &bars[s]);
+    bulk_load(st + (size_t)p.stage_rows * K, wd + tr0 * nb * 2, db, &bars[s]);
+  };
+
+  if (tid == 0) {
+    for (int s = 0; s < p.n_stages; s++) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (int t = 0; t < min(n_tiles, p.n_stages); t++) issue(t);
+  pdl_trigger();
+  pdl_wait();
+
+  // ---- prologue: the quantized activation in shared memory ----
+  if (p.pro == PRO_ACT) {
+    for (int b = tid; b < nb; b += NT) {
+      const uint8_t* src = p.act + (size_t)b * 36;
+      ad[b] = *(const float*)src;
+      const uint32_t* sq = (const uint32_t*)(src + 4);
+      uint32_t* dq = (uint32_t*)(aq + 32 * b);
+#pragma unroll
+      for (int k = 0; k < 8; k++) dq[k] = sq[k];
+    }
+  } else {
+    float scale = 1.0f;
+    if (p.pro >= PRO_NORM_QUANT) {
+      if (p.pro == PRO_EMBED_NORM) {
+        // mi_compute_get_rows on the Q8_0 embedding (ref src/ops_cpu.cpp:128-139).
+        const int32_t pos = *p.pos;
+        int tok = (pos >= 0 && pos < p.tokens_len) ? p.tokens[pos] : -1;
+        if (tok < 0 || tok >= p.embed_rows) {
+          if (tid == 0) atomicExch(p.err, 1 /* MI_CUDA_ERR_ARG */);
+          tok = 0;
+        }
+        for (int64_t k = tid; k < K; k += NT) {
+          const int64_t b = k >> 5;
+          const float d = packed_scale(p.embed, K, p.embed_npad, tok, b);
+          const float v = __fmul_rn((float)packed_qs(p.embed, K, tok, b)[k & 31], d);
+          xs[k] = v;
+          if (blockIdx.x == 0) p.x_out[k] = v;
+        }
+      } else {
+        for (int64_t k = tid; k < K; k += NT) xs[k] = p.x[k];
+      }
+      __syncthreads();
+      if (tid == 0) {
+        // mi_compute_rms_norm (ref src/ops_cpu.cpp:154-160): one ordered chain.
+        float ss = 0.0f;
+#pragma unroll 8
+        for (int64_t k = 0; k < K; k++) ss = __fadd_rn(ss, __fmul_rn(xs[k], xs[k]));
+        const float mean = __fdiv_rn(ss, (float)K);
+        misc[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+      }
+      __syncthreads();
+      scale = misc[0];
+    }
+    for (int b = warp; b < nb; b += NW) {
+      const int64_t k = (int64_t)b * 32 + lane;
+      float v;
+      if (p.pro >= PRO_NORM_QUANT)
+        v = __fmul_rn(__fmul_rn(xs[k], scale), p.norm_w[k]);  // rms_norm, then MUL weight
+      else
+        v = p.x[k];
+      float d;
+      aq[k] = quantize_lane(v, &d);
+      if (lane == 0) ad[b] = d;
+    }
+  }
+  __syncthreads();
+
+  // ---- weight tiles ----
+  const int rr = lane >> 3, j = lane & 7;
+  const int* aq4 = (const int*)aq;
+  bool ok = true;
+  for (int t = 0; t < n_tiles; t++) {
+    const int s = t % p.n_stages;
+    ok = mbar_wait_bounded(&bars[s], (uint32_t)((t / p.n_stages) & 1), p.err);
+    if (!__syncthreads_and(ok)) {
+      ok = false;
+      break;
+    }
+    const uint8_t* st = stages + (size_t)s * L.stage_bytes;
+    const int64_t tr0 = r0 + (int64_t)t * p.stage_rows;
+    const int ngroups = (int)(min((int64_t)p.stage_rows, r1 - tr0) >> 2);
+    const uint32_t* sq = (const uint32_t*)st;
+    const __half* sd = (const __half*)(st + (size_t)p.stage_rows * K);
+    for (int g = warp; g < ngroups; g += NW) {
+      const uint32_t* gq = sq + (size_t)g * K;
+      const __half* gd = sd + (size_t)g * nb * 4;
+      float acc = 0.0f;
+#pragma unroll 4
+      for (int i = 0; i < nb; i++) {
+        const int pi = __dp4a((int)gq[i * 32 + lane], aq4[i * 8 + j], 0);
+        const float dxdy = __fmul_rn(__half2float(gd[i * 4 + rr]), ad[i]);
+        acc = __fmaf_rn(__int2float_rn(pi), dxdy, acc);
+      }
+      const float s4 = __fadd_rn(acc, __shfl_xor_sync(FULL, acc, 4));
+      const float s1 = __fadd_rn(s4, __shfl_xor_sync(FULL, s4, 1));
+      const float s2 = __fadd_rn(s1, __shfl_xor_sync(FULL, s1, 2));
+      if (j == 0) res[t * p.stage_rows + g * 4 + rr] = s2;
+    }
+    __syncthreads();
+    if (tid == 0 && t + p.n_stages < n_tiles) {
+      fence_proxy_async_smem();
+      issue(t + p.n_stages);
+    }
+  }
+  if (!ok) {
+    // Give copies still in flight a bounded chance to land before the CTA's
+    // shared memory is released.
+    if (tid == 0)
+      for (int t = 0; t < min(n_tiles, p.n_stages); t++)
+        (void)mbar_wait_bounded(&bars[t], 0u, nullptr);
+    return;
+  }
+
+  // ---- epilogue ----
+  if (p.epi == EPI_SILU_GATEUP) {
+    for (int lr = tid; lr < nrows; lr += NT) {
+      const int64_t r = r0 + lr;
+      if ((r & 7) >= 4 || r >= p.N) continue;
+      const float g = res[lr], u = res[lr + 4];
+      p.out[(r >> 3) * 4 + (r & 7)] = __fmul_rn(silu_exact(g, p.et), u);  // mul(silu(gate), up)
+    }
+    return;
+  }
+  if (p.epi != EPI_ARGMAX) {
+    for (int lr = tid; lr < nrows; lr += NT) {
+      const int64_t r = r0 + lr;
+      if (r >= p.N) continue;
+      float v = res[lr];
+      if (p.epi == EPI_BIAS) v = __fadd_rn(v, p.bias[r]);
+      else if (p.epi == EPI_RESID) v = __fadd_rn(p.resid[r], v);
+      p.out[r] = v;
+    }
+    return;
+  }
+
+  // EPI_ARGMAX: logits plus mi_qwen2_sample_greedy (ref src/model_qwen2.cpp:690-700):
+  // the first index of the maximum.
+  float bv = -INFINITY;
+  int32_t bi = 0x7fffffff;
+  for (int lr = tid; lr < nrows; lr += NT) {
+    const int64_t r = r0 + lr;
+    if (r >= p.N) continue;
+    const float v = res[lr];
+    p.out[r] = v;
+    if (v > bv || bi == 0x7fffffff) {
+      bv = v;
+      bi = (int32_t)r;
+    }
+  }
+  __shared__ float red_v[NW];
+  __shared__ int32_t red_i[NW];
+  __shared__ uint32_t ticket;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(FULL, bv, o);
+    const int32_t oi = __shfl_xor_sync(FULL, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if (lane == 0) {
+    red_v[warp] = bv;
+    red_i[warp] = bi;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    for (int w = 1; w < NW; w++)
+      if (red_v[w] > bv || (red_v[w] == bv && red_i[w] < bi)) {
+        bv = red_v[w];
+        bi = red_i[w];
+      }
+    p.part_val[blockIdx.x] = bv;
+    p.part_idx[blockIdx.x] = bi;
+    __threadfence();
+    ticket = atomicAdd(p.counter, 1u);
+  }
+  __syncthreads();
+  if (ticket != gridDim.x - 1) return;
+  // Last CTA: reduce the per-CTA winners in CTA order.
+  if (tid == 0) {
+    __threadfence();
+    float best = __ldcg(&p.part_val[0]);
+    int32_t besti = __ldcg(&p.part_idx[0]);
+    for (unsigned c = 1; c < gridDim.x; c++) {
+      const float v = __ldcg(&p.part_val[c]);
+      const int32_t i = __ldcg(&p.part_idx[c]);
+      if (v > best || (v == best && i < besti)) {
+        best = v;
+        besti = i;
+      }
+    }
+    *p.next_token = besti;
+    const int32_t pos = *p.pos_rw;
+    if (*p.feedback && pos >= 0 && pos + 1 < p.tokens_len) p.tokens_rw[pos + 1] = besti;
+    *p.pos_rw = pos + 1;
+    *p.counter = 0u;
+  }
+}
+
+GemvPlan plan_gemv(int64_t k, int64_t n, int num_sms, int pro) {
+  GemvPlan pl{};
+  const int64_t n_pad = (n + 7) / 8 * 8;
+  const int64_t groups8 = n_pad / 8;
+  const int64_t target = std::max<int64_t>(1, std::min<int64_t>(num_sms, groups8));
+  pl.rows_per_cta = (int32_t)(((n_pad + target - 1) / target + 7) / 8 * 8);
+  pl.grid = (int)((n_pad + pl.rows_per_cta - 1) / pl.rows_per_cta);
+  const int64_t row_bytes = k + k / 32 * 2;
+  const int64_t big = 72 * 1024, small = 32 * 1024;
+  int64_t sr = std::max<int64_t>(8, (big / row_bytes) / 8 * 8);
+  sr = std::min<int64_t>(sr, pl.rows_per_cta);
+  int64_t tiles = (pl.rows_per_cta + sr - 1) / sr;
+  if (tiles > 4) {  // streaming: smaller stages, a deeper ring
+    sr = std::max<int64_t>(8, (small / row_bytes) / 8 * 8);
+    tiles = (pl.rows_per_cta + sr - 1) / sr;
+  }
+  pl.stage_rows = (int32_t)sr;
+  pl.n_stages = (int32_t)std::min<int64_t>(tiles, 4);
+  const size_t limit = 220 * 1024;
+  for (;;) {
+    pl.smem = gemv_smem(k, pl.rows_per_cta, pl.stage_rows, pl.n_stages, pro).total;
+    if (pl.smem <= limit || pl.n_stages == 1) break;
+    pl.n_stages--;
+  }
+  pl.threads = 256;
+  return pl;
+}
+
+cudaError_t prepare_kernels() {
+  int dev = 0, optin = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  cudaFuncAttributes fa{};
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, gemv_q8_kernel<256>);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(gemv_q8_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              optin - (int)fa.sharedSizeBytes);
+}
+
+cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& plan, cudaStream_t s, bool pdl) {
+  GemvParams q = p;
+  q.rows_per_cta = plan.rows_per_cta;
+  q.stage_rows = plan.stage_rows;
+  q.n_stages = plan.n_stages;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)plan.grid);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = plan.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gemv_q8_kernel<256>, q);
+}
+
+// ---------------------------------------------------------------------------
+// Decode attention: MI_OP_ATTN_QK + MI_OP_SOFTMAX + MI_OP_ATTN_KQV for one
+// query token (ref src/ops_cpu.cpp:304-410), one CTA per query head, the GQA
+// mapping kvh = h / n_rep applied by index (no K/V copy). In executor mode it
+// also performs the step's RoPE on q and k (src/ops_cpu.cpp:270-302) and the
+// KV-cache append (MI_OP_CPY, src/ops_cpu.cpp:446-460).
+// ---------------------------------------------------------------------------
+template <bool EXEC>
+__global__ void __launch_bounds__(256) attn_decode_kernel(const AttnParams p) {
+  __shared__ float qr[256], kr[256], vr[256];
+  __shared__ float red[8];
+  __shared__ float sh[2];
+  const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int D = p.head_dim, half = D >> 1, HKV = p.n_head_kv;
+  const int kvh = h / (p.n_head / HKV);
+  pdl_trigger();
+  pdl_wait();
+  int n_past, n_kv;
+  if (EXEC) {
+    n_past = *p.pos;
+    if (n_past < 0 || n_past >= p.n_ctx) {  // no cache row / RoPE entry for this position
+      if (tid == 0) atomicExch(p.err, 6 /* MI_CUDA_ERR_STATE */);
+      return;
+    }
+    n_kv = n_past + 1;
+    const float2* cs = p.rope_cs + (size_t)n_past * half;
+    const float* q = p.qkv + (size_t)h * D;
+    const float* k = p.qkv + (size_t)p.n_head * D + (size_t)kvh * D;
+    const float* v = p.qkv + (size_t)(p.n_head + HKV) * D + (size_t)kvh * D;
+    for (int i = tid; i < half; i += blockDim.x) {
+      const float2 c = cs[i];
+      const float q0 = q[i], q1 = q[i + half], k0 = k[i], k1 = k[i + half];
+      qr[i] = __fsub_rn(__fmul_rn(q0, c.x), __fmul_rn(q1, c.y));
+      qr[i + half] = __fadd_rn(__fmul_rn(q0, c.y), __fmul_rn(q1, c.x));
+      kr[i] = __fsub_rn(__fmul_rn(k0, c.x), __fmul_rn(k1, c.y));
+      kr[i + half] = __fadd_rn(__fmul_rn(k0, c.y), __fmul_rn(k1, c.x));
+    }
+    for (int i = tid; i < D; i += blockDim.x) vr[i] = v[i];
+    __syncthreads();
+    if (h % (p.n_head / HKV) == 0) {
+      float* kd = p.cache_k + ((size_t)n_past * HKV + kvh) * D;
+      float* vd = p.cache_v + ((size_t)n_past * HKV + kvh) * D;
+      for (int i = tid; i < D; i += blockDim.x) {
+        kd[i] = kr[i];
+        vd[i] = vr[i];
+      }
+    }
+  } else {
+    n_kv = p.n_kv_fixed;
+    n_past = n_kv - 1;
+    for (int i = tid; i < D; i += blockDim.x) qr[i] = p.q_rot[(size_t)h * D + i];
+    __syncthreads();
+  }
+  float* sc = p.scores + (size_t)h * p.scores_stride;
+
+  // scores[i] * scale, d ascending with separate roundings (src/ops_cpu.cpp:373-376).
+  float lmax = -INFINITY;
+  for (int i = tid; i < n_kv; i += blockDim.x) {
+    const float* kp = (EXEC && i == n_past) ? kr : p.cache_k + ((size_t)i * HKV + kvh) * D;
+    float acc = 0.0f;
+    for (int d = 0; d < D; d++) acc = __fadd_rn(acc, __fmul_rn(kp[d], qr[d]));
+    const float v = __fmul_rn(acc, p.scale);
+    sc[i] = v;
+    lmax = fmaxf(lmax, v);
+  }
+  lmax = warp_max(lmax);
+  if (lane == 0) red[warp] = lmax;
+  __syncthreads();
+  if (tid == 0) {
+    float m = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++) m = fmaxf(m, red[w]);
+    sh[0] = m;
+  }
+  __syncthreads();
+  const float mx = sh[0];
+  for (int i = tid; i < n_kv; i += blockDim.x) sc[i] = expf_exact(__fsub_rn(sc[i], mx), p.et);
+  __syncthreads();
+  if (tid == 0) {
+    // The softmax denominator: one ordered chain (src/ops_cpu.cpp:331-336).
+    float sum = 0.0f;
+#pragma unroll 8
+    for (int i = 0; i < n_kv; i++) sum = __fadd_rn(sum, sc[i]);
+    sh[1] = __fdiv_rn(1.0f, sum);
+  }
+  __syncthreads();
+  const float inv = sh[1];
+  for (int i = tid; i < n_kv; i += blockDim.x) sc[i] = __fmul_rn(sc[i], inv);
+  __syncthreads();
+  // out[o] = sum_t V[o, kvh, t] * P[t], t ascending (src/ops_cpu.cpp:402-406).
+  for (int o = tid; o < D; o += blockDim.x) {
+    float acc = 0.0f;
+    const float* vcol = p.cache_v + (size_t)kvh * D + o;
+    const size_t vstride = (size_t)HKV * D;
+#pragma unroll 4
+    for (int t = 0; t < n_kv; t++) {
+      const float vv = (EXEC && t == n_past) ? vr[o] : vcol[(size_t)t * vstride];
+      acc = __fadd_rn(acc, __fmul_rn(vv, sc[t]));
+    }
+    p.out[(size_t)h * D + o] = acc;
+  }
+}
+
+cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)p.n_head);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  if (exec_mode) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<true>, p);
+  return cudaLaunchKernelEx(&cfg, attn_decode_kernel<false>, p);
+}
+
+// ---------------------------------------------------------------------------
+// Small ops
+// ---------------------------------------------------------------------------
+
+// GGUF Q8_0 rows -> packed layout. Source row i goes to packed row
+// (i/4)*group_stride + row_offset + i%4 (row_offset a multiple of 4), which
+// lets one packed matrix hold Q|K|V stacked or gate/up interleaved by groups.
+__global__ void pack_q8_0_kernel(const uint8_t* raw, int64_t K, int64_t n, int64_t src_row0,
+                                 uint8_t* dst, int64_t npad, int64_t row_offset, int64_t gstride) {
+  const int64_t nb = K / 32;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n * nb) return;
+  const int64_t i = src_row0 + idx / nb, b = idx % nb;
+  const int64_t r = (i >> 2) * gstride + row_offset + (i & 3);
+  const uint16_t* src = (const uint16_t*)(raw + idx * 34);
+  uint32_t* q = (uint32_t*)(dst + (r >> 2) * 4 * K + b * 128 + (r & 3) * 32);
+#pragma unroll
+  for (int w = 0; w < 8; w++) q[w] = (uint32_t)src[1 + 2 * w] | ((uint32_t)src[2 + 2 * w] << 16);
+  uint16_t* d = (uint16_t*)(dst + npad * K);
+  d[((r >> 2) * nb + b) * 4 + (r & 3)] = src[0];
+}
+
+cudaError_t launch_pack_q8_0(const uint8_t* raw, int64_t k, int64_t n, int64_t src_row0,
+                             uint8_t* dst, int64_t dst_npad, int64_t row_offset,
+                             int64_t group_stride, cudaStream_t s) {
+  const int64_t total = n * (k / 32);
+  if (total == 0) return cudaSuccess;
+  pack_q8_0_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(
+      raw, k, n, src_row0, dst, dst_npad, row_offset, group_stride);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_zero_pad_rows(uint8_t* dst, int64_t k, int64_t n_pad, cudaStream_t s) {
+  return cudaMemsetAsync(dst, 0, (size_t)(n_pad * k + n_pad * (k / 32) * 2), s);
+}
+
+// mi_compute_quantize_q8_0 (src/ops_cpu.cpp:462-479): one warp per block.
+__global__ void quantize_act_kernel(const float* x, int64_t K, int64_t m, uint8_t* act) {
+  const int64_t nb = K / 32;
+  const int64_t blk = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (blk >= m * nb) return;
+  const int64_t row = blk / nb, b = blk % nb;
+  float d;
+  const int8_t q = quantize_lane(x[row * K + b * 32 + lane], &d);
+  uint8_t* out = act + (row * nb + b) * 36;
+  ((int8_t*)out)[4 + lane] = q;
+  if (lane == 0) *(float*)out = d;
+}
+
+cudaError_t launch_quantize_act(const float* x, int64_t k, int64_t m, uint8_t* act,
+                                cudaStream_t s) {
+  const int64_t warps = m * (k / 32);
+  if (warps == 0) return cudaSuccess;
+  quantize_act_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(x, k, m, act);
+  return cudaGetLastError();
+}
+
+// Per-block int32 sums through the GEMV's lane partials.
+__global__ void block_isums_kernel(const uint8_t* w, int64_t K, int64_t n, int64_t npad,
+                                   const uint8_t* act, int32_t* isums) {
+  const int64_t nb = K / 32;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n * nb) return;
+  const int64_t r = idx / nb, b = idx % nb;
+  const int* wq = (const int*)packed_qs(w, K, r, b);
+  const int* aq = (const int*)(act + b * 36 + 4);
+  int s = 0;
+#pragma unroll
+  for (int j = 0; j < 8; j++) s += __dp4a(wq[j], aq[j], 0);
+  isums[idx] = s;
+}
+
+cudaError_t launch_block_isums(const uint8_t* w, int64_t k, int64_t n, int64_t n_pad,
+                               const uint8_t* act, int32_t* isums, cudaStream_t s) {
+  const int64_t total = n * (k / 32);
+  if (total == 0) return cudaSuccess;
+  block_isums_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(w, k, n, n_pad, act, isums);
+  return cudaGetLastError();
+}
+
+// mi_compute_get_rows on a Q8_0 table (src/ops_cpu.cpp:128-139).
+__global__ void get_rows_kernel(const uint8_t* table, int64_t ne0, int64_t npad,
+                                const int32_t* ids, int64_t n_ids, float* dst) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n_ids * ne0) return;
+  const int64_t j = idx / ne0, k = idx % ne0;
+  const int64_t tok = ids[j];
+  const float d = packed_scale(table, ne0, npad, tok, k >> 5);
+  dst[idx] = __fmul_rn((float)packed_qs(table, ne0, tok, k >> 5)[k & 31], d);
+}
+
+cudaError_t launch_get_rows(const uint8_t* table, int64_t ne0, int64_t n_pad,
+                            const int32_t* ids, int64_t n_ids, float* dst, cudaStream_t s) {
+  const int64_t total = n_ids * ne0;
+  if (total == 0) return cudaSuccess;
+  get_rows_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(table, ne0, n_pad, ids, n_ids,
+                                                                   dst);
+  return cudaGetLastError();
+}
+
+// mi_compute_rms_norm (src/ops_cpu.cpp:143-165): one CTA per row.
+__global__ void rms_norm_kernel(const float* x, int64_t ne0, float eps, float* dst) {
+  __shared__ float scale;
+  const float* xr = x + (int64_t)blockIdx.x * ne0;
+  if (threadIdx.x == 0) {
+    float ss = 0.0f;
+    for (int64_t i = 0; i < ne0; i++) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+    const float mean = __fdiv_rn(ss, (float)ne0);
+    scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+  }
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < ne0; i += blockDim.x)
+    dst[(int64_t)blockIdx.x * ne0 + i] = __fmul_rn(xr[i], scale);
+}
+
+cudaError_t launch_rms_norm(const float* x, int64_t ne0, int64_t n_rows, float eps, float* dst,
+                            cudaStream_t s) {
+  if (n_rows == 0) return cudaSuccess;
+  rms_norm_kernel<<<(unsigned)n_rows, 256, 0, s>>>(x, ne0, eps, dst);
+  return cudaGetLastError();
+}
+
+// ew_binop (src/ops_cpu.cpp:56-80): op 0 = mul, 1 = add, 2 = scale by v.
+__global__ void binop_kernel(int op, const float* a, const float* b, int64_t ne0, int64_t n_rows,
+                             int64_t b_rows, float v, float* dst) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= ne0 * n_rows) return;
+  const int64_t r = idx / ne0, i = idx % ne0;
+  const float x = a[idx];
+  float y;
+  if (op == 2) {
+    y = __fmul_rn(x, v);
+  } else {
+    const float bb = b[(b_rows > 1 ? r : 0) * ne0 + i];
+    y = op == 0 ? __fmul_rn(x, bb) : __fadd_rn(x, bb);
+  }
+  dst[idx] = y;
+}
+
+cudaError_t launch_binop(int op, const float* a, const float* b, int64_t ne0, int64_t n_rows,
+                         int64_t b_rows, float v, float* dst, cudaStream_t s) {
+  const int64_t total = ne0 * n_rows;
+  if (total == 0) return cudaSuccess;
+  binop_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(op, a, b, ne0, n_rows, b_rows, v,
+                                                                dst);
+  return cudaGetLastError();
+}
+
+__global__ void silu_kernel(const float* x, int64_t n, float* dst, const ExpTab et) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[i] = silu_exact(x[i], et);
+}
+
+cudaError_t launch_silu(const float* x, int64_t n, float* dst, const ExpTab& et, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  silu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, n, dst, et);
+  return cudaGetLastError();
+}
+
+__global__ void expf_range_kernel(uint64_t first, int64_t n, float* dst, const ExpTab et) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[i] = expf_exact(__uint_as_float((uint32_t)(first + (uint64_t)i)), et);
+}
+
+cudaError_t launch_expf_range(uint64_t first, int64_t count, float* dst, const ExpTab& et,
+                              cudaStream_t s) {
+  if (count == 0) return cudaSuccess;
+  expf_range_kernel<<<(unsigned)((count + 255) / 256), 256, 0, s>>>(first, count, dst, et);
+  return cudaGetLastError();
+}
+
+__global__ void expf_kernel(const float* x, int64_t n, float* dst, const ExpTab et) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[i] = expf_exact(x[i], et);
+}
+
+cudaError_t launch_expf(const float* x, int64_t n, float* dst, const ExpTab& et, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  expf_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, n, dst, et);
+  return cudaGetLastError();
+}
+
+// mi_compute_rope NEOX (src/ops_cpu.cpp:270-302); cs[t][p] holds the (cos, sin)
+// of position n_past + t.
+__global__ void rope_kernel(const float* x, int64_t hd, int64_t nh, int64_t nt, int32_t n_dims,
+                            const float2* cs, float* dst) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= nt * nh * hd) return;
+  const int64_t i = idx % hd, row = idx / hd, t = row / nh;
+  const int64_t half = n_dims / 2;
+  const float* xr = x + row * hd;
+  float y;
+  if (i >= n_dims) {
+    y = xr[i];
+  } else {
+    const int64_t pp = i < half ? i : i - half;
+    const float2 c = cs[t * half + pp];
+    const float x0 = xr[pp], x1 = xr[pp + half];
+    y = i < half ? __fsub_rn(__fmul_rn(x0, c.x), __fmul_rn(x1, c.y))
+                 : __fadd_rn(__fmul_rn(x0, c.y), __fmul_rn(x1, c.x));
+  }
+  dst[idx] = y;
+}
+
+cudaError_t launch_rope(const float* x, int64_t head_dim, int64_t n_head, int64_t n_tokens,
+                        int32_t n_dims, const float2* cs, float* dst, cudaStream_t s) {
+  const int64_t total = n_tokens * n_head * head_dim;
+  if (total == 0) return cudaSuccess;
+  rope_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(x, head_dim, n_head, n_tokens,
+                                                               n_dims, cs, dst);
+  return cudaGetLastError();
+}
+
+// mi_compute_attn_qk (src/ops_cpu.cpp:356-380), one thread per (h, j, i).
+__global__ void attn_qk_kernel(const float* q, const float* k, int64_t hd, int64_t nh,
+                               int64_t nhkv, int64_t n_kv, int64_t nt, float* scores) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= nh * nt * n_kv) return;
+  const int64_t i = idx % n_kv, hj = idx / n_kv, j = hj % nt, h = hj / nt;
+  const int64_t kvh = h / (nh / nhkv);
+  const float* kr = k + (i * nhkv + kvh) * hd;
+  const float* qr = q + (j * nh + h) * hd;
+  float acc = 0.0f;
+  for (int64_t d = 0; d < hd; d++) acc = __fadd_rn(acc, __fmul_rn(kr[d], qr[d]));
+  scores[idx] = acc;
+}
+
+cudaError_t launch_attn_qk(const float* q, const float* k, int64_t hd, int64_t nh, int64_t nhkv,
+                           int64_t n_kv, int64_t nt, float* scores, cudaStream_t s) {
+  const int64_t total = nh * nt * n_kv;
+  if (total == 0) return cudaSuccess;
+  attn_qk_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(q, k, hd, nh, nhkv, n_kv, nt,
+                                                                  scores);
+  return cudaGetLastError();
+}
+
+// mi_compute_softmax (src/ops_cpu.cpp:304-346): one CTA per (h, j) row.
+__global__ void softmax_kernel(const float* x, int64_t n_kv, int64_t nt, int32_t n_past,
+                               float scale, float* dst, const ExpTab et) {
+  __shared__ float red[8];
+  __shared__ float sh[2];
+  const int64_t row = blockIdx.x, j = row % nt;
+  const float* xr = x + row * n_kv;
+  float* yr = dst + row * n_kv;
+  int64_t allowed = n_past + j + 1;
+  if (allowed > n_kv) allowed = n_kv;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float m = -INFINITY;
+  for (int64_t i = tid; i < allowed; i += blockDim.x) m = fmaxf(m, __fmul_rn(xr[i], scale));
+  m = warp_max(m);
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  if (tid == 0) {
+    float mm = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++) mm = fmaxf(mm, red[w]);
+    sh[0] = mm;
+  }
+  __syncthreads();
+  const float mx = sh[0];
+  for (int64_t i = tid; i < allowed; i += blockDim.x)
+    yr[i] = expf_exact(__fsub_rn(__fmul_rn(xr[i], scale), mx), et);
+  __syncthreads();
+  if (tid == 0) {
+    float sum = 0.0f;
+    for (int64_t i = 0; i < allowed; i++) sum = __fadd_rn(sum, yr[i]);
+    sh[1] = __fdiv_rn(1.0f, sum);
+  }
+  __syncthreads();
+  const float inv = sh[1];
+  for (int64_t i = tid; i < n_kv; i += blockDim.x) yr[i] = i < allowed ? __fmul_rn(yr[i], inv) : 0.0f;
+}
+
+cudaError_t launch_softmax(const float* x, int64_t n_kv, int64_t nt, int64_t nh, int32_t n_past,
+                           float scale, float* dst, const ExpTab& et, cudaStream_t s) {
+  if (nt * nh == 0) return cudaSuccess;
+  softmax_kernel<<<(unsigned)(nt * nh), 256, 0, s>>>(x, n_kv, nt, n_past, scale, dst, et);
+  return cudaGetLastError();
+}
+
+// mi_compute_attn_kqv (src/ops_cpu.cpp:386-410), one thread per (h, o, j).
+__global__ void attn_kqv_kernel(const float* pr, const float* v, int64_t hd, int64_t nh,
+                                int64_t nhkv, int64_t n_kv, int64_t nt, float* dst) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= nh * hd * nt) return;
+  const int64_t o = idx % hd, hj = idx / hd, h = hj % nh, j = hj / nh;
+  const int64_t kvh = h / (nh / nhkv);
+  const float* p = pr + (h * nt + j) * n_kv;
+  float acc = 0.0f;
+  for (int64_t t = 0; t < n_kv; t++) acc = __fadd_rn(acc, __fmul_rn(v[(t * nhkv + kvh) * hd + o], p[t]));
+  dst[idx] = acc;
+}
+
+cudaError_t launch_attn_kqv(const float* p, const float* v, int64_t hd, int64_t nh, int64_t nhkv,
+                            int64_t n_kv, int64_t nt, float* dst, cudaStream_t s) {
+  const int64_t total = nh * hd * nt;
+  if (total == 0) return cudaSuccess;
+  attn_kqv_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(p, v, hd, nh, nhkv, n_kv, nt,
+                                                                   dst);
+  return cudaGetLastError();
+}
+
+// First index of the maximum: per-CTA winners, the last CTA reduces them.
+__global__ void argmax_kernel(const float* x, int64_t n, float* part_val, int32_t* part_idx,
+                              uint32_t* counter, int32_t* out) {
+  __shared__ float rv[8];
+  __shared__ int32_t ri[8];
+  __shared__ uint32_t ticket;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float bv = -INFINITY;
+  int32_t bi = 0x7fffffff;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + tid; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    if (v > bv || bi == 0x7fffffff) {
+      bv = v;
+      bi = (int32_t)i;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(FULL, bv, o);
+    const int32_t oi = __shfl_xor_sync(FULL, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if (lane == 0) {
+    rv[warp] = bv;
+    ri[warp] = bi;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++)
+      if (rv[w] > bv || (rv[w] == bv && ri[w] < bi)) {
+        bv = rv[w];
+        bi = ri[w];
+      }
+    part_val[blockIdx.x] = bv;
+    part_idx[blockIdx.x] = bi;
+    __threadfence();
+    ticket = atomicAdd(counter, 1u);
+  }
+  __syncthreads();
+  if (ticket != gridDim.x - 1 || tid != 0) return;
+  __threadfence();
+  float best = __ldcg(&part_val[0]);
+  int32_t besti = __ldcg(&part_idx[0]);
+  for (unsigned c = 1; c < gridDim.x; c++) {
+    const float v = __ldcg(&part_val[c]);
+    const int32_t i = __ldcg(&part_idx[c]);
+    if (v > best || (v == best && i < besti)) {
+      best = v;
+      besti = i;
+    }
+  }
+  *out = besti;
+  *counter = 0u;
+}
+
+cudaError_t launch_argmax(const float* x, int64_t n, float* part_val, int32_t* part_idx,
+                          uint32_t* counter, int32_t* out, cudaStream_t s) {
+  if (n <= 0) return cudaErrorInvalidValue;
+  const int64_t g = std::min<int64_t>(148, (n + 255) / 256);
+  argmax_kernel<<<(unsigned)g, 256, 0, s>>>(x, n, part_val, part_idx, counter, out);
+  return cudaGetLastError();
+}
+
+__global__ void advance_kernel(int32_t* pos) {
+  pdl_trigger();
+  pdl_wait();
+  if (threadIdx.x == 0) *pos += 1;
+}
+
+cudaError_t launch_advance(int32_t* pos, cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(32);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, advance_kernel, pos);
+}
+
+__global__ void set_pos_kernel(int32_t* pos, int32_t value) {
+  if (threadIdx.x == 0) *pos = value;
+}
+
+cudaError_t launch_set_pos(int32_t* pos, int32_t value, cudaStream_t s) {
+  set_pos_kernel<<<1, 32, 0, s>>>(pos, value);
+  return cudaGetLastError();
+}
+
+}  // namespace mi

@@ -1,0 +1,150 @@
+// Device-side building blocks shared by every kernel of the backend:
+// PTX wrappers (mbarrier, bulk async copy, programmatic dependent launch),
+// the libm-exact expf, and the exact-order arithmetic helpers.
+//
+// Exactness rule for every kernel: float arithmetic is written with the
+// round-to-nearest intrinsics (__fadd_rn, __fmul_rn, __fdiv_rn, __fsqrt_rn,
+// __fmaf_rn) in the reference's operation order, and the library is compiled
+// with -fmad=false, so no multiply-add is ever contracted behind our back.
+// __fmaf_rn appears only where the reference's AVX2 kernel issues an FMA.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "mi_expf_core.h"
+#include "mi_internal.h"
+
+namespace mi {
+
+// Iteration bound of every spin wait (each try_wait blocks for a while in
+// hardware, so this is seconds, far beyond any legitimate wait).
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// Global -> shared bulk copy (TMA engine, no tensor map). dst and src 16-byte
+// aligned, bytes a multiple of 16; completion is counted on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on a phase of `bar`. On expiry records MI_CUDA_ERR_TIMEOUT in
+// *err and returns false; the caller then skips its work and exits.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int32_t* err) {
+  for (uint32_t it = 0; it < kSpinLimit; it++)
+    if (mbar_try_wait(bar, parity)) return true;
+  if (err) atomicExch(err, 5 /* MI_CUDA_ERR_TIMEOUT */);
+  return false;
+}
+
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start while its predecessor runs; pdl_wait() blocks until
+// the predecessor grid has completed and its writes are visible. Both are
+// no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// libm-exact expf: the double-precision core plus one probe of the exception
+// hash (two buckets of four (key, value) pairs, loaded as four independent
+// 16-byte reads).
+__device__ __forceinline__ float expf_exact(float x, const ExpTab& t) {
+  float y = mi_expf_core(x);
+  if (x == x) {
+    uint32_t key = __float_as_uint(x);
+    uint32_t b1 = mi_expf_bucket(key, t.mul1, t.log2b);
+    uint32_t b2 = mi_expf_bucket(key, t.mul2, t.log2b);
+    const uint4* p1 = t.buckets + 2 * (size_t)b1;
+    const uint4* p2 = t.buckets + 2 * (size_t)b2;
+    uint4 a0 = __ldg(p1), a1 = __ldg(p1 + 1), c0 = __ldg(p2), c1 = __ldg(p2 + 1);
+    if (a0.x == key) y = __uint_as_float(a0.y);
+    if (a0.z == key) y = __uint_as_float(a0.w);
+    if (a1.x == key) y = __uint_as_float(a1.y);
+    if (a1.z == key) y = __uint_as_float(a1.w);
+    if (c0.x == key) y = __uint_as_float(c0.y);
+    if (c0.z == key) y = __uint_as_float(c0.w);
+    if (c1.x == key) y = __uint_as_float(c1.y);
+    if (c1.z == key) y = __uint_as_float(c1.w);
+  }
+  return y;
+}
+
+// x / (1 + expf(-x)), ref src/ops_cpu.cpp:424.
+__device__ __forceinline__ float silu_exact(float x, const ExpTab& t) {
+  return __fdiv_rn(x, __fadd_rn(1.0f, expf_exact(-x, t)));
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// One Q8_0_ACT block value: the reference's per-block quantizer
+// (src/quant.cpp:199-218) for the element this lane holds; the warp holds the
+// block's 32 elements. Returns q, writes d (same on every lane).
+__device__ __forceinline__ int8_t quantize_lane(float v, float* d_out) {
+  float amax = warp_max(fabsf(v));
+  float d = __fdiv_rn(amax, 127.0f);
+  float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+  int q = __float2int_rn(__fmul_rn(v, id));
+  q = q > 127 ? 127 : (q < -127 ? -127 : q);
+  *d_out = d;
+  return (int8_t)q;
+}
+
+// Packed Q8_0 layout (see mi_cuda_q8_0_pack): qs plane of n_pad*K bytes, then
+// the fp16 scale plane. Row r, block b:
+//   qs at (r/4)*4K + b*128 + (r%4)*32, scale at plane + ((r/4)*nb + b)*4 + r%4.
+__device__ __forceinline__ const int8_t* packed_qs(const uint8_t* w, int64_t K, int64_t r,
+                                                   int64_t b) {
+  return (const int8_t*)(w + (r >> 2) * 4 * K + b * 128 + (r & 3) * 32);
+}
+__device__ __forceinline__ float packed_scale(const uint8_t* w, int64_t K, int64_t n_pad,
+                                              int64_t r, int64_t b) {
+  const __half* d = (const __half*)(w + n_pad * K);
+  return __half2float(d[((r >> 2) * (K / 32) + b) * 4 + (r & 3)]);
+}
+
+}  // namespace mi

@@ -1,0 +1,173 @@
+// Internal host/device interface of the backend (not part of the C-ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace mi {
+
+// Device view of the expf exception hash (see mi_expf_core.h).
+struct ExpTab {
+  const uint4* buckets;
+  uint32_t log2b, mul1, mul2;
+};
+
+// ---------------------------------------------------------------------------
+// Q8_0 GEMV
+// ---------------------------------------------------------------------------
+enum GemvPrologue : int32_t {
+  PRO_ACT = 0,         // activation given as Q8_0_ACT blocks
+  PRO_QUANT = 1,       // quantize F32 x in the prologue
+  PRO_NORM_QUANT = 2,  // rms_norm(x) * norm_w, then quantize
+  PRO_EMBED_NORM = 3,  // x = dequantized embedding row tokens[*pos]; then as PRO_NORM_QUANT
+};
+
+enum GemvEpilogue : int32_t {
+  EPI_STORE = 0,        // out[r] = dot
+  EPI_BIAS = 1,         // out[r] = dot + bias[r]
+  EPI_RESID = 2,        // out[r] = resid[r] + dot
+  EPI_SILU_GATEUP = 3,  // packed rows 8q+t / 8q+4+t are gate / up row 4q+t:
+                        // out[4q+t] = silu(gate) * up
+  EPI_ARGMAX = 4,       // out[r] = dot, plus the greedy token over all rows
+};
+
+struct GemvParams {
+  const uint8_t* w;
+  int64_t K, N, n_pad;
+  int32_t rows_per_cta, stage_rows, n_stages, pro, epi;
+  int32_t tokens_len;  // entries of `tokens` / `tokens_rw` (bounds for pos)
+  // prologue inputs
+  const float* x;
+  const uint8_t* act;  // Q8_0_ACT, K/32 blocks of 36 B
+  const float* norm_w;
+  float eps;
+  int32_t pad1;
+  const uint8_t* embed;  // packed Q8_0 embedding table [K x embed_npad]
+  int64_t embed_npad, embed_rows;
+  const int32_t* tokens;
+  const int32_t* pos;
+  float* x_out;  // PRO_EMBED_NORM: CTA 0 stores the embedding row here
+  // epilogue
+  const float* bias;
+  const float* resid;
+  float* out;
+  // EPI_ARGMAX
+  float* part_val;
+  int32_t* part_idx;
+  uint32_t* counter;
+  int32_t* next_token;
+  int32_t* tokens_rw;  // with *feedback != 0 the winner is also stored at tokens[pos+1]
+  int32_t* pos_rw;     // ... and pos is advanced
+  const int32_t* feedback;
+  ExpTab et;
+  int32_t* err;
+};
+
+struct GemvPlan {
+  int grid, threads;
+  int32_t rows_per_cta, stage_rows, n_stages;
+  size_t smem;
+};
+
+// Work split for an n-row, k-column packed matrix over the device's SMs.
+GemvPlan plan_gemv(int64_t k, int64_t n, int num_sms, int pro);
+// Per-device kernel attributes (dynamic shared memory limit); called once per
+// device at context creation, outside any stream capture.
+cudaError_t prepare_kernels();
+cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& plan, cudaStream_t s, bool pdl);
+
+// ---------------------------------------------------------------------------
+// Decode attention (one query token per head)
+// ---------------------------------------------------------------------------
+struct AttnParams {
+  const float* qkv;     // executor: q | k | v projections (pre-RoPE q and k)
+  const float* q_rot;   // op: rotated queries [n_head][hd]
+  float* cache_k;       // [n_ctx][n_head_kv][hd]
+  float* cache_v;
+  int32_t head_dim, n_head, n_head_kv, n_kv_fixed;  // n_kv_fixed: op mode
+  const int32_t* pos;   // executor: current position (n_past)
+  const float2* rope_cs;  // executor: [pos][head_dim/2] (cos, sin)
+  float scale;
+  int32_t n_ctx;         // executor: cache / RoPE table capacity (bounds for pos)
+  float* scores;        // scratch [n_head][scores_stride]
+  int64_t scores_stride;
+  float* out;           // [n_head][hd]
+  ExpTab et;
+  int32_t* err;
+};
+cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t s, bool pdl);
+
+// ---------------------------------------------------------------------------
+// Small ops
+// ---------------------------------------------------------------------------
+// Packs n GGUF rows (source rows src_row0 .. src_row0+n-1 of a matrix) into a
+// packed matrix with dst_npad rows: source row i lands on packed row
+// (i/4)*group_stride + row_offset + i%4.
+cudaError_t launch_pack_q8_0(const uint8_t* raw, int64_t k, int64_t n, int64_t src_row0,
+                             uint8_t* dst, int64_t dst_npad, int64_t row_offset,
+                             int64_t group_stride, cudaStream_t s);
+cudaError_t launch_expf_range(uint64_t first, int64_t count, float* dst, const ExpTab& et,
+                              cudaStream_t s);
+cudaError_t launch_zero_pad_rows(uint8_t* dst, int64_t k, int64_t n_pad, cudaStream_t s);
+cudaError_t launch_quantize_act(const float* x, int64_t k, int64_t m, uint8_t* act,
+                                cudaStream_t s);
+cudaError_t launch_block_isums(const uint8_t* w, int64_t k, int64_t n, int64_t n_pad,
+                               const uint8_t* act, int32_t* isums, cudaStream_t s);
+cudaError_t launch_get_rows(const uint8_t* table, int64_t ne0, int64_t n_pad,
+                            const int32_t* ids, int64_t n_ids, float* dst, cudaStream_t s);
+cudaError_t launch_rms_norm(const float* x, int64_t ne0, int64_t n_rows, float eps, float* dst,
+                            cudaStream_t s);
+cudaError_t launch_binop(int op, const float* a, const float* b, int64_t ne0, int64_t n_rows,
+                         int64_t b_rows, float v, float* dst, cudaStream_t s);
+cudaError_t launch_silu(const float* x, int64_t n, float* dst, const ExpTab& et, cudaStream_t s);
+cudaError_t launch_expf(const float* x, int64_t n, float* dst, const ExpTab& et, cudaStream_t s);
+cudaError_t launch_rope(const float* x, int64_t head_dim, int64_t n_head, int64_t n_tokens,
+                        int32_t n_dims, const float2* cs, float* dst, cudaStream_t s);
+cudaError_t launch_attn_qk(const float* q, const float* k, int64_t hd, int64_t nh, int64_t nhkv,
+                           int64_t n_kv, int64_t nt, float* scores, cudaStream_t s);
+cudaError_t launch_softmax(const float* x, int64_t n_kv, int64_t nt, int64_t nh, int32_t n_past,
+                           float scale, float* dst, const ExpTab& et, cudaStream_t s);
+cudaError_t launch_attn_kqv(const float* p, const float* v, int64_t hd, int64_t nh, int64_t nhkv,
+                            int64_t n_kv, int64_t nt, float* dst, cudaStream_t s);
+cudaError_t launch_argmax(const float* x, int64_t n, float* part_val, int32_t* part_idx,
+                          uint32_t* counter, int32_t* out, cudaStream_t s);
+cudaError_t launch_advance(int32_t* pos, cudaStream_t s, bool pdl);
+cudaError_t launch_set_pos(int32_t* pos, int32_t value, cudaStream_t s);
+
+// ---------------------------------------------------------------------------
+// Library state (ops_capi.cu)
+// ---------------------------------------------------------------------------
+struct DeviceCtx {
+  int device = -1;
+  int num_sms = 0;
+  ExpTab et{};
+  void* et_buf = nullptr;
+  int32_t* err = nullptr;  // device error word
+  // scratch for mi_cuda_argmax
+  float* am_val = nullptr;
+  int32_t* am_idx = nullptr;
+  uint32_t* am_counter = nullptr;
+  // RoPE table cache for the per-op entry point
+  float2* rope = nullptr;
+  int32_t rope_n_pos = 0, rope_n_dims = 0;
+  float rope_base = 0.0f;
+};
+
+// Per-device context, initialized on first use (loads the expf table).
+DeviceCtx* device_ctx(int device, std::string* err);
+DeviceCtx* current_ctx(std::string* err);
+void set_error(const std::string& msg);
+
+// Host RoPE table (host_math.cpp): cs[(pos - pos0) * (n_dims/2) + p] for
+// pos in [pos0, pos0 + n_pos), evaluated with the host libm exactly as the
+// reference (src/ops_cpu.cpp:286-292).
+void build_rope_table(int32_t pos0, int32_t n_pos, int32_t n_dims, float freq_base, float* cs);
+
+// Host expf helpers (host_math.cpp).
+void expf_fingerprints(uint32_t* core, uint32_t* libm);
+// Counts floats with bits in [first, first+n) where libm expf != y[i - first].
+uint64_t expf_count_mismatch(uint64_t first, int64_t n, const float* y);
+
+}  // namespace mi

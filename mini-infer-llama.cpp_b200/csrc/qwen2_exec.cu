@@ -1,0 +1,728 @@
+// Qwen2 decode executor: the device-resident replacement of the reference's
+// model API (src/model_qwen2.h:83-189).
+//
+// The reference rebuilds and re-plans its graph every step and runs its ~700
+// exec nodes one barrier at a time (src/model_qwen2.cpp:609-688,
+// src/threadpool.cpp:171-180). Here the same computation is five fused
+// kernels per layer plus one for the LM head, captured once into a CUDA graph
+// and replayed every step:
+//   1. QKV GEMV   prologue: [embedding lookup (layer 0)], rms_norm * attn_norm,
+//                 quantize; epilogue: + [bq|bk|bv]
+//   2. attention  RoPE(q, k), KV-cache append, QK, softmax, KV
+//   3. O GEMV     prologue: quantize; epilogue: + residual
+//   4. gate/up    prologue: rms_norm * ffn_norm, quantize; epilogue: silu(g)*u
+//   5. down GEMV  prologue: quantize; epilogue: + residual
+//   LM head      prologue: rms_norm * output_norm, quantize; epilogue: logits
+//                 + greedy argmax (+ optional feedback into the token buffer)
+// Kernels are chained with programmatic dependent launch: each GEMV starts
+// streaming its weights into shared memory while its predecessor still runs.
+// The step position lives on the device, so one graph serves every step.
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "gguf_reader.h"
+#include "mi_cuda.h"
+#include "mi_internal.h"
+
+using namespace mi;
+
+namespace {
+
+struct Mat {
+  uint8_t* w = nullptr;
+  int64_t K = 0, N = 0, npad = 0;
+};
+
+struct Layer {
+  Mat qkv, o, gateup, down;
+  float* bqkv = nullptr;
+  float* attn_norm = nullptr;
+  float* ffn_norm = nullptr;
+};
+
+struct StepState {
+  int32_t pos;
+  int32_t next_token;
+  int32_t feedback;
+  uint32_t counter;
+  int32_t err;
+  int32_t pad[3];
+};
+
+int fail(int code, const std::string& msg) {
+  set_error(msg);
+  return code;
+}
+
+#define CK(expr)                                                                         \
+  do {                                                                                   \
+    cudaError_t _e = (expr);                                                             \
+    if (_e != cudaSuccess)                                                               \
+      return fail(MI_CUDA_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e)); \
+  } while (0)
+
+int64_t npad8(int64_t n) { return (n + 7) / 8 * 8; }
+size_t packed_bytes(int64_t k, int64_t n) { return (size_t)(npad8(n) * k + npad8(n) * (k / 32) * 2); }
+size_t a256(size_t v) { return (v + 255) / 256 * 256; }
+
+}  // namespace
+
+struct mi_cuda_model {
+  int device = 0;
+  DeviceCtx* ctx = nullptr;
+  mi_cuda_qwen2_hparams hp{};
+  bool tied = true;
+  uint8_t* buf = nullptr;
+  size_t bytes = 0;
+  Mat embed, lm_head;
+  float* output_norm = nullptr;
+  std::vector<Layer> layers;
+};
+
+struct mi_cuda_kv_cache {
+  mi_cuda_model* model = nullptr;
+  int32_t n_ctx = 0;
+  cudaStream_t stream = nullptr;
+  uint8_t* buf = nullptr;
+  float* cache = nullptr;  // [layer][k|v][n_ctx][HKV][D]
+  float2* rope = nullptr;
+  float *x = nullptr, *x2 = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr;
+  float* logits = nullptr;
+  float* scores = nullptr;
+  float* part_val = nullptr;
+  int32_t* part_idx = nullptr;
+  int32_t* tokens = nullptr;
+  StepState* state = nullptr;
+  StepState* h_state = nullptr;  // pinned
+  int32_t* h_tokens = nullptr;   // pinned staging, n_ctx + 1
+  cudaGraphExec_t g_head = nullptr, g_nohead = nullptr;
+  int32_t kernels_per_step = 0;
+  bool pdl = true;
+  GemvPlan plan_qkv{}, plan_o{}, plan_gu{}, plan_down{}, plan_head{};
+  cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+};
+
+namespace {
+
+// Uploads n GGUF Q8_0 rows of `t` into packed matrix `dst` (rows mapped by
+// row_offset / group_stride, see launch_pack_q8_0) through pinned staging.
+int upload_q8(const GgufTensor* t, const Mat& dst, int64_t row_offset, int64_t gstride,
+              uint8_t* d_stage, uint8_t* h_stage, size_t stage_bytes, cudaStream_t s) {
+  const int64_t K = t->ne[0], n = t->ne[1];
+  const size_t row = (size_t)(K / 32 * 34);
+  const int64_t rows_per = std::max<int64_t>(4, (int64_t)(stage_bytes / row) / 4 * 4);
+  for (int64_t r0 = 0; r0 < n; r0 += rows_per) {
+    const int64_t rn = std::min(rows_per, n - r0);
+    CK(cudaStreamSynchronize(s));
+    std::memcpy(h_stage, t->data + (size_t)r0 * row, (size_t)rn * row);
+    CK(cudaMemcpyAsync(d_stage, h_stage, (size_t)rn * row, cudaMemcpyHostToDevice, s));
+    CK(launch_pack_q8_0(d_stage, K, rn, r0, dst.w, dst.npad, row_offset, gstride, s));
+  }
+  return MI_CUDA_OK;
+}
+
+int upload_f32(const GgufTensor* t, float* dst, cudaStream_t s) {
+  CK(cudaMemcpyAsync(dst, t->data, t->nbytes, cudaMemcpyHostToDevice, s));
+  CK(cudaStreamSynchronize(s));
+  return MI_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mi_cuda_qwen2_model_load(const char* gguf_path, int device, mi_cuda_model** out) {
+  if (!gguf_path || !out) return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_model_load: null argument");
+  *out = nullptr;
+  std::string err;
+  DeviceCtx* ctx = device_ctx(device, &err);
+  if (!ctx) return fail(MI_CUDA_ERR_CUDA, err);
+  CK(cudaSetDevice(device));
+  GgufFile g;
+  if (!g.open(gguf_path, &err)) return fail(MI_CUDA_ERR_IO, err);
+
+  // Hyperparameters: the same keys as mi_qwen2_hparams_load (ref src/model_qwen2.cpp:426-464).
+  mi_cuda_qwen2_hparams hp{};
+  uint32_t u[6];
+  const char* keys[6] = {"qwen2.embedding_length", "qwen2.block_count",
+                         "qwen2.attention.head_count", "qwen2.attention.head_count_kv",
+                         "qwen2.feed_forward_length", "qwen2.context_length"};
+  for (int i = 0; i < 6; i++)
+    if (!g.get_u32(keys[i], &u[i]))
+      return fail(MI_CUDA_ERR_FORMAT, std::string("qwen2 hparams: missing or wrong-typed key '") + keys[i] + "'");
+  if (!g.get_f32("qwen2.rope.freq_base", &hp.rope_freq_base) ||
+      !g.get_f32("qwen2.attention.layer_norm_rms_epsilon", &hp.rms_eps))
+    return fail(MI_CUDA_ERR_FORMAT, "qwen2 hparams: missing rope.freq_base or layer_norm_rms_epsilon");
+  hp.n_embd = (int32_t)u[0];
+  hp.n_layer = (int32_t)u[1];
+  hp.n_head = (int32_t)u[2];
+  hp.n_head_kv = (int32_t)u[3];
+  hp.n_ff = (int32_t)u[4];
+  hp.n_ctx_train = (int32_t)u[5];
+  if (hp.n_head == 0 || hp.n_embd % hp.n_head != 0)
+    return fail(MI_CUDA_ERR_FORMAT, "qwen2 hparams: embedding_length is not divisible by head_count");
+  if (hp.n_head_kv == 0 || hp.n_head % hp.n_head_kv != 0)
+    return fail(MI_CUDA_ERR_FORMAT, "qwen2 hparams: head_count is not a multiple of head_count_kv");
+  hp.head_dim = hp.n_embd / hp.n_head;
+  const GgufTensor* te = g.find("token_embd.weight");
+  if (!te) return fail(MI_CUDA_ERR_FORMAT, "missing tensor token_embd.weight");
+  hp.n_vocab = (int32_t)te->ne[1];
+  const int64_t E = hp.n_embd, D = hp.head_dim, kvd = (int64_t)hp.n_head_kv * D, FF = hp.n_ff;
+  if (E % 64 != 0 || FF % 64 != 0 || D % 2 != 0 || D > 256)
+    return fail(MI_CUDA_ERR_FORMAT, "unsupported shape (n_embd and n_ff must be multiples of 64, head_dim <= 256)");
+
+  auto need = [&](const std::string& name, uint32_t type, int64_t ne0, int64_t ne1,
+                  const GgufTensor** t) -> int {
+    *t = g.find(name);
+    if (!*t) return fail(MI_CUDA_ERR_FORMAT, "missing weight tensor: " + name);
+    if ((*t)->type != type)
+      return fail(MI_CUDA_ERR_FORMAT, "weight " + name + (type == kGgmlQ8_0 ? " must be Q8_0" : " must be F32"));
+    if ((*t)->ne[0] != ne0 || (*t)->ne[1] != ne1)
+      return fail(MI_CUDA_ERR_FORMAT, "weight " + name + " has an unexpected shape");
+    return MI_CUDA_OK;
+  };
+
+  auto m = std::make_unique<mi_cuda_model>();
+  m->device = device;
+  m->ctx = ctx;
+  m->hp = hp;
+  const GgufTensor* tout = g.find("output.weight");
+  m->tied = tout == nullptr;
+  int rc;
+  rc = need("token_embd.weight", kGgmlQ8_0, E, hp.n_vocab, &te);
+    if (rc) return rc;
+  if (!m->tied && (rc = need("output.weight", kGgmlQ8_0, E, hp.n_vocab, &tout))) return rc;
+  const GgufTensor* tnorm;
+  rc = need("output_norm.weight", kGgmlF32, E, 1, &tnorm);
+    if (rc) return rc;
+
+  // One device allocation for every weight (256-byte aligned sub-buffers).
+  size_t total = a256(packed_bytes(E, hp.n_vocab)) + a256(E * 4);
+  if (!m->tied) total += a256(packed_bytes(E, hp.n_vocab));
+  const size_t per_layer = a256(packed_bytes(E, E + 2 * kvd)) + a256((E + 2 * kvd) * 4) +
+                           a256(packed_bytes(E, E)) + a256(packed_bytes(E, 2 * FF)) +
+                           a256(packed_bytes(FF, E)) + 2 * a256(E * 4);
+  total += per_layer * (size_t)hp.n_layer;
+  CK(cudaMalloc(&m->buf, total));
+  m->bytes = total;
+  size_t off = 0;
+  auto take = [&](size_t b) {
+    uint8_t* p = m->buf + off;
+    off += a256(b);
+    return p;
+  };
+  auto mat = [&](int64_t K, int64_t N) {
+    Mat x;
+    x.K = K;
+    x.N = N;
+    x.npad = npad8(N);
+    x.w = take(packed_bytes(K, N));
+    return x;
+  };
+  m->embed = mat(E, hp.n_vocab);
+  m->lm_head = m->tied ? m->embed : mat(E, hp.n_vocab);
+  m->output_norm = (float*)take(E * 4);
+  m->layers.resize((size_t)hp.n_layer);
+  for (auto& L : m->layers) {
+    L.qkv = mat(E, E + 2 * kvd);
+    L.bqkv = (float*)take((E + 2 * kvd) * 4);
+    L.o = mat(E, E);
+    L.gateup = mat(E, 2 * FF);
+    L.down = mat(FF, E);
+    L.attn_norm = (float*)take(E * 4);
+    L.ffn_norm = (float*)take(E * 4);
+  }
+  CK(cudaMemset(m->buf, 0, total));
+
+  cudaStream_t s;
+  CK(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+  const size_t stage = 64u << 20;
+  uint8_t *d_stage = nullptr, *h_stage = nullptr;
+  cudaError_t e = cudaMalloc(&d_stage, stage);
+  if (e == cudaSuccess) e = cudaMallocHost(&h_stage, stage);
+  auto cleanup = [&]() {
+    cudaStreamSynchronize(s);
+    if (d_stage) cudaFree(d_stage);
+    if (h_stage) cudaFreeHost(h_stage);
+    cudaStreamDestroy(s);
+  };
+  if (e != cudaSuccess) {
+    cleanup();
+    cudaFree(m->buf);
+    return fail(MI_CUDA_ERR_CUDA, "staging allocation failed");
+  }
+  rc = upload_q8(te, m->embed, 0, 4, d_stage, h_stage, stage, s);
+  if (!rc && !m->tied) rc = upload_q8(tout, m->lm_head, 0, 4, d_stage, h_stage, stage, s);
+  if (!rc) rc = upload_f32(tnorm, m->output_norm, s);
+  for (int l = 0; !rc && l < hp.n_layer; l++) {
+    Layer& L = m->layers[(size_t)l];
+    const std::string b = "blk." + std::to_string(l) + ".";
+    const GgufTensor *an, *wq, *bq, *wk, *bk, *wv, *bv, *wo, *fn, *wg, *wu, *wd;
+    rc = need(b + "attn_norm.weight", kGgmlF32, E, 1, &an);
+    if (rc) break;
+    rc = need(b + "attn_q.weight", kGgmlQ8_0, E, E, &wq);
+    if (rc) break;
+    rc = need(b + "attn_q.bias", kGgmlF32, E, 1, &bq);
+    if (rc) break;
+    rc = need(b + "attn_k.weight", kGgmlQ8_0, E, kvd, &wk);
+    if (rc) break;
+    rc = need(b + "attn_k.bias", kGgmlF32, kvd, 1, &bk);
+    if (rc) break;
+    rc = need(b + "attn_v.weight", kGgmlQ8_0, E, kvd, &wv);
+    if (rc) break;
+    rc = need(b + "attn_v.bias", kGgmlF32, kvd, 1, &bv);
+    if (rc) break;
+    rc = need(b + "attn_output.weight", kGgmlQ8_0, E, E, &wo);
+    if (rc) break;
+    rc = need(b + "ffn_norm.weight", kGgmlF32, E, 1, &fn);
+    if (rc) break;
+    rc = need(b + "ffn_gate.weight", kGgmlQ8_0, E, FF, &wg);
+    if (rc) break;
+    rc = need(b + "ffn_up.weight", kGgmlQ8_0, E, FF, &wu);
+    if (rc) break;
+    rc = need(b + "ffn_down.weight", kGgmlQ8_0, FF, E, &wd);
+    if (rc) break;
+    // Q | K | V stacked in one matrix; gate/up interleaved by groups of 4 rows.
+    rc = upload_q8(wq, L.qkv, 0, 4, d_stage, h_stage, stage, s);
+    if (rc) break;
+    rc = upload_q8(wk, L.qkv, E, 4, d_stage, h_stage, stage, s);
+    if (rc) break;
+    rc = upload_q8(wv, L.qkv, E + kvd, 4, d_stage, h_stage, stage, s);
+    if (rc) break;
+    rc = upload_q8(wo, L.o, 0, 4, d_stage, h_stage, stage, s);
+    if (rc) break;
+    rc = upload_q8(wg, L.gateup, 0, 8, d_stage, h_stage, stage, s);
+    if (rc) break;
+    rc = upload_q8(wu, L.gateup, 4, 8, d_stage, h_stage, stage, s);
+    if (rc) break;
+    rc = upload_q8(wd, L.down, 0, 4, d_stage, h_stage, stage, s);
+    if (rc) break;
+    rc = upload_f32(an, L.attn_norm, s);
+    if (rc) break;
+    rc = upload_f32(fn, L.ffn_norm, s);
+    if (rc) break;
+    rc = upload_f32(bq, L.bqkv, s);
+    if (rc) break;
+    rc = upload_f32(bk, L.bqkv + E, s);
+    if (rc) break;
+    rc = upload_f32(bv, L.bqkv + E + kvd, s);
+    if (rc) break;
+  }
+  cleanup();
+  if (!rc && cudaGetLastError() != cudaSuccess) rc = fail(MI_CUDA_ERR_CUDA, "weight upload failed");
+  if (rc) {
+    cudaFree(m->buf);
+    return rc;
+  }
+  *out = m.release();
+  return MI_CUDA_OK;
+}
+
+void mi_cuda_qwen2_model_free(mi_cuda_model* model) {
+  if (!model) return;
+  cudaSetDevice(model->device);
+  cudaFree(model->buf);
+  delete model;
+}
+
+int mi_cuda_qwen2_get_hparams(const mi_cuda_model* model, mi_cuda_qwen2_hparams* out) {
+  if (!model || !out) return fail(MI_CUDA_ERR_ARG, "null argument");
+  *out = model->hp;
+  return MI_CUDA_OK;
+}
+
+size_t mi_cuda_qwen2_weight_bytes(const mi_cuda_model* model) { return model ? model->bytes : 0; }
+
+}  // extern "C"
+
+namespace {
+
+// Enqueues one decode step (n_tokens = 1) on kv->stream; with_head adds the
+// LM head + greedy argmax, otherwise the step only advances the position.
+int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
+  mi_cuda_model* m = kv->model;
+  const mi_cuda_qwen2_hparams& hp = m->hp;
+  const int64_t E = hp.n_embd, D = hp.head_dim, kvd = (int64_t)hp.n_head_kv * D, FF = hp.n_ff;
+  const ExpTab et = m->ctx->et;
+  int32_t* err = &kv->state->err;
+  const size_t layer_floats = (size_t)2 * kv->n_ctx * kvd;
+  int count = 0;
+  bool pdl = false;  // the first kernel of a step has no in-graph predecessor
+  for (int l = 0; l < hp.n_layer; l++) {
+    const Layer& L = m->layers[(size_t)l];
+    GemvParams p{};
+    p.w = L.qkv.w;
+    p.K = E;
+    p.N = L.qkv.N;
+    p.n_pad = L.qkv.npad;
+    p.pro = l == 0 ? PRO_EMBED_NORM : PRO_NORM_QUANT;
+    p.x = kv->x;
+    p.norm_w = L.attn_norm;
+    p.eps = hp.rms_eps;
+    p.embed = m->embed.w;
+    p.embed_npad = m->embed.npad;
+    p.embed_rows = hp.n_vocab;
+    p.tokens = kv->tokens;
+    p.tokens_len = kv->n_ctx + 1;
+    p.pos = &kv->state->pos;
+    p.x_out = kv->x;
+    p.epi = EPI_BIAS;
+    p.bias = L.bqkv;
+    p.out = kv->qkv;
+    p.et = et;
+    p.err = err;
+    CK(launch_gemv(p, kv->plan_qkv, kv->stream, pdl));
+    pdl = kv->pdl;
+    count++;
+
+    AttnParams a{};
+    a.qkv = kv->qkv;
+    a.cache_k = kv->cache + (size_t)l * layer_floats;
+    a.cache_v = a.cache_k + (size_t)kv->n_ctx * kvd;
+    a.head_dim = (int32_t)D;
+    a.n_head = hp.n_head;
+    a.n_head_kv = hp.n_head_kv;
+    a.pos = &kv->state->pos;
+    a.rope_cs = kv->rope;
+    a.scale = 1.0f / std::sqrt((float)hp.head_dim);
+    a.n_ctx = kv->n_ctx;
+    a.scores = kv->scores;
+    a.scores_stride = kv->n_ctx;
+    a.out = kv->attn;
+    a.et = et;
+    a.err = err;
+    CK(launch_attn_decode(a, true, kv->stream, pdl));
+    count++;
+
+    GemvParams o{};
+    o.w = L.o.w;
+    o.K = E;
+    o.N = E;
+    o.n_pad = L.o.npad;
+    o.pro = PRO_QUANT;
+    o.x = kv->attn;
+    o.epi = EPI_RESID;
+    o.resid = kv->x;
+    o.out = kv->x2;
+    o.et = et;
+    o.err = err;
+    CK(launch_gemv(o, kv->plan_o, kv->stream, pdl));
+    count++;
+
+    GemvParams gu{};
+    gu.w = L.gateup.w;
+    gu.K = E;
+    gu.N = 2 * FF;
+    gu.n_pad = L.gateup.npad;
+    gu.pro = PRO_NORM_QUANT;
+    gu.x = kv->x2;
+    gu.norm_w = L.ffn_norm;
+    gu.eps = hp.rms_eps;
+    gu.epi = EPI_SILU_GATEUP;
+    gu.out = kv->act;
+    gu.et = et;
+    gu.err = err;
+    CK(launch_gemv(gu, kv->plan_gu, kv->stream, pdl));
+    count++;
+
+    GemvParams dn{};
+    dn.w = L.down.w;
+    dn.K = FF;
+    dn.N = E;
+    dn.n_pad = L.down.npad;
+    dn.pro = PRO_QUANT;
+    dn.x = kv->act;
+    dn.epi = EPI_RESID;
+    dn.resid = kv->x2;
+    dn.out = kv->x;
+    dn.et = et;
+    dn.err = err;
+    CK(launch_gemv(dn, kv->plan_down, kv->stream, pdl));
+    count++;
+  }
+  if (with_head) {
+    GemvParams h{};
+    h.w = m->lm_head.w;
+    h.K = E;
+    h.N = hp.n_vocab;
+    h.n_pad = m->lm_head.npad;
+    h.pro = PRO_NORM_QUANT;
+    h.x = kv->x;
+    h.norm_w = m->output_norm;
+    h.eps = hp.rms_eps;
+    h.epi = EPI_ARGMAX;
+    h.out = kv->logits;
+    h.part_val = kv->part_val;
+    h.part_idx = kv->part_idx;
+    h.counter = &kv->state->counter;
+    h.next_token = &kv->state->next_token;
+    h.tokens_rw = kv->tokens;
+    h.tokens_len = kv->n_ctx + 1;
+    h.pos_rw = &kv->state->pos;
+    h.feedback = &kv->state->feedback;
+    h.et = et;
+    h.err = err;
+    CK(launch_gemv(h, kv->plan_head, kv->stream, pdl));
+  } else {
+    CK(launch_advance(&kv->state->pos, kv->stream, pdl));
+  }
+  count++;
+  if (n_kernels) *n_kernels = count;
+  return MI_CUDA_OK;
+}
+
+int capture(mi_cuda_kv_cache* kv, bool with_head, cudaGraphExec_t* out, int32_t* n_kernels) {
+  CK(cudaStreamBeginCapture(kv->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = enqueue_step(kv, with_head, n_kernels);
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamEndCapture(kv->stream, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (e != cudaSuccess) return fail(MI_CUDA_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+  e = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return fail(MI_CUDA_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+  return MI_CUDA_OK;
+}
+
+int check_state_error(mi_cuda_kv_cache* kv) {
+  CK(cudaStreamSynchronize(kv->stream));
+  int32_t err = 0;
+  CK(cudaMemcpy(&err, &kv->state->err, 4, cudaMemcpyDeviceToHost));
+  if (err) {
+    CK(cudaMemset(&kv->state->err, 0, 4));
+    if (err == MI_CUDA_ERR_TIMEOUT) return fail(MI_CUDA_ERR_TIMEOUT, "a device-side wait timed out");
+    if (err == MI_CUDA_ERR_STATE) return fail(MI_CUDA_ERR_STATE, "decode position outside the KV cache");
+    return fail(err, "a kernel reported an invalid token id or position");
+  }
+  return MI_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** out) {
+  if (!m || !out || n_ctx <= 0) return fail(MI_CUDA_ERR_ARG, "mi_cuda_kv_cache_init: bad arguments");
+  *out = nullptr;
+  CK(cudaSetDevice(m->device));
+  const mi_cuda_qwen2_hparams& hp = m->hp;
+  const int64_t E = hp.n_embd, D = hp.head_dim, kvd = (int64_t)hp.n_head_kv * D, FF = hp.n_ff;
+  auto kv = std::make_unique<mi_cuda_kv_cache>();
+  kv->model = m;
+  kv->n_ctx = n_ctx;
+  const int sms = m->ctx->num_sms;
+  kv->plan_qkv = plan_gemv(E, E + 2 * kvd, sms, PRO_EMBED_NORM);
+  kv->plan_o = plan_gemv(E, E, sms, PRO_QUANT);
+  kv->plan_gu = plan_gemv(E, 2 * FF, sms, PRO_NORM_QUANT);
+  kv->plan_down = plan_gemv(FF, E, sms, PRO_QUANT);
+  kv->plan_head = plan_gemv(E, hp.n_vocab, sms, PRO_NORM_QUANT);
+
+  const size_t cache_bytes = (size_t)hp.n_layer * 2 * n_ctx * kvd * 4;
+  const size_t rope_bytes = (size_t)n_ctx * (D / 2) * 8;
+  size_t off = 0;
+  auto slot = [&](size_t b) {
+    size_t o = off;
+    off += a256(b);
+    return o;
+  };
+  const size_t o_cache = slot(cache_bytes), o_rope = slot(rope_bytes), o_x = slot(E * 4),
+               o_x2 = slot(E * 4), o_qkv = slot((E + 2 * kvd) * 4), o_attn = slot(E * 4),
+               o_act = slot(FF * 4), o_logits = slot((size_t)hp.n_vocab * 4),
+               o_scores = slot((size_t)hp.n_head * n_ctx * 4), o_pv = slot(1024 * 4),
+               o_pi = slot(1024 * 4), o_tok = slot((size_t)(n_ctx + 1) * 4),
+               o_state = slot(sizeof(StepState));
+  CK(cudaMalloc(&kv->buf, off));
+  CK(cudaMemset(kv->buf, 0, off));
+  kv->cache = (float*)(kv->buf + o_cache);
+  kv->rope = (float2*)(kv->buf + o_rope);
+  kv->x = (float*)(kv->buf + o_x);
+  kv->x2 = (float*)(kv->buf + o_x2);
+  kv->qkv = (float*)(kv->buf + o_qkv);
+  kv->attn = (float*)(kv->buf + o_attn);
+  kv->act = (float*)(kv->buf + o_act);
+  kv->logits = (float*)(kv->buf + o_logits);
+  kv->scores = (float*)(kv->buf + o_scores);
+  kv->part_val = (float*)(kv->buf + o_pv);
+  kv->part_idx = (int32_t*)(kv->buf + o_pi);
+  kv->tokens = (int32_t*)(kv->buf + o_tok);
+  kv->state = (StepState*)(kv->buf + o_state);
+  if (kv->plan_head.grid > 1024) return fail(MI_CUDA_ERR_ARG, "LM head grid too large");
+
+  std::vector<float> cs((size_t)n_ctx * (D / 2) * 2);
+  build_rope_table(0, n_ctx, (int32_t)D, hp.rope_freq_base, cs.data());
+  CK(cudaMemcpy(kv->rope, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+  CK(cudaMallocHost(&kv->h_state, sizeof(StepState)));
+  CK(cudaMallocHost(&kv->h_tokens, (size_t)(n_ctx + 1) * 4));
+  CK(cudaStreamCreateWithFlags(&kv->stream, cudaStreamNonBlocking));
+  for (auto& e : kv->ev) CK(cudaEventCreate(&e));
+
+  int rc = capture(kv.get(), true, &kv->g_head, &kv->kernels_per_step);
+  if (!rc) rc = capture(kv.get(), false, &kv->g_nohead, nullptr);
+  if (rc) {
+    // Retry without programmatic dependent launch if the graph refused it.
+    kv->pdl = false;
+    if (kv->g_head) cudaGraphExecDestroy(kv->g_head);
+    kv->g_head = nullptr;
+    cudaGetLastError();
+    rc = capture(kv.get(), true, &kv->g_head, &kv->kernels_per_step);
+    if (!rc) rc = capture(kv.get(), false, &kv->g_nohead, nullptr);
+    if (rc) return rc;
+  }
+  *out = kv.release();
+  return MI_CUDA_OK;
+}
+
+void mi_cuda_kv_cache_free(mi_cuda_kv_cache* kv) {
+  if (!kv) return;
+  cudaSetDevice(kv->model->device);
+  if (kv->stream) cudaStreamSynchronize(kv->stream);
+  if (kv->g_head) cudaGraphExecDestroy(kv->g_head);
+  if (kv->g_nohead) cudaGraphExecDestroy(kv->g_nohead);
+  for (auto& e : kv->ev)
+    if (e) cudaEventDestroy(e);
+  if (kv->stream) cudaStreamDestroy(kv->stream);
+  if (kv->h_state) cudaFreeHost(kv->h_state);
+  if (kv->h_tokens) cudaFreeHost(kv->h_tokens);
+  cudaFree(kv->buf);
+  delete kv;
+}
+
+int mi_cuda_qwen2_set_position(mi_cuda_kv_cache* kv, const int32_t* h_tokens, int32_t n,
+                               int32_t pos) {
+  if (!kv || n < 0 || n > kv->n_ctx + 1 || pos < 0 || pos > kv->n_ctx || (n > 0 && !h_tokens))
+    return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_set_position: bad arguments");
+  CK(cudaSetDevice(kv->model->device));
+  CK(cudaStreamSynchronize(kv->stream));
+  if (n > 0) {
+    std::memcpy(kv->h_tokens, h_tokens, (size_t)n * 4);
+    CK(cudaMemcpyAsync(kv->tokens, kv->h_tokens, (size_t)n * 4, cudaMemcpyHostToDevice, kv->stream));
+  }
+  *kv->h_state = StepState{};
+  kv->h_state->pos = pos;
+  kv->h_state->feedback = 1;
+  CK(cudaMemcpyAsync(kv->state, kv->h_state, sizeof(StepState), cudaMemcpyHostToDevice, kv->stream));
+  return MI_CUDA_OK;
+}
+
+int mi_cuda_qwen2_decode_steps(mi_cuda_kv_cache* kv, int32_t n_steps, int32_t pos0,
+                               int32_t period) {
+  if (!kv || n_steps < 0 || period < 0 || pos0 < 0 || pos0 >= kv->n_ctx)
+    return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_decode_steps: bad arguments");
+  CK(cudaSetDevice(kv->model->device));
+  for (int32_t i = 0; i < n_steps; i++) {
+    if (period > 0 && i > 0 && i % period == 0) CK(launch_set_pos(&kv->state->pos, pos0, kv->stream));
+    CK(cudaGraphLaunch(kv->g_head, kv->stream));
+  }
+  return MI_CUDA_OK;
+}
+
+int mi_cuda_qwen2_read_tokens(mi_cuda_kv_cache* kv, int32_t first, int32_t n, int32_t* h_out) {
+  if (!kv || !h_out || first < 0 || n < 0 || first + n > kv->n_ctx + 1)
+    return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_read_tokens: bad arguments");
+  CK(cudaSetDevice(kv->model->device));
+  CK(cudaMemcpyAsync(kv->h_tokens + first, kv->tokens + first, (size_t)n * 4, cudaMemcpyDeviceToHost,
+                     kv->stream));
+  int rc = check_state_error(kv);
+  if (rc) return rc;
+  std::memcpy(h_out, kv->h_tokens + first, (size_t)n * 4);
+  return MI_CUDA_OK;
+}
+
+mi_cuda_stream mi_cuda_qwen2_stream(mi_cuda_kv_cache* kv) { return kv ? (mi_cuda_stream)kv->stream : nullptr; }
+
+int32_t mi_cuda_qwen2_kernels_per_step(mi_cuda_kv_cache* kv) { return kv ? kv->kernels_per_step : 0; }
+
+int mi_cuda_qwen2_forward(mi_cuda_model* m, mi_cuda_kv_cache* kv, const int32_t* h_tokens,
+                          int32_t n_tokens, int32_t n_past, int32_t last_logits_only,
+                          float* h_logits_out) {
+  if (!m || !kv || kv->model != m || !h_tokens || n_tokens <= 0 || n_past < 0)
+    return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_forward: bad arguments");
+  if (n_past + n_tokens > kv->n_ctx)
+    return fail(MI_CUDA_ERR_STATE, "mi_cuda_qwen2_forward: n_past + n_tokens exceeds n_ctx");
+  for (int32_t i = 0; i < n_tokens; i++)
+    if (h_tokens[i] < 0 || h_tokens[i] >= m->hp.n_vocab)
+      return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_forward: token id out of range");
+  CK(cudaSetDevice(m->device));
+  CK(cudaStreamSynchronize(kv->stream));
+  std::memcpy(kv->h_tokens + n_past, h_tokens, (size_t)n_tokens * 4);
+  CK(cudaMemcpyAsync(kv->tokens + n_past, kv->h_tokens + n_past, (size_t)n_tokens * 4,
+                     cudaMemcpyHostToDevice, kv->stream));
+  *kv->h_state = StepState{};
+  kv->h_state->pos = n_past;
+  kv->h_state->feedback = 0;
+  CK(cudaMemcpyAsync(kv->state, kv->h_state, sizeof(StepState), cudaMemcpyHostToDevice, kv->stream));
+  const size_t V = (size_t)m->hp.n_vocab;
+  for (int32_t t = 0; t < n_tokens; t++) {
+    const bool head = !last_logits_only || t == n_tokens - 1;
+    CK(cudaGraphLaunch(head ? kv->g_head : kv->g_nohead, kv->stream));
+    if (head && h_logits_out) {
+      float* dst = h_logits_out + (last_logits_only ? 0 : (size_t)t * V);
+      CK(cudaMemcpyAsync(dst, kv->logits, V * 4, cudaMemcpyDeviceToHost, kv->stream));
+    }
+  }
+  return check_state_error(kv);
+}
+
+int mi_cuda_qwen2_last_token(mi_cuda_kv_cache* kv, int32_t* h_token_out) {
+  if (!kv || !h_token_out) return fail(MI_CUDA_ERR_ARG, "null argument");
+  CK(cudaSetDevice(kv->model->device));
+  CK(cudaMemcpyAsync(&kv->h_state->next_token, &kv->state->next_token, 4, cudaMemcpyDeviceToHost,
+                     kv->stream));
+  CK(cudaStreamSynchronize(kv->stream));
+  *h_token_out = kv->h_state->next_token;
+  return MI_CUDA_OK;
+}
+
+int32_t mi_cuda_qwen2_sample_greedy(const float* h_logits, int32_t n_vocab) {
+  int32_t best = 0;
+  float bv = h_logits[0];
+  for (int32_t i = 1; i < n_vocab; i++)
+    if (h_logits[i] > bv) {
+      bv = h_logits[i];
+      best = i;
+    }
+  return best;
+}
+
+int mi_cuda_qwen2_generate(mi_cuda_model* m, mi_cuda_kv_cache* kv, const int32_t* h_prompt,
+                           int32_t n_prompt, int32_t n_predict, int32_t* h_tokens_out,
+                           double* prefill_ms, double* decode_ms) {
+  if (!m || !kv || kv->model != m || !h_prompt || n_prompt <= 0 || n_predict <= 0 || !h_tokens_out)
+    return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_generate: bad arguments");
+  if (n_prompt > kv->n_ctx) return fail(MI_CUDA_ERR_STATE, "prompt longer than n_ctx");
+  for (int32_t i = 0; i < n_prompt; i++)
+    if (h_prompt[i] < 0 || h_prompt[i] >= m->hp.n_vocab)
+      return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_generate: token id out of range");
+  int rc = mi_cuda_qwen2_set_position(kv, h_prompt, n_prompt, 0);
+  if (rc) return rc;
+  // The reference loop stops once n_past reaches n_ctx (src/main.cpp:409-423).
+  const int32_t n_decode = std::min<int32_t>(n_predict - 1, kv->n_ctx - n_prompt);
+  CK(cudaEventRecord(kv->ev[0], kv->stream));
+  for (int32_t t = 0; t + 1 < n_prompt; t++) CK(cudaGraphLaunch(kv->g_nohead, kv->stream));
+  CK(cudaGraphLaunch(kv->g_head, kv->stream));
+  CK(cudaEventRecord(kv->ev[1], kv->stream));
+  for (int32_t i = 0; i < n_decode; i++) CK(cudaGraphLaunch(kv->g_head, kv->stream));
+  CK(cudaEventRecord(kv->ev[2], kv->stream));
+  const int32_t produced = 1 + n_decode;
+  CK(cudaMemcpyAsync(kv->h_tokens, kv->tokens + n_prompt, (size_t)produced * 4,
+                     cudaMemcpyDeviceToHost, kv->stream));
+  rc = check_state_error(kv);
+  if (rc) return rc;
+  std::memcpy(h_tokens_out, kv->h_tokens, (size_t)produced * 4);
+  for (int32_t i = produced; i < n_predict; i++) h_tokens_out[i] = -1;
+  float a = 0, b = 0;
+  CK(cudaEventElapsedTime(&a, kv->ev[0], kv->ev[1]));
+  CK(cudaEventElapsedTime(&b, kv->ev[1], kv->ev[2]));
+  if (prefill_ms) *prefill_ms = a;
+  if (decode_ms) *decode_ms = b;
+  return MI_CUDA_OK;
+}
+
+}  // extern "C"
