@@ -152,6 +152,22 @@ int mi_cuda_attention_decode(const float* d_q, const float* d_cache_k, const flo
                              int64_t head_dim, int64_t n_head, int64_t n_head_kv, int64_t n_kv,
                              float scale, void* d_scratch, float* d_dst, mi_cuda_stream s);
 
+/* No counterpart in the reference. mi_cuda_attention_decode for callers that
+ * cannot allocate device memory on their call path (a zero-allocation runtime
+ * after start-up, code running while the caller records a CUDA graph, a plugin
+ * host that owns all device memory): same inputs, outputs and results, but the
+ * score scratch is a 4 MiB array inside the library that every GPU loading the
+ * library keeps until exit, so n_head * n_kv may be at most 1,048,576 (larger
+ * sizes return MI_CUDA_ERR_ARG). It allocates nothing; mi_cuda_init(device) must
+ * have run once before (it loads the expf table), else MI_CUDA_ERR_STATE. The
+ * first call on a device looks up the array's device address and may load the
+ * module, so make it before any stream capture. All calls on a device share the
+ * array: calls that can overlap on the GPU race and must be serialized. */
+int mi_cuda_attention_decode_noalloc(const float* d_q, const float* d_cache_k,
+                                     const float* d_cache_v, int64_t head_dim, int64_t n_head,
+                                     int64_t n_head_kv, int64_t n_kv, float scale, float* d_dst,
+                                     mi_cuda_stream s);
+
 /* mi_qwen2_sample_greedy on the device (ref src/model_qwen2.cpp:690-700):
  * first index of the maximum. */
 int mi_cuda_argmax(const float* d_x, int64_t n, int32_t* d_out, mi_cuda_stream s);

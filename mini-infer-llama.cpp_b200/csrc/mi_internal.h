@@ -158,6 +158,9 @@ struct DeviceCtx {
 // Per-device context, initialized on first use (loads the expf table).
 DeviceCtx* device_ctx(int device, std::string* err);
 DeviceCtx* current_ctx(std::string* err);
+// The context of `device` if mi_cuda_init (or any entry point) already created
+// it, else nullptr; never creates one (creation allocates device memory).
+const DeviceCtx* existing_device_ctx(int device);
 void set_error(const std::string& msg);
 
 // Host RoPE table (host_math.cpp): cs[(pos - pos0) * (n_dims/2) + p] for

@@ -119,6 +119,12 @@ DeviceCtx* device_ctx(int device, std::string* err) {
   return c;
 }
 
+const DeviceCtx* existing_device_ctx(int device) {
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (device < 0 || (size_t)device >= g_ctx.size()) return nullptr;
+  return g_ctx[(size_t)device];
+}
+
 DeviceCtx* current_ctx(std::string* err) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {

@@ -66,6 +66,7 @@ _SIGS = {
     "mi_cuda_attn_kqv": (I32, [P, P, I64, I64, I64, I64, I64, P, P]),
     "mi_cuda_attention_decode_scratch_bytes": (SZ, [I64, I64]),
     "mi_cuda_attention_decode": (I32, [P, P, P, I64, I64, I64, I64, F32, P, P, P]),
+    "mi_cuda_attention_decode_noalloc": (I32, [P, P, P, I64, I64, I64, I64, F32, P, P]),
     "mi_cuda_argmax": (I32, [P, I64, P, P]),
     "mi_cuda_expf": (I32, [P, I64, P, P]),
     "mi_cuda_expf_verify": (I32, [U64, U64, P]),
