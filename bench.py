@@ -175,6 +175,96 @@ def run_reference_arm(args, rank: int):
     }), flush=True)
 
 
+L2_BYTES = 126 * 2 ** 20
+
+
+def _time_rotating(torch, fn, n_copies, launches, warmup):
+    """Device time per launch of fn(copy_index), cycling over copies."""
+    for i in range(warmup):
+        fn(i % n_copies)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(launches):
+        fn(i % n_copies)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / launches
+
+
+def run_gemv_sweep(args):
+    """Config 1: isolated Q8_0 GEMV (activation quantize fused) at the 0.5B shapes;
+    distinct weight copies rotate so every launch reads its weights from HBM."""
+    import torch
+    import mi_cuda
+    mi_cuda.init(0)
+    peak, peak_kind = load_peaks()
+    shapes = [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",")]
+    for n, k in shapes:
+        nb = mi_cuda.lib().mi_cuda_q8_0_packed_bytes(k, n)
+        npad = (n + 7) // 8 * 8
+        n_copies = max(1, -(-4 * L2_BYTES // nb)) if args.cold else 1
+        g = torch.Generator(device="cuda").manual_seed(n + k)
+        copies = []
+        for _ in range(n_copies):
+            buf = torch.empty(nb, dtype=torch.uint8, device="cuda")
+            buf[:npad * k].view(torch.int8).copy_(torch.randint(-127, 128, (npad * k,), generator=g, device="cuda",
+                                                                dtype=torch.int8))
+            sc = (torch.rand(npad * k // 32, generator=g, device="cuda") * 0.004 + 1e-4).to(torch.float16)
+            buf[npad * k:].view(torch.float16).copy_(sc)
+            copies.append(buf)
+        x = torch.randn(k, generator=g, device="cuda")
+        out = torch.empty(n, dtype=torch.float32, device="cuda")
+        L = mi_cuda.lib()
+        st = torch.cuda.current_stream().cuda_stream
+
+        def fn(i):
+            mi_cuda.check(L.mi_cuda_mul_mat_q8_0_f32(copies[i].data_ptr(), k, n, x.data_ptr(), 1, out.data_ptr(), st))
+
+        ms = _time_rotating(torch, fn, n_copies, args.steps, args.warmup)
+        algo = n * k * 34 // 32 + 4 * k + 4 * n
+        gbs = algo / (ms / 1e3) / 1e9
+        print(json.dumps({"config": "gemv", "shape": f"{n}x{k}", "us_per_launch": ms * 1e3,
+                          "bytes_per_launch": algo, "achieved_gbs": gbs, "peak_gbs": peak,
+                          "frac": gbs / peak, "peak_kind": peak_kind, "weight_copies": n_copies,
+                          "launches": args.steps}), flush=True)
+        del copies
+
+
+def run_attention(args):
+    """Config 2: fused decode attention, 14 query / 2 KV heads, head_dim 64, F32 KV,
+    one query token; K/V copies rotate so each launch reads its cache from HBM."""
+    import torch
+    import mi_cuda
+    mi_cuda.init(0)
+    peak, peak_kind = load_peaks()
+    H, HKV, D = 14, 2, 64
+    for n_kv in [int(v) for v in args.nkv.split(",")]:
+        kvb = 2 * n_kv * HKV * D * 4
+        n_copies = max(1, -(-4 * L2_BYTES // kvb)) if args.cold else 1
+        g = torch.Generator(device="cuda").manual_seed(n_kv)
+        ks = [torch.randn((n_kv, HKV, D), generator=g, device="cuda") for _ in range(n_copies)]
+        vs = [torch.randn((n_kv, HKV, D), generator=g, device="cuda") for _ in range(n_copies)]
+        q = torch.randn((H, D), generator=g, device="cuda")
+        out = torch.empty((H, D), dtype=torch.float32, device="cuda")
+        L = mi_cuda.lib()
+        scratch = torch.empty(L.mi_cuda_attention_decode_scratch_bytes(H, n_kv), dtype=torch.uint8, device="cuda")
+        st = torch.cuda.current_stream().cuda_stream
+
+        def fn(i):
+            mi_cuda.check(L.mi_cuda_attention_decode(q.data_ptr(), ks[i].data_ptr(), vs[i].data_ptr(), D, H, HKV,
+                                                     n_kv, 0.125, scratch.data_ptr(), out.data_ptr(), st))
+
+        ms = _time_rotating(torch, fn, n_copies, args.steps, args.warmup)
+        algo = kvb + 2 * H * D * 4
+        gbs = algo / (ms / 1e3) / 1e9
+        print(json.dumps({"config": "attention", "n_kv": n_kv, "us_per_launch": ms * 1e3,
+                          "bytes_per_launch": algo, "achieved_gbs": gbs, "peak_gbs": peak,
+                          "frac": gbs / peak, "peak_kind": peak_kind, "kv_copies": n_copies,
+                          "launches": args.steps}), flush=True)
+        del ks, vs
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -183,9 +273,19 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=PERIOD)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", choices=["decode", "gemv", "attention"], default="decode",
+                    help="decode: config 0 (default); gemv: config-1 GEMV sweep; attention: config 2")
+    ap.add_argument("--shapes", default="896x896,128x896,4864x896,896x4864,151936x896",
+                    help="gemv: NxK list")
+    ap.add_argument("--nkv", default="128,1024,4096,32768", help="attention: n_kv list")
+    ap.add_argument("--cold", type=int, default=1, help="gemv/attention: rotate copies past L2")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.config == "gemv":
+        return run_gemv_sweep(args)
+    if args.config == "attention":
+        return run_attention(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
