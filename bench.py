@@ -279,6 +279,7 @@ def main():
                     help="gemv: NxK list")
     ap.add_argument("--nkv", default="128,1024,4096,32768", help="attention: n_kv list")
     ap.add_argument("--cold", type=int, default=1, help="gemv/attention: rotate copies past L2")
+    ap.add_argument("--trace", action="store_true", help="decode: add the last step's kernel timeline")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -338,6 +339,24 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     gen = kv.read_tokens(N_PROMPT, N_PREDICT)
+    trace = None
+    if args.trace:
+        # per-kernel timeline of the last timed step (first CTA of each kernel)
+        t = kv.step_trace().astype(np.int64)
+        names = ["qkv", "attn", "o", "gate_up", "down"]
+        kinds = [names[i % 5] for i in range(t.shape[0] - 1)] + ["lm_head"]
+        trace = {"step_us": float(t[-1, 3] - t[0, 0]) / 1e3, "per_kernel_us": {}}
+        for k in dict.fromkeys(kinds):
+            idx = [i for i, kk in enumerate(kinds) if kk == k]
+            dep = [t[i, 1] - t[i - 1, 3] for i in idx if i > 0]  # wait after the predecessor's epilogue started
+            trace["per_kernel_us"][k] = {
+                "dep_to_prologue": float(np.mean([t[i, 2] - t[i, 1] for i in idx])) / 1e3,
+                "prologue_to_epilogue": float(np.mean([t[i, 3] - t[i, 2] for i in idx])) / 1e3,
+                "handoff": float(np.mean(dep)) / 1e3 if dep else None}
+        ai = [i for i, kk in enumerate(kinds) if kk == "attn"]
+        trace["attention_phases_us"] = {
+            name: float(np.mean([t[i, b] - t[i, a] for i in ai])) / 1e3
+            for name, a, b in (("scores", 2, 4), ("max_exp", 4, 5), ("sum", 5, 6), ("kv", 6, 7))}
 
     # roofline: algorithmic bytes of the timed steps over their device time
     n_kvs = [N_PROMPT + (i % PERIOD) + 1 for i in range(args.steps)]
@@ -397,6 +416,8 @@ def main():
             "cpu_baseline": cpu,
             "parity": parity,
         }
+        if trace is not None:
+            line["trace"] = trace
         print(json.dumps(line), flush=True)
     kv.free()
     model.free()

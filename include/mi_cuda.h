@@ -240,6 +240,16 @@ int mi_cuda_qwen2_set_position(mi_cuda_kv_cache* kv, const int32_t* h_tokens, in
 int mi_cuda_qwen2_decode_steps(mi_cuda_kv_cache* kv, int32_t n_steps, int32_t pos0,
                                int32_t period);
 int mi_cuda_qwen2_read_tokens(mi_cuda_kv_cache* kv, int32_t first, int32_t n, int32_t* h_out);
+/* Step trace (the reference's barrier statistics, src/threadpool.cpp:78-81,
+ * become device timestamps): for each kernel of the most recent decode step,
+ * 8 globaltimer stamps (ns) from its first CTA -- entry, predecessor done
+ * (dependency wait returned), prologue done, epilogue start, then up to four
+ * kernel-specific phase marks (attention: scores, exp, sum, KV done; 0 when
+ * unused). Copies up to max_slots kernels x 8 stamps into h_out; *n_slots =
+ * slots copied. */
+int mi_cuda_qwen2_step_trace(mi_cuda_kv_cache* kv, uint64_t* h_out, int32_t max_slots,
+                             int32_t* n_slots);
+
 /* The executor's CUDA stream (cudaStream_t) and its per-step kernel count. */
 mi_cuda_stream mi_cuda_qwen2_stream(mi_cuda_kv_cache* kv);
 int32_t mi_cuda_qwen2_kernels_per_step(mi_cuda_kv_cache* kv);

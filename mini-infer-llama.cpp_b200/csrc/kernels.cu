@@ -5,6 +5,7 @@
 // replaces.
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 
 #include "mi_device.cuh"
 
@@ -19,11 +20,11 @@ constexpr unsigned FULL = 0xffffffffu;
 // activation scales, per-row results, F32 input staging (norm prologues),
 // then n_stages weight stages of stage_rows rows each (quants, then scales).
 struct GemvSmem {
-  size_t act_qs, act_d, res, xs, stages, stage_bytes, total;
+  size_t act_qs, act_d, res, xs, sq, stages, stage_bytes, total;
 };
 
 __host__ __device__ inline GemvSmem gemv_smem(int64_t K, int32_t rows_per_cta, int32_t stage_rows,
-                                              int32_t n_stages, int32_t pro) {
+                                              int32_t n_stages, int32_t pro, int32_t stage_x) {
   GemvSmem L;
   size_t off = 128;
   L.act_qs = off;
@@ -33,6 +34,8 @@ __host__ __device__ inline GemvSmem gemv_smem(int64_t K, int32_t rows_per_cta, i
   L.res = off;
   off += (size_t)(((int64_t)rows_per_cta * 4 + 15) / 16 * 16);
   L.xs = off;
+  if (pro >= PRO_NORM_QUANT || (pro == PRO_QUANT && stage_x)) off += (size_t)(K * 4);
+  L.sq = off;  // squares for the rms_norm chain
   if (pro >= PRO_NORM_QUANT) off += (size_t)(K * 4);
   off = (off + 127) / 128 * 128;
   L.stages = off;
@@ -62,14 +65,14 @@ __host__ __device__ inline GemvSmem gemv_smem(int64_t K, int32_t rows_per_cta, i
 // the embedding lookup and rms_norm), the warps consume the stages, and the
 // epilogue applies bias / residual / SiLU*up / argmax.
 // ---------------------------------------------------------------------------
-template <int NT>
+template <int NT, int TPR>
 __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int NW = NT / 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t K = p.K;
   const int nb = (int)(K >> 5);
-  const GemvSmem L = gemv_smem(K, p.rows_per_cta, p.stage_rows, p.n_stages, p.pro);
+  const GemvSmem L = gemv_smem(K, p.rows_per_cta, p.stage_rows, p.n_stages, p.pro, p.stage_x);
   uint64_t* bars = (uint64_t*)smem;
   float* misc = (float*)(smem + 64);
   int8_t* aq = (int8_t*)(smem + L.act_qs);
@@ -96,6 +99,7 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
     bulk_load(st + (size_t)p.stage_rows * K, wd + tr0 * nb * 2, db, &bars[s]);
   };
 
+  trace_mark(p.trace, p.trace_slot, 0);
   if (tid == 0) {
     for (int s = 0; s < p.n_stages; s++) mbar_init(&bars[s], 1);
     fence_mbar_init();
@@ -104,7 +108,8 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
   if (tid == 0)
     for (int t = 0; t < min(n_tiles, p.n_stages); t++) issue(t);
   pdl_trigger();
-  pdl_wait();
+  pdl_wait_cta();
+  trace_mark(p.trace, p.trace_slot, 1);
 
   // ---- prologue: the quantized activation in shared memory ----
   if (p.pro == PRO_ACT) {
@@ -118,31 +123,36 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
     }
   } else {
     float scale = 1.0f;
-    if (p.pro >= PRO_NORM_QUANT) {
-      if (p.pro == PRO_EMBED_NORM) {
-        // mi_compute_get_rows on the Q8_0 embedding (ref src/ops_cpu.cpp:128-139).
-        const int32_t pos = *p.pos;
-        int tok = (pos >= 0 && pos < p.tokens_len) ? p.tokens[pos] : -1;
-        if (tok < 0 || tok >= p.embed_rows) {
-          if (tid == 0) atomicExch(p.err, 1 /* MI_CUDA_ERR_ARG */);
-          tok = 0;
-        }
-        for (int64_t k = tid; k < K; k += NT) {
-          const int64_t b = k >> 5;
-          const float d = packed_scale(p.embed, K, p.embed_npad, tok, b);
-          const float v = __fmul_rn((float)packed_qs(p.embed, K, tok, b)[k & 31], d);
-          xs[k] = v;
-          if (blockIdx.x == 0) p.x_out[k] = v;
-        }
-      } else {
-        for (int64_t k = tid; k < K; k += NT) xs[k] = p.x[k];
+    if (p.pro == PRO_EMBED_NORM) {
+      // mi_compute_get_rows on the Q8_0 embedding (ref src/ops_cpu.cpp:128-139).
+      const int32_t pos = *p.pos;
+      int tok = (pos >= 0 && pos < p.tokens_len) ? p.tokens[pos] : -1;
+      if (tok < 0 || tok >= p.embed_rows) {
+        if (tid == 0) atomicExch(p.err, 1 /* MI_CUDA_ERR_ARG */);
+        tok = 0;
       }
+      for (int64_t k = tid; k < K; k += NT) {
+        const int64_t b = k >> 5;
+        const float d = packed_scale(p.embed, K, p.embed_npad, tok, b);
+        const float v = __fmul_rn((float)packed_qs(p.embed, K, tok, b)[k & 31], d);
+        xs[k] = v;
+        if (blockIdx.x == 0) p.x_out[k] = v;
+      }
+    } else if (p.pro >= PRO_NORM_QUANT || p.stage_x) {
+      // All loads of x in flight at once (K is a multiple of 32).
+      const float4* x4 = (const float4*)p.x;
+      float4* xs4 = (float4*)xs;
+      for (int64_t k = tid; k < K / 4; k += NT) xs4[k] = x4[k];
+    }
+    __syncthreads();
+    if (p.pro >= PRO_NORM_QUANT) {
+      // mi_compute_rms_norm (ref src/ops_cpu.cpp:154-160): the squares in
+      // parallel, then their sum as one ordered chain.
+      float* sq = (float*)(smem + L.sq);
+      for (int64_t k = tid; k < K; k += NT) sq[k] = __fmul_rn(xs[k], xs[k]);
       __syncthreads();
       if (tid == 0) {
-        // mi_compute_rms_norm (ref src/ops_cpu.cpp:154-160): one ordered chain.
-        float ss = 0.0f;
-#pragma unroll 8
-        for (int64_t k = 0; k < K; k++) ss = __fadd_rn(ss, __fmul_rn(xs[k], xs[k]));
+        const float ss = ordered_sum_smem(sq, (int)K);
         const float mean = __fdiv_rn(ss, (float)K);
         misc[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
       }
@@ -155,13 +165,14 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
       if (p.pro >= PRO_NORM_QUANT)
         v = __fmul_rn(__fmul_rn(xs[k], scale), p.norm_w[k]);  // rms_norm, then MUL weight
       else
-        v = p.x[k];
+        v = p.stage_x ? xs[k] : p.x[k];
       float d;
       aq[k] = quantize_lane(v, &d);
       if (lane == 0) ad[b] = d;
     }
   }
   __syncthreads();
+  trace_mark(p.trace, p.trace_slot, 2);
 
   // ---- weight tiles ----
   const int rr = lane >> 3, j = lane & 7;
@@ -179,20 +190,53 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
     const int ngroups = (int)(min((int64_t)p.stage_rows, r1 - tr0) >> 2);
     const uint32_t* sq = (const uint32_t*)st;
     const __half* sd = (const __half*)(st + (size_t)p.stage_rows * K);
-    for (int g = warp; g < ngroups; g += NW) {
-      const uint32_t* gq = sq + (size_t)g * K;
-      const __half* gd = sd + (size_t)g * nb * 4;
-      float acc = 0.0f;
+    if (TPR == 8) {
+      // 8 threads per row, one lane each; a warp covers one group of 4 rows.
+      for (int g = warp; g < ngroups; g += NW) {
+        const uint32_t* gq = sq + (size_t)g * K;
+        const __half* gd = sd + (size_t)g * nb * 4;
+        float acc = 0.0f;
 #pragma unroll 4
-      for (int i = 0; i < nb; i++) {
-        const int pi = __dp4a((int)gq[i * 32 + lane], aq4[i * 8 + j], 0);
-        const float dxdy = __fmul_rn(__half2float(gd[i * 4 + rr]), ad[i]);
-        acc = __fmaf_rn(__int2float_rn(pi), dxdy, acc);
+        for (int i = 0; i < nb; i++) {
+          const int pi = __dp4a((int)gq[i * 32 + lane], aq4[i * 8 + j], 0);
+          const float dxdy = __fmul_rn(__half2float(gd[i * 4 + rr]), ad[i]);
+          acc = __fmaf_rn(__int2float_rn(pi), dxdy, acc);
+        }
+        const float s4 = __fadd_rn(acc, __shfl_xor_sync(FULL, acc, 4));
+        const float s1 = __fadd_rn(s4, __shfl_xor_sync(FULL, s4, 1));
+        const float s2 = __fadd_rn(s1, __shfl_xor_sync(FULL, s1, 2));
+        if (j == 0) res[t * p.stage_rows + g * 4 + rr] = s2;
       }
-      const float s4 = __fadd_rn(acc, __shfl_xor_sync(FULL, acc, 4));
-      const float s1 = __fadd_rn(s4, __shfl_xor_sync(FULL, s4, 1));
-      const float s2 = __fadd_rn(s1, __shfl_xor_sync(FULL, s1, 2));
-      if (j == 0) res[t * p.stage_rows + g * 4 + rr] = s2;
+    } else {
+      // 2 threads per row, lanes 4h..4h+3 each from one 16-byte load; a warp
+      // covers 4 groups (16 rows). Thread h=0 ends with l0..l3, its partner
+      // (lane ^ 1) with l4..l7.
+      const int gw = lane >> 3, r4 = (lane >> 1) & 3, h = lane & 1;
+      const uint4* aq16 = (const uint4*)aq;
+      for (int g0 = warp * 4; g0 < ngroups; g0 += NW * 4) {
+        const int g = g0 + gw;
+        const bool valid = g < ngroups;
+        const int gc = valid ? g : g0;  // out-of-range groups recompute g0, never store
+        const uint4* gq = (const uint4*)(sq + (size_t)gc * K);
+        const __half* gd = sd + (size_t)gc * nb * 4;
+        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll 2
+        for (int i = 0; i < nb; i++) {
+          const uint4 w = gq[i * 8 + (lane & 7)];
+          const uint4 a = aq16[i * 2 + h];
+          const float dxdy = __fmul_rn(__half2float(gd[i * 4 + r4]), ad[i]);
+          a0 = __fmaf_rn(__int2float_rn(__dp4a((int)w.x, (int)a.x, 0)), dxdy, a0);
+          a1 = __fmaf_rn(__int2float_rn(__dp4a((int)w.y, (int)a.y, 0)), dxdy, a1);
+          a2 = __fmaf_rn(__int2float_rn(__dp4a((int)w.z, (int)a.z, 0)), dxdy, a2);
+          a3 = __fmaf_rn(__int2float_rn(__dp4a((int)w.w, (int)a.w, 0)), dxdy, a3);
+        }
+        const float s0 = __fadd_rn(a0, __shfl_xor_sync(FULL, a0, 1));
+        const float s1 = __fadd_rn(a1, __shfl_xor_sync(FULL, a1, 1));
+        const float s2 = __fadd_rn(a2, __shfl_xor_sync(FULL, a2, 1));
+        const float s3 = __fadd_rn(a3, __shfl_xor_sync(FULL, a3, 1));
+        if (valid && h == 0)
+          res[t * p.stage_rows + g * 4 + r4] = __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+      }
     }
     __syncthreads();
     if (tid == 0 && t + p.n_stages < n_tiles) {
@@ -210,6 +254,22 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
   }
 
   // ---- epilogue ----
+  trace_mark(p.trace, p.trace_slot, 3);
+  if (p.epi == EPI_SILU_GATEUP_Q) {
+    // This CTA's 64 packed rows are gate/up rows of act elements [32b, 32b+32):
+    // act[a] = silu(gate) * up, then the down projection's quantize node.
+    if (warp == 0) {
+      const int64_t a = (r0 >> 3) * 4 + lane;       // act element of this lane
+      const int lr = (int)((a >> 2) * 8 + (a & 3) - r0);  // its gate row, local
+      const float v = __fmul_rn(silu_exact(res[lr], p.et), res[lr + 4]);
+      float d;
+      const int8_t q = quantize_lane(v, &d);
+      uint8_t* blk = p.act_out + (size_t)(r0 >> 6) * 36;
+      ((int8_t*)blk)[4 + lane] = q;
+      if (lane == 0) *(float*)blk = d;
+    }
+    return;
+  }
   if (p.epi == EPI_SILU_GATEUP) {
     for (int lr = tid; lr < nrows; lr += NT) {
       const int64_t r = r0 + lr;
@@ -296,31 +356,44 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
   }
 }
 
-GemvPlan plan_gemv(int64_t k, int64_t n, int num_sms, int pro) {
+cudaError_t prepare_attn_kernels(int optin);
+
+GemvPlan plan_gemv(int64_t k, int64_t n, int num_sms, int pro, int32_t rows_per_cta) {
   GemvPlan pl{};
   const int64_t n_pad = (n + 7) / 8 * 8;
   const int64_t groups8 = n_pad / 8;
   const int64_t target = std::max<int64_t>(1, std::min<int64_t>(num_sms, groups8));
-  pl.rows_per_cta = (int32_t)(((n_pad + target - 1) / target + 7) / 8 * 8);
+  pl.rows_per_cta = rows_per_cta > 0 ? rows_per_cta
+                                     : (int32_t)(((n_pad + target - 1) / target + 7) / 8 * 8);
   pl.grid = (int)((n_pad + pl.rows_per_cta - 1) / pl.rows_per_cta);
   const int64_t row_bytes = k + k / 32 * 2;
-  const int64_t big = 72 * 1024, small = 32 * 1024;
+  const int64_t big = 72 * 1024, stream_stage = 62 * 1024;
   int64_t sr = std::max<int64_t>(8, (big / row_bytes) / 8 * 8);
   sr = std::min<int64_t>(sr, pl.rows_per_cta);
   int64_t tiles = (pl.rows_per_cta + sr - 1) / sr;
-  if (tiles > 4) {  // streaming: smaller stages, a deeper ring
-    sr = std::max<int64_t>(8, (small / row_bytes) / 8 * 8);
+  if (tiles > 4) {  // streaming (LM head): a ring of stages
+    sr = std::max<int64_t>(8, (stream_stage / row_bytes) / 8 * 8);
     tiles = (pl.rows_per_cta + sr - 1) / sr;
   }
   pl.stage_rows = (int32_t)sr;
   pl.n_stages = (int32_t)std::min<int64_t>(tiles, 4);
   const size_t limit = 220 * 1024;
+  pl.stage_x = 1;
   for (;;) {
-    pl.smem = gemv_smem(k, pl.rows_per_cta, pl.stage_rows, pl.n_stages, pro).total;
-    if (pl.smem <= limit || pl.n_stages == 1) break;
-    pl.n_stages--;
+    pl.smem = gemv_smem(k, pl.rows_per_cta, pl.stage_rows, pl.n_stages, pro, pl.stage_x).total;
+    if (pl.smem <= limit) break;
+    if (pl.n_stages > 1) pl.n_stages--;
+    else if (pl.stage_x && pro == PRO_QUANT) pl.stage_x = 0;  // very wide K: quantize from global
+    else break;
   }
   pl.threads = 256;
+  // Wide stages (>= 64 rows keep >= 4 warps busy) use 2 threads per row and
+  // 16-byte loads; narrow ones use 8 threads per row for more parallelism.
+  pl.tpr = pl.stage_rows >= 64 ? 2 : 8;
+  if (const char* e = std::getenv("MI_CUDA_GEMV_TPR")) {
+    const int v = std::atoi(e);
+    if (v == 2 || v == 8) pl.tpr = v;
+  }
   return pl;
 }
 
@@ -328,11 +401,17 @@ cudaError_t prepare_kernels() {
   int dev = 0, optin = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  cudaFuncAttributes fa{};
-  if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, gemv_q8_kernel<256>);
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(gemv_q8_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              optin - (int)fa.sharedSizeBytes);
+  cudaFuncAttributes f8{}, f2{};
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&f8, gemv_q8_kernel<256, 8>);
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&f2, gemv_q8_kernel<256, 2>);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemv_q8_kernel<256, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             optin - (int)f8.sharedSizeBytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemv_q8_kernel<256, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             optin - (int)f2.sharedSizeBytes);
+  if (e == cudaSuccess) e = prepare_attn_kernels(optin);
+  return e;
 }
 
 cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& plan, cudaStream_t s, bool pdl) {
@@ -340,6 +419,7 @@ cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& plan, cudaStream_t 
   q.rows_per_cta = plan.rows_per_cta;
   q.stage_rows = plan.stage_rows;
   q.n_stages = plan.n_stages;
+  q.stage_x = plan.stage_x;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)plan.grid);
   cfg.blockDim = dim3(256);
@@ -350,7 +430,8 @@ cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& plan, cudaStream_t 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemv_q8_kernel<256>, q);
+  if (plan.tpr == 2) return cudaLaunchKernelEx(&cfg, gemv_q8_kernel<256, 2>, q);
+  return cudaLaunchKernelEx(&cfg, gemv_q8_kernel<256, 8>, q);
 }
 
 // ---------------------------------------------------------------------------
@@ -359,30 +440,83 @@ cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& plan, cudaStream_t 
 // mapping kvh = h / n_rep applied by index (no K/V copy). In executor mode it
 // also performs the step's RoPE on q and k (src/ops_cpu.cpp:270-302) and the
 // KV-cache append (MI_OP_CPY, src/ops_cpu.cpp:446-460).
+//
+// K and V are staged through shared memory in chunks of kv_tile positions (K
+// rows padded to head_dim + 1 floats so the per-position dot products read
+// conflict-free columns). In executor mode the first chunk -- every cached
+// position before this step's -- is loaded before the dependency wait, so the
+// loads overlap the QKV GEMV. Scores stay in shared memory when they fit.
+// Every chain keeps the reference's order: d ascending in QK, the softmax
+// denominator over positions in order, t ascending in KV.
 // ---------------------------------------------------------------------------
 template <bool EXEC>
 __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnParams p) {
+  extern __shared__ __align__(16) float sm[];
   __shared__ float qr[256], kr[256], vr[256];
   __shared__ float red[8];
   __shared__ float sh[2];
   const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int D = p.head_dim, half = D >> 1, HKV = p.n_head_kv;
+  const int NT = blockDim.x;
+  const int D = p.head_dim, half = D >> 1, HKV = p.n_head_kv, D4 = D >> 2;
   const int kvh = h / (p.n_head / HKV);
-  pdl_trigger();
-  pdl_wait();
+  const int KT = p.kv_tile, KP = D + 1;
+  float* Ks = sm;
+  float* Vs = Ks + (size_t)KT * KP;
+  float* scs = Vs + (size_t)KT * D;
+  const size_t rs = (size_t)HKV * D;
+  const float* kbase = p.cache_k + (size_t)kvh * D;
+  const float* vbase = p.cache_v + (size_t)kvh * D;
+
   int n_past, n_kv;
   if (EXEC) {
+    // pos was set before this step's graph started and changes only at its end.
     n_past = *p.pos;
     if (n_past < 0 || n_past >= p.n_ctx) {  // no cache row / RoPE entry for this position
+      pdl_trigger();
       if (tid == 0) atomicExch(p.err, 6 /* MI_CUDA_ERR_STATE */);
       return;
     }
     n_kv = n_past + 1;
+  } else {
+    n_kv = p.n_kv_fixed;
+    n_past = n_kv - 1;
+  }
+  // Rows [c0, c0 + rows) of the cache into the K / V chunk buffers; in executor
+  // mode row n_past is this step's and comes from kr / vr instead.
+  auto load_k = [&](int c0, int rows) {
+    for (int e = tid; e < rows * D4; e += NT) {
+      const int r = e / D4, c = e - r * D4;
+      if (EXEC && c0 + r == n_past) continue;
+      const float4 v = *(const float4*)(kbase + (size_t)(c0 + r) * rs + c * 4);
+      float* d = Ks + (size_t)r * KP + c * 4;
+      d[0] = v.x;
+      d[1] = v.y;
+      d[2] = v.z;
+      d[3] = v.w;
+    }
+  };
+  auto load_v = [&](int c0, int rows) {
+    for (int e = tid; e < rows * D4; e += NT) {
+      const int r = e / D4, c = e - r * D4;
+      if (EXEC && c0 + r == n_past) continue;
+      *(float4*)(Vs + (size_t)r * D + c * 4) = *(const float4*)(vbase + (size_t)(c0 + r) * rs + c * 4);
+    }
+  };
+  const int rows0 = min(KT, n_kv);
+  trace_mark(p.trace, p.trace_slot, 0);
+  if (EXEC) {
+    load_k(0, rows0);
+    load_v(0, rows0);
+  }
+  pdl_trigger();
+  pdl_wait_cta();
+  trace_mark(p.trace, p.trace_slot, 1);
+  if (EXEC) {
     const float2* cs = p.rope_cs + (size_t)n_past * half;
     const float* q = p.qkv + (size_t)h * D;
     const float* k = p.qkv + (size_t)p.n_head * D + (size_t)kvh * D;
     const float* v = p.qkv + (size_t)(p.n_head + HKV) * D + (size_t)kvh * D;
-    for (int i = tid; i < half; i += blockDim.x) {
+    for (int i = tid; i < half; i += NT) {
       const float2 c = cs[i];
       const float q0 = q[i], q1 = q[i + half], k0 = k[i], k1 = k[i + half];
       qr[i] = __fsub_rn(__fmul_rn(q0, c.x), __fmul_rn(q1, c.y));
@@ -390,84 +524,148 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnParams p) {
       kr[i] = __fsub_rn(__fmul_rn(k0, c.x), __fmul_rn(k1, c.y));
       kr[i + half] = __fadd_rn(__fmul_rn(k0, c.y), __fmul_rn(k1, c.x));
     }
-    for (int i = tid; i < D; i += blockDim.x) vr[i] = v[i];
+    for (int i = tid; i < D; i += NT) vr[i] = v[i];
     __syncthreads();
     if (h % (p.n_head / HKV) == 0) {
       float* kd = p.cache_k + ((size_t)n_past * HKV + kvh) * D;
       float* vd = p.cache_v + ((size_t)n_past * HKV + kvh) * D;
-      for (int i = tid; i < D; i += blockDim.x) {
+      for (int i = tid; i < D; i += NT) {
         kd[i] = kr[i];
         vd[i] = vr[i];
       }
     }
+    if (n_past < KT)
+      for (int i = tid; i < D; i += NT) {
+        Ks[(size_t)n_past * KP + i] = kr[i];
+        Vs[(size_t)n_past * D + i] = vr[i];
+      }
   } else {
-    n_kv = p.n_kv_fixed;
-    n_past = n_kv - 1;
-    for (int i = tid; i < D; i += blockDim.x) qr[i] = p.q_rot[(size_t)h * D + i];
-    __syncthreads();
+    for (int i = tid; i < D; i += NT) qr[i] = p.q_rot[(size_t)h * D + i];
+    load_k(0, rows0);
+    load_v(0, rows0);
   }
-  float* sc = p.scores + (size_t)h * p.scores_stride;
+  __syncthreads();
+  trace_mark(p.trace, p.trace_slot, 2);
+  float* sc = p.scores_in_smem ? scs : p.scores + (size_t)h * p.scores_stride;
+  const int n_chunks = (n_kv + KT - 1) / KT;
 
   // scores[i] * scale, d ascending with separate roundings (src/ops_cpu.cpp:373-376).
   float lmax = -INFINITY;
-  for (int i = tid; i < n_kv; i += blockDim.x) {
-    const float* kp = (EXEC && i == n_past) ? kr : p.cache_k + ((size_t)i * HKV + kvh) * D;
-    float acc = 0.0f;
-    for (int d = 0; d < D; d++) acc = __fadd_rn(acc, __fmul_rn(kp[d], qr[d]));
-    const float v = __fmul_rn(acc, p.scale);
-    sc[i] = v;
-    lmax = fmaxf(lmax, v);
+  for (int c = 0; c < n_chunks; c++) {
+    const int c0 = c * KT, rows = min(KT, n_kv - c0);
+    if (c > 0) {
+      __syncthreads();
+      load_k(c0, rows);
+      if (EXEC && n_past >= c0 && n_past < c0 + rows)
+        for (int i = tid; i < D; i += NT) Ks[(size_t)(n_past - c0) * KP + i] = kr[i];
+      __syncthreads();
+    }
+    for (int i = tid; i < rows; i += NT) {
+      const float acc = ordered_dot(0.0f, Ks + (size_t)i * KP, 1, qr, D);
+      const float v = __fmul_rn(acc, p.scale);
+      sc[c0 + i] = v;
+      lmax = fmaxf(lmax, v);
+    }
   }
+  trace_mark(p.trace, p.trace_slot, 4);
   lmax = warp_max(lmax);
   if (lane == 0) red[warp] = lmax;
   __syncthreads();
   if (tid == 0) {
     float m = red[0];
-    for (int w = 1; w < (int)(blockDim.x >> 5); w++) m = fmaxf(m, red[w]);
+    for (int w = 1; w < (NT >> 5); w++) m = fmaxf(m, red[w]);
     sh[0] = m;
   }
   __syncthreads();
   const float mx = sh[0];
-  for (int i = tid; i < n_kv; i += blockDim.x) sc[i] = expf_exact(__fsub_rn(sc[i], mx), p.et);
+  for (int i = tid; i < n_kv; i += NT) sc[i] = expf_exact(__fsub_rn(sc[i], mx), p.et);
   __syncthreads();
+  trace_mark(p.trace, p.trace_slot, 5);
   if (tid == 0) {
     // The softmax denominator: one ordered chain (src/ops_cpu.cpp:331-336).
     float sum = 0.0f;
+    if (p.scores_in_smem) {
+      sum = ordered_sum_smem(sc, n_kv);
+    } else {
 #pragma unroll 8
-    for (int i = 0; i < n_kv; i++) sum = __fadd_rn(sum, sc[i]);
+      for (int i = 0; i < n_kv; i++) sum = __fadd_rn(sum, sc[i]);
+    }
     sh[1] = __fdiv_rn(1.0f, sum);
   }
   __syncthreads();
   const float inv = sh[1];
-  for (int i = tid; i < n_kv; i += blockDim.x) sc[i] = __fmul_rn(sc[i], inv);
+  trace_mark(p.trace, p.trace_slot, 6);
+  for (int i = tid; i < n_kv; i += NT) sc[i] = __fmul_rn(sc[i], inv);
   __syncthreads();
+
   // out[o] = sum_t V[o, kvh, t] * P[t], t ascending (src/ops_cpu.cpp:402-406).
-  for (int o = tid; o < D; o += blockDim.x) {
-    float acc = 0.0f;
-    const float* vcol = p.cache_v + (size_t)kvh * D + o;
-    const size_t vstride = (size_t)HKV * D;
-#pragma unroll 4
-    for (int t = 0; t < n_kv; t++) {
-      const float vv = (EXEC && t == n_past) ? vr[o] : vcol[(size_t)t * vstride];
-      acc = __fadd_rn(acc, __fmul_rn(vv, sc[t]));
+  float acc = 0.0f;
+  for (int c = 0; c < n_chunks; c++) {
+    const int c0 = c * KT, rows = min(KT, n_kv - c0);
+    if (c > 0) {
+      __syncthreads();
+      load_v(c0, rows);
+      if (EXEC && n_past >= c0 && n_past < c0 + rows)
+        for (int i = tid; i < D; i += NT) Vs[(size_t)(n_past - c0) * D + i] = vr[i];
+      __syncthreads();
     }
-    p.out[(size_t)h * D + o] = acc;
+    if (tid < D) acc = ordered_dot(acc, Vs + tid, D, sc + c0, rows);
+  }
+  trace_mark(p.trace, p.trace_slot, 7);
+  trace_mark(p.trace, p.trace_slot, 3);
+  if (tid < D && p.out) p.out[(size_t)h * D + tid] = acc;
+  if (p.act_out && tid < D) {
+    // The O projection's quantize node (src/ops_cpu.cpp:462-479) for this head's
+    // outputs: warp w holds block h*D/32 + w of the concatenated heads.
+    float d;
+    const int8_t q = quantize_lane(acc, &d);
+    uint8_t* blk = p.act_out + ((size_t)h * (D >> 5) + (tid >> 5)) * 36;
+    ((int8_t*)blk)[4 + lane] = q;
+    if (lane == 0) *(float*)blk = d;
   }
 }
 
+namespace {
+constexpr int kAttnSmemBudget = 140 * 1024;  // dynamic shared memory per CTA
+constexpr int kScoresSmemMax = 8192;         // scores kept on chip up to this many positions
+}  // namespace
+
+cudaError_t prepare_attn_kernels(int optin) {
+  cudaFuncAttributes f0{}, f1{};
+  cudaError_t e = cudaFuncGetAttributes(&f0, attn_decode_kernel<false>);
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&f1, attn_decode_kernel<true>);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attn_decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             optin - (int)f0.sharedSizeBytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attn_decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             optin - (int)f1.sharedSizeBytes);
+  return e;
+}
+
 cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t s, bool pdl) {
+  AttnParams q = p;
+  // Positions the scores may need: n_ctx in executor mode, n_kv otherwise.
+  const int64_t max_kv = exec_mode ? p.n_ctx : p.n_kv_fixed;
+  q.scores_in_smem = max_kv <= kScoresSmemMax ? 1 : 0;
+  const int64_t sc_bytes = q.scores_in_smem ? ((max_kv * 4 + 15) / 16 * 16) : 0;
+  const int64_t row_bytes = (int64_t)(2 * p.head_dim + 1) * 4;
+  int64_t kt = (kAttnSmemBudget - sc_bytes) / row_bytes;
+  kt = std::min<int64_t>(256, kt) / 32 * 32;
+  if (kt < 32) kt = 32;
+  q.kv_tile = (int32_t)kt;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.n_head);
   cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = (size_t)(kt * row_bytes + sc_bytes);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (exec_mode) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<true>, p);
-  return cudaLaunchKernelEx(&cfg, attn_decode_kernel<false>, p);
+  if (exec_mode) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<true>, q);
+  return cudaLaunchKernelEx(&cfg, attn_decode_kernel<false>, q);
 }
 
 // ---------------------------------------------------------------------------

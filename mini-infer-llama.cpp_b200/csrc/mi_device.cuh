@@ -82,8 +82,31 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 // the predecessor grid has completed and its writes are visible. Both are
 // no-ops for a kernel launched without the attribute.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// The CTA-wide form: one thread waits (the predecessor's writes become visible
+// to the whole grid), the rest park on the CTA barrier, so a kernel launched
+// early does not keep 256 threads polling beside the kernel it waits for.
+__device__ __forceinline__ void pdl_wait_cta() {
+  if (threadIdx.x == 0) pdl_wait();
+  __syncthreads();
+}
 __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Step trace: CTA 0 of a traced kernel stores globaltimer stamps at fixed
+// points into its slot of kTracePoints entries: 0 entry, 1 dependency
+// satisfied, 2 prologue done, 3 epilogue start; 4-7 kernel-specific phases.
+constexpr int kTracePoints = 8;
+__device__ __forceinline__ void trace_mark(uint64_t* trace, int32_t slot, int point) {
+  if (trace && blockIdx.x == 0 && threadIdx.x == 0)
+    trace[(size_t)slot * kTracePoints + point] = globaltimer_ns();
 }
 
 // libm-exact expf: the double-precision core plus one probe of the exception
@@ -115,6 +138,57 @@ __device__ __forceinline__ float silu_exact(float x, const ExpTab& t) {
   return __fdiv_rn(x, __fadd_rn(1.0f, expf_exact(-x, t)));
 }
 
+// Sequential float sum s = ((0 + a[0]) + a[1]) + ... + a[n-1] (one rounding
+// per add, in order) for one thread, with the shared-memory loads issued 16
+// elements ahead of the dependent adds so the chain runs at add latency.
+// `a` is 16-byte aligned; any n.
+__device__ __forceinline__ float ordered_sum_smem(const float* a, int n) {
+  const float4* a4 = (const float4*)a;
+  const int n4 = n >> 2;
+  float s = 0.0f;
+  float4 b0 = make_float4(0, 0, 0, 0), b1 = b0, b2 = b0, b3 = b0;
+  if (n4 > 0) b0 = a4[0];
+  if (n4 > 1) b1 = a4[1];
+  if (n4 > 2) b2 = a4[2];
+  if (n4 > 3) b3 = a4[3];
+  int i = 0;
+  for (; i + 4 <= n4; i += 4) {
+    const float4 c0 = b0, c1 = b1, c2 = b2, c3 = b3;
+    if (i + 4 < n4) b0 = a4[i + 4];
+    if (i + 5 < n4) b1 = a4[i + 5];
+    if (i + 6 < n4) b2 = a4[i + 6];
+    if (i + 7 < n4) b3 = a4[i + 7];
+    s = __fadd_rn(s, c0.x); s = __fadd_rn(s, c0.y); s = __fadd_rn(s, c0.z); s = __fadd_rn(s, c0.w);
+    s = __fadd_rn(s, c1.x); s = __fadd_rn(s, c1.y); s = __fadd_rn(s, c1.z); s = __fadd_rn(s, c1.w);
+    s = __fadd_rn(s, c2.x); s = __fadd_rn(s, c2.y); s = __fadd_rn(s, c2.z); s = __fadd_rn(s, c2.w);
+    s = __fadd_rn(s, c3.x); s = __fadd_rn(s, c3.y); s = __fadd_rn(s, c3.z); s = __fadd_rn(s, c3.w);
+  }
+  for (; i < n4; i++) {
+    const float4 c = a4[i];
+    s = __fadd_rn(s, c.x); s = __fadd_rn(s, c.y); s = __fadd_rn(s, c.z); s = __fadd_rn(s, c.w);
+  }
+  for (int k = n4 * 4; k < n; k++) s = __fadd_rn(s, a[k]);
+  return s;
+}
+
+// acc + v[0]*p[0] + v[vs]*p[1] + ... in order, each product and each sum
+// rounded separately (no FMA), loads batched 16 ahead of the dependent adds.
+__device__ __forceinline__ float ordered_dot(float acc, const float* v, int vs, const float* p, int n) {
+  int t = 0;
+  for (; t + 16 <= n; t += 16) {
+    float a[16], b[16];
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+      a[u] = v[(size_t)(t + u) * vs];
+      b[u] = p[t + u];
+    }
+#pragma unroll
+    for (int u = 0; u < 16; u++) acc = __fadd_rn(acc, __fmul_rn(a[u], b[u]));
+  }
+  for (; t < n; t++) acc = __fadd_rn(acc, __fmul_rn(v[(size_t)t * vs], p[t]));
+  return acc;
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -125,7 +199,9 @@ __device__ __forceinline__ float warp_max(float v) {
 // (src/quant.cpp:199-218) for the element this lane holds; the warp holds the
 // block's 32 elements. Returns q, writes d (same on every lane).
 __device__ __forceinline__ int8_t quantize_lane(float v, float* d_out) {
-  float amax = warp_max(fabsf(v));
+  // max |v| over the block: the bit patterns of non-negative floats order like
+  // their values, so one integer warp reduction gives the exact maximum.
+  const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))));
   float d = __fdiv_rn(amax, 127.0f);
   float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
   int q = __float2int_rn(__fmul_rn(v, id));

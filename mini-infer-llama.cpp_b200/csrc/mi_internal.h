@@ -31,6 +31,9 @@ enum GemvEpilogue : int32_t {
   EPI_SILU_GATEUP = 3,  // packed rows 8q+t / 8q+4+t are gate / up row 4q+t:
                         // out[4q+t] = silu(gate) * up
   EPI_ARGMAX = 4,       // out[r] = dot, plus the greedy token over all rows
+  EPI_SILU_GATEUP_Q = 5,  // as EPI_SILU_GATEUP, but each CTA owns 64 packed rows (one
+                          // 32-element block of the result) and stores that block
+                          // quantized to Q8_0_ACT at act_out (the down GEMV's input)
 };
 
 struct GemvParams {
@@ -38,6 +41,7 @@ struct GemvParams {
   int64_t K, N, n_pad;
   int32_t rows_per_cta, stage_rows, n_stages, pro, epi;
   int32_t tokens_len;  // entries of `tokens` / `tokens_rw` (bounds for pos)
+  int32_t stage_x;     // set by the launcher: F32 input staged in shared memory
   // prologue inputs
   const float* x;
   const uint8_t* act;  // Q8_0_ACT, K/32 blocks of 36 B
@@ -53,6 +57,7 @@ struct GemvParams {
   const float* bias;
   const float* resid;
   float* out;
+  uint8_t* act_out;  // EPI_SILU_GATEUP_Q: Q8_0_ACT blocks of the result
   // EPI_ARGMAX
   float* part_val;
   int32_t* part_idx;
@@ -63,16 +68,19 @@ struct GemvParams {
   const int32_t* feedback;
   ExpTab et;
   int32_t* err;
+  uint64_t* trace;     // optional step trace (4 stamps per kernel slot)
+  int32_t trace_slot;
 };
 
 struct GemvPlan {
-  int grid, threads;
-  int32_t rows_per_cta, stage_rows, n_stages;
+  int grid, threads, tpr;
+  int32_t rows_per_cta, stage_rows, n_stages, stage_x;
   size_t smem;
 };
 
 // Work split for an n-row, k-column packed matrix over the device's SMs.
-GemvPlan plan_gemv(int64_t k, int64_t n, int num_sms, int pro);
+// rows_per_cta > 0 fixes the rows per CTA (a multiple of 8).
+GemvPlan plan_gemv(int64_t k, int64_t n, int num_sms, int pro, int32_t rows_per_cta = 0);
 // Per-device kernel attributes (dynamic shared memory limit); called once per
 // device at context creation, outside any stream capture.
 cudaError_t prepare_kernels();
@@ -91,11 +99,16 @@ struct AttnParams {
   const float2* rope_cs;  // executor: [pos][head_dim/2] (cos, sin)
   float scale;
   int32_t n_ctx;         // executor: cache / RoPE table capacity (bounds for pos)
-  float* scores;        // scratch [n_head][scores_stride]
+  float* scores;        // scratch [n_head][scores_stride] (used when the scores do not fit on chip)
   int64_t scores_stride;
-  float* out;           // [n_head][hd]
+  float* out;           // [n_head][hd]; may be null when act_out is set
+  uint8_t* act_out;     // optional: the output quantized to Q8_0_ACT (head_dim % 32 == 0)
   ExpTab et;
   int32_t* err;
+  int32_t kv_tile;         // set by the launcher: K/V positions per shared-memory chunk
+  int32_t scores_in_smem;  // set by the launcher
+  uint64_t* trace;         // optional step trace (4 stamps per kernel slot)
+  int32_t trace_slot;
 };
 cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t s, bool pdl);
 

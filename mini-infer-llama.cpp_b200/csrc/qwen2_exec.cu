@@ -19,6 +19,7 @@
 // The step position lives on the device, so one graph serves every step.
 #include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -65,6 +66,8 @@ int fail(int code, const std::string& msg) {
       return fail(MI_CUDA_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e)); \
   } while (0)
 
+constexpr int kTraceStamps = 8;  // globaltimer stamps per kernel slot (mi_device.cuh)
+
 int64_t npad8(int64_t n) { return (n + 7) / 8 * 8; }
 size_t packed_bytes(int64_t k, int64_t n) { return (size_t)(npad8(n) * k + npad8(n) * (k / 32) * 2); }
 size_t a256(size_t v) { return (v + 255) / 256 * 256; }
@@ -91,6 +94,9 @@ struct mi_cuda_kv_cache {
   float* cache = nullptr;  // [layer][k|v][n_ctx][HKV][D]
   float2* rope = nullptr;
   float *x = nullptr, *x2 = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr;
+  // Q8_0_ACT inputs of the O and down GEMVs, quantized by their producers
+  uint8_t *attn_q = nullptr, *act_q = nullptr;
+  bool quant_attn = false;  // head_dim % 32 == 0: attention emits whole blocks
   float* logits = nullptr;
   float* scores = nullptr;
   float* part_val = nullptr;
@@ -101,6 +107,8 @@ struct mi_cuda_kv_cache {
   int32_t* h_tokens = nullptr;   // pinned staging, n_ctx + 1
   cudaGraphExec_t g_head = nullptr, g_nohead = nullptr;
   int32_t kernels_per_step = 0;
+  uint64_t* trace = nullptr;  // [slot][4] globaltimer stamps of the last step
+  int32_t trace_slots = 0;
   bool pdl = true;
   GemvPlan plan_qkv{}, plan_o{}, plan_gu{}, plan_down{}, plan_head{};
   cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
@@ -172,8 +180,9 @@ int mi_cuda_qwen2_model_load(const char* gguf_path, int device, mi_cuda_model** 
   if (!te) return fail(MI_CUDA_ERR_FORMAT, "missing tensor token_embd.weight");
   hp.n_vocab = (int32_t)te->ne[1];
   const int64_t E = hp.n_embd, D = hp.head_dim, kvd = (int64_t)hp.n_head_kv * D, FF = hp.n_ff;
-  if (E % 64 != 0 || FF % 64 != 0 || D % 2 != 0 || D > 256)
-    return fail(MI_CUDA_ERR_FORMAT, "unsupported shape (n_embd and n_ff must be multiples of 64, head_dim <= 256)");
+  if (E % 64 != 0 || FF % 64 != 0 || D % 4 != 0 || D > 256)
+    return fail(MI_CUDA_ERR_FORMAT,
+                "unsupported shape (n_embd and n_ff multiples of 64, head_dim a multiple of 4 up to 256)");
 
   auto need = [&](const std::string& name, uint32_t type, int64_t ne0, int64_t ne1,
                   const GgufTensor** t) -> int {
@@ -375,6 +384,8 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     p.out = kv->qkv;
     p.et = et;
     p.err = err;
+    p.trace = kv->trace;
+    p.trace_slot = count;
     CK(launch_gemv(p, kv->plan_qkv, kv->stream, pdl));
     pdl = kv->pdl;
     count++;
@@ -392,9 +403,12 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     a.n_ctx = kv->n_ctx;
     a.scores = kv->scores;
     a.scores_stride = kv->n_ctx;
-    a.out = kv->attn;
+    a.out = kv->quant_attn ? nullptr : kv->attn;
+    a.act_out = kv->quant_attn ? kv->attn_q : nullptr;
     a.et = et;
     a.err = err;
+    a.trace = kv->trace;
+    a.trace_slot = count;
     CK(launch_attn_decode(a, true, kv->stream, pdl));
     count++;
 
@@ -403,13 +417,16 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     o.K = E;
     o.N = E;
     o.n_pad = L.o.npad;
-    o.pro = PRO_QUANT;
+    o.pro = kv->quant_attn ? PRO_ACT : PRO_QUANT;
+    o.act = kv->attn_q;
     o.x = kv->attn;
     o.epi = EPI_RESID;
     o.resid = kv->x;
     o.out = kv->x2;
     o.et = et;
     o.err = err;
+    o.trace = kv->trace;
+    o.trace_slot = count;
     CK(launch_gemv(o, kv->plan_o, kv->stream, pdl));
     count++;
 
@@ -422,10 +439,12 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     gu.x = kv->x2;
     gu.norm_w = L.ffn_norm;
     gu.eps = hp.rms_eps;
-    gu.epi = EPI_SILU_GATEUP;
-    gu.out = kv->act;
+    gu.epi = EPI_SILU_GATEUP_Q;
+    gu.act_out = kv->act_q;
     gu.et = et;
     gu.err = err;
+    gu.trace = kv->trace;
+    gu.trace_slot = count;
     CK(launch_gemv(gu, kv->plan_gu, kv->stream, pdl));
     count++;
 
@@ -434,13 +453,15 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     dn.K = FF;
     dn.N = E;
     dn.n_pad = L.down.npad;
-    dn.pro = PRO_QUANT;
-    dn.x = kv->act;
+    dn.pro = PRO_ACT;
+    dn.act = kv->act_q;
     dn.epi = EPI_RESID;
     dn.resid = kv->x2;
     dn.out = kv->x;
     dn.et = et;
     dn.err = err;
+    dn.trace = kv->trace;
+    dn.trace_slot = count;
     CK(launch_gemv(dn, kv->plan_down, kv->stream, pdl));
     count++;
   }
@@ -466,6 +487,8 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     h.feedback = &kv->state->feedback;
     h.et = et;
     h.err = err;
+    h.trace = kv->trace;
+    h.trace_slot = count;
     CK(launch_gemv(h, kv->plan_head, kv->stream, pdl));
   } else {
     CK(launch_advance(&kv->state->pos, kv->stream, pdl));
@@ -517,11 +540,16 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
   auto kv = std::make_unique<mi_cuda_kv_cache>();
   kv->model = m;
   kv->n_ctx = n_ctx;
+  // MI_CUDA_NO_PDL=1 captures the step without programmatic dependent launch
+  // (plain stream order), for comparing the two schedules.
+  if (const char* e = std::getenv("MI_CUDA_NO_PDL")) kv->pdl = std::atoi(e) == 0;
   const int sms = m->ctx->num_sms;
+  kv->quant_attn = D % 32 == 0;
   kv->plan_qkv = plan_gemv(E, E + 2 * kvd, sms, PRO_EMBED_NORM);
-  kv->plan_o = plan_gemv(E, E, sms, PRO_QUANT);
-  kv->plan_gu = plan_gemv(E, 2 * FF, sms, PRO_NORM_QUANT);
-  kv->plan_down = plan_gemv(FF, E, sms, PRO_QUANT);
+  kv->plan_o = plan_gemv(E, E, sms, kv->quant_attn ? PRO_ACT : PRO_QUANT);
+  // one 32-element block of the FFN activation (64 packed gate/up rows) per CTA
+  kv->plan_gu = plan_gemv(E, 2 * FF, sms, PRO_NORM_QUANT, 64);
+  kv->plan_down = plan_gemv(FF, E, sms, PRO_ACT);
   kv->plan_head = plan_gemv(E, hp.n_vocab, sms, PRO_NORM_QUANT);
 
   const size_t cache_bytes = (size_t)hp.n_layer * 2 * n_ctx * kvd * 4;
@@ -537,7 +565,9 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
                o_act = slot(FF * 4), o_logits = slot((size_t)hp.n_vocab * 4),
                o_scores = slot((size_t)hp.n_head * n_ctx * 4), o_pv = slot(1024 * 4),
                o_pi = slot(1024 * 4), o_tok = slot((size_t)(n_ctx + 1) * 4),
-               o_state = slot(sizeof(StepState));
+               o_state = slot(sizeof(StepState)), o_attnq = slot(E / 32 * 36),
+               o_actq = slot(FF / 32 * 36),
+               o_trace = slot((size_t)(5 * hp.n_layer + 1) * kTraceStamps * 8);
   CK(cudaMalloc(&kv->buf, off));
   CK(cudaMemset(kv->buf, 0, off));
   kv->cache = (float*)(kv->buf + o_cache);
@@ -553,6 +583,10 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
   kv->part_idx = (int32_t*)(kv->buf + o_pi);
   kv->tokens = (int32_t*)(kv->buf + o_tok);
   kv->state = (StepState*)(kv->buf + o_state);
+  kv->attn_q = kv->buf + o_attnq;
+  kv->act_q = kv->buf + o_actq;
+  kv->trace = (uint64_t*)(kv->buf + o_trace);
+  kv->trace_slots = 5 * hp.n_layer + 1;
   if (kv->plan_head.grid > 1024) return fail(MI_CUDA_ERR_ARG, "LM head grid too large");
 
   std::vector<float> cs((size_t)n_ctx * (D / 2) * 2);
@@ -638,6 +672,18 @@ int mi_cuda_qwen2_read_tokens(mi_cuda_kv_cache* kv, int32_t first, int32_t n, in
 mi_cuda_stream mi_cuda_qwen2_stream(mi_cuda_kv_cache* kv) { return kv ? (mi_cuda_stream)kv->stream : nullptr; }
 
 int32_t mi_cuda_qwen2_kernels_per_step(mi_cuda_kv_cache* kv) { return kv ? kv->kernels_per_step : 0; }
+
+int mi_cuda_qwen2_step_trace(mi_cuda_kv_cache* kv, uint64_t* h_out, int32_t max_slots,
+                             int32_t* n_slots) {
+  if (!kv || !h_out || max_slots < 0 || !n_slots)
+    return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_step_trace: bad arguments");
+  CK(cudaSetDevice(kv->model->device));
+  CK(cudaStreamSynchronize(kv->stream));
+  const int32_t n = std::min(max_slots, kv->trace_slots);
+  CK(cudaMemcpy(h_out, kv->trace, (size_t)n * kTraceStamps * 8, cudaMemcpyDeviceToHost));
+  *n_slots = n;
+  return MI_CUDA_OK;
+}
 
 int mi_cuda_qwen2_forward(mi_cuda_model* m, mi_cuda_kv_cache* kv, const int32_t* h_tokens,
                           int32_t n_tokens, int32_t n_past, int32_t last_logits_only,

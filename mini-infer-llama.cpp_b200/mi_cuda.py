@@ -85,6 +85,7 @@ _SIGS = {
     "mi_cuda_qwen2_read_tokens": (I32, [P, I32, I32, P]),
     "mi_cuda_qwen2_stream": (P, [P]),
     "mi_cuda_qwen2_kernels_per_step": (I32, [P]),
+    "mi_cuda_qwen2_step_trace": (I32, [P, P, I32, P]),
 }
 
 _lib = None
@@ -374,6 +375,16 @@ class KVCache:
     @property
     def kernels_per_step(self) -> int:
         return int(lib().mi_cuda_qwen2_kernels_per_step(self.h))
+
+    def step_trace(self) -> np.ndarray:
+        """[kernels, 8] globaltimer stamps (ns) of the last step (first CTA):
+        entry, predecessor done, prologue done, epilogue start, then the
+        kernel's own phase marks (attention: scores, exp, sum, KV done)."""
+        n = self.kernels_per_step
+        out = np.zeros((n, 8), dtype=np.uint64)
+        got = C.c_int32()
+        check(lib().mi_cuda_qwen2_step_trace(self.h, out.ctypes.data, n, C.byref(got)))
+        return out[:got.value]
 
     def free(self):
         if self.h:

@@ -75,6 +75,24 @@ def test_generate_token_identical(mc, model_path, shape, seed, n_ctx, n_prompt, 
     model.free()
 
 
+def test_step_trace(mc, model_path):
+    path = model_path("SMALL", 4)
+    model = mc.Qwen2Model(path)
+    kv = mc.KVCache(model, 64)
+    kv.set_position(np.array([1, 2, 3], dtype=np.int32), 2)
+    kv.decode_steps(3)
+    t = kv.step_trace().astype(np.int64)
+    assert t.shape == (kv.kernels_per_step, 8) == (5 * 4 + 1, 8)
+    assert np.all(t[:, :4] > 0)
+    assert np.all(np.diff(t[:, :4], axis=1) >= 0)    # entry <= dep done <= prologue <= epilogue
+    attn = t[1::5][:4]                               # attention phases: scores, exp, sum, KV
+    assert np.all(np.diff(attn[:, [2, 4, 5, 6, 7]], axis=1) >= 0)
+    assert np.all(t[1:, 1] >= t[:-1, 1])             # kernels' dependent sections run in order
+    assert t[-1, 3] - t[0, 0] < 10_000_000           # the step took less than 10 ms
+    kv.free()
+    model.free()
+
+
 def test_context_limit_matches_reference(mc, model_path):
     # The reference stops decoding once n_past reaches n_ctx (src/main.cpp:409-423).
     path = model_path("TINY", 1)
