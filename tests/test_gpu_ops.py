@@ -64,7 +64,7 @@ def test_quantize_act_bitexact(mc, S, torch_cuda, k, m):
 CONFIG1 = [(896, 896), (128, 896), (4864, 896), (896, 4864), (151936, 896)]
 
 
-@pytest.mark.parametrize("n,k", CONFIG1 + [(132, 64), (12, 96)])
+@pytest.mark.parametrize("n,k", CONFIG1 + [(132, 64), (12, 96), (4096, 2048), (2048, 8192), (3584, 3584)])
 def test_gemv_config1_bitexact(mc, S, torch_cuda, n, k):
     torch = torch_cuda
     rng = np.random.default_rng(n + 3 * k)
