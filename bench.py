@@ -50,6 +50,10 @@ N_CTX, N_PROMPT, N_PREDICT = 2048, 32, 128
 PERIOD = N_PREDICT - 1  # decode forwards per generated sequence
 METRIC = "decode tok/s (0.5B-shape Q8_0, ctx 2048)"
 PUBLISHED_BEST = 64.035  # reference Q8_0 decode tok/s, 4 threads (README.md:106)
+# DRAM bytes (read + write) of one decode step, summed from ncu captures of every
+# kernel of one step at n_kv = 33 (profiles/decode_step_qwen2_05b.md):
+# 24 x 17.24 MB per layer + 150.3 MB for the LM head.
+TRAFFIC_PER_STEP = 24 * 17.24e6 + 150.3e6
 
 
 def step_bytes(hp, n_kv: int) -> int:
@@ -406,7 +410,9 @@ def main():
                        "n_ctx": N_CTX, "prompt": N_PROMPT, "parallelism": f"replicas x{world}",
                        "l2": "inputs larger than L2: 527 MB of weights streamed from HBM every step"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                         "frac": achieved / peak, "traffic": TRAFFIC_PER_STEP,
+                         "traffic_source": "ncu dram__bytes_read+write, one step, n_kv 33",
+                         "peak_kind": peak_kind,
                          "kernel": f"decode step graph ({kv.kernels_per_step} kernels)",
                          "bytes_per_step": total_bytes / args.steps},
             "e2e": {"value": e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": 4 + 32,

@@ -14,13 +14,16 @@ namespace mi {
 namespace {
 
 constexpr unsigned FULL = 0xffffffffu;
+// Shortest chain evaluated with spec_ordered_sum; below it one thread's serial
+// chain is faster than the CTA-wide speculation's fixed cost.
+constexpr int kSpecSumMin = 256;
 
 // Shared-memory map of the GEMV kernel, computed identically on host and
 // device: [0,64) mbarriers, [64,128) broadcast scalars, activation quants,
 // activation scales, per-row results, F32 input staging (norm prologues),
 // then n_stages weight stages of stage_rows rows each (quants, then scales).
 struct GemvSmem {
-  size_t act_qs, act_d, res, xs, sq, stages, stage_bytes, total;
+  size_t act_qs, act_d, res, xs, sq, spec, stages, stage_bytes, total;
 };
 
 __host__ __device__ inline GemvSmem gemv_smem(int64_t K, int32_t rows_per_cta, int32_t stage_rows,
@@ -35,8 +38,10 @@ __host__ __device__ inline GemvSmem gemv_smem(int64_t K, int32_t rows_per_cta, i
   off += (size_t)(((int64_t)rows_per_cta * 4 + 15) / 16 * 16);
   L.xs = off;
   if (pro >= PRO_NORM_QUANT || (pro == PRO_QUANT && stage_x)) off += (size_t)(K * 4);
-  L.sq = off;  // squares for the rms_norm chain
-  if (pro >= PRO_NORM_QUANT) off += (size_t)(K * 4);
+  L.sq = off;  // squares for the rms_norm chain, plus the chain loads' slack
+  if (pro >= PRO_NORM_QUANT) off += (size_t)(K * 4 + kChainSlackBytes);
+  L.spec = off;  // spec_ordered_sum scratch for that chain (8 warps, up to 4 chains a lane)
+  if (pro >= PRO_NORM_QUANT) off += (size_t)((spec_sum_scratch_bytes(8, 4) + 15) / 16 * 16);
   off = (off + 127) / 128 * 128;
   L.stages = off;
   L.stage_bytes = (size_t)(((int64_t)stage_rows * K + (int64_t)stage_rows * (K / 32) * 2 + 127) / 128 * 128);
@@ -151,8 +156,9 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
       float* sq = (float*)(smem + L.sq);
       for (int64_t k = tid; k < K; k += NT) sq[k] = __fmul_rn(xs[k], xs[k]);
       __syncthreads();
+      const float ss = K <= 1024 ? spec_ordered_sum<NT, 2>(sq, (int)K, smem + L.spec)
+                                 : spec_ordered_sum<NT, 4>(sq, (int)K, smem + L.spec);
       if (tid == 0) {
-        const float ss = ordered_sum_smem(sq, (int)K);
         const float mean = __fdiv_rn(ss, (float)K);
         misc[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
       }
@@ -397,23 +403,33 @@ GemvPlan plan_gemv(int64_t k, int64_t n, int num_sms, int pro, int32_t rows_per_
   return pl;
 }
 
+namespace {
+template <int TPR>
+cudaError_t set_gemv_smem(int optin) {
+  cudaFuncAttributes f{};
+  cudaError_t e = cudaFuncGetAttributes(&f, gemv_q8_kernel<256, TPR>);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemv_q8_kernel<256, TPR>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             optin - (int)f.sharedSizeBytes);
+  return e;
+}
+}  // namespace
+
 cudaError_t prepare_kernels() {
   int dev = 0, optin = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  cudaFuncAttributes f8{}, f2{};
-  if (e == cudaSuccess) e = cudaFuncGetAttributes(&f8, gemv_q8_kernel<256, 8>);
-  if (e == cudaSuccess) e = cudaFuncGetAttributes(&f2, gemv_q8_kernel<256, 2>);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(gemv_q8_kernel<256, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             optin - (int)f8.sharedSizeBytes);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(gemv_q8_kernel<256, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             optin - (int)f2.sharedSizeBytes);
+  if (e == cudaSuccess) e = set_gemv_smem<8>(optin);
+  if (e == cudaSuccess) e = set_gemv_smem<2>(optin);
   if (e == cudaSuccess) e = prepare_attn_kernels(optin);
   return e;
 }
 
+// One kernel function serves every prologue/epilogue combination of a thread
+// mapping: consecutive GEMVs of a step then run the same code, which is still
+// in the SMs' instruction caches (measured: per-variant instantiations made
+// the decode step about 2.5% slower).
 cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& plan, cudaStream_t s, bool pdl) {
   GemvParams q = p;
   q.rows_per_cta = plan.rows_per_cta;
@@ -449,12 +465,13 @@ cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& plan, cudaStream_t 
 // Every chain keeps the reference's order: d ascending in QK, the softmax
 // denominator over positions in order, t ascending in KV.
 // ---------------------------------------------------------------------------
-template <bool EXEC>
+template <bool EXEC, bool SPEC>
 __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnParams p) {
   extern __shared__ __align__(16) float sm[];
   __shared__ float qr[256], kr[256], vr[256];
   __shared__ float red[8];
   __shared__ float sh[2];
+  __shared__ __align__(16) uint8_t spec[SPEC ? spec_sum_scratch_bytes(8, 4) : 16];
   const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int NT = blockDim.x;
   const int D = p.head_dim, half = D >> 1, HKV = p.n_head_kv, D4 = D >> 2;
@@ -581,8 +598,15 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnParams p) {
   for (int i = tid; i < n_kv; i += NT) sc[i] = expf_exact(__fsub_rn(sc[i], mx), p.et);
   __syncthreads();
   trace_mark(p.trace, p.trace_slot, 5);
-  if (tid == 0) {
-    // The softmax denominator: one ordered chain (src/ops_cpu.cpp:331-336).
+  // The softmax denominator: one ordered chain (src/ops_cpu.cpp:331-336),
+  // evaluated by the whole CTA with spec_ordered_sum when it is long (the SPEC
+  // instantiation; the code costs the short-context kernel registers and
+  // time even when not taken, so that one leaves it out).
+  if (SPEC && p.scores_in_smem && n_kv >= kSpecSumMin) {
+    const float sum = n_kv <= 1024 ? spec_ordered_sum<256, 2>(sc, n_kv, spec)
+                                   : spec_ordered_sum<256, 4>(sc, n_kv, spec);
+    if (tid == 0) sh[1] = __fdiv_rn(1.0f, sum);
+  } else if (tid == 0) {
     float sum = 0.0f;
     if (p.scores_in_smem) {
       sum = ordered_sum_smem(sc, n_kv);
@@ -630,16 +654,23 @@ constexpr int kAttnSmemBudget = 140 * 1024;  // dynamic shared memory per CTA
 constexpr int kScoresSmemMax = 8192;         // scores kept on chip up to this many positions
 }  // namespace
 
+namespace {
+template <bool EXEC, bool SPEC>
+cudaError_t set_attn_smem(int optin) {
+  cudaFuncAttributes f{};
+  cudaError_t e = cudaFuncGetAttributes(&f, attn_decode_kernel<EXEC, SPEC>);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attn_decode_kernel<EXEC, SPEC>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             optin - (int)f.sharedSizeBytes);
+  return e;
+}
+}  // namespace
+
 cudaError_t prepare_attn_kernels(int optin) {
-  cudaFuncAttributes f0{}, f1{};
-  cudaError_t e = cudaFuncGetAttributes(&f0, attn_decode_kernel<false>);
-  if (e == cudaSuccess) e = cudaFuncGetAttributes(&f1, attn_decode_kernel<true>);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(attn_decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             optin - (int)f0.sharedSizeBytes);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(attn_decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             optin - (int)f1.sharedSizeBytes);
+  cudaError_t e = set_attn_smem<true, false>(optin);
+  if (e == cudaSuccess) e = set_attn_smem<false, false>(optin);
+  if (e == cudaSuccess) e = set_attn_smem<false, true>(optin);
   return e;
 }
 
@@ -648,7 +679,7 @@ cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t
   // Positions the scores may need: n_ctx in executor mode, n_kv otherwise.
   const int64_t max_kv = exec_mode ? p.n_ctx : p.n_kv_fixed;
   q.scores_in_smem = max_kv <= kScoresSmemMax ? 1 : 0;
-  const int64_t sc_bytes = q.scores_in_smem ? ((max_kv * 4 + 15) / 16 * 16) : 0;
+  const int64_t sc_bytes = q.scores_in_smem ? ((max_kv * 4 + 15) / 16 * 16 + kChainSlackBytes) : 0;
   const int64_t row_bytes = (int64_t)(2 * p.head_dim + 1) * 4;
   int64_t kt = (kAttnSmemBudget - sc_bytes) / row_bytes;
   kt = std::min<int64_t>(256, kt) / 32 * 32;
@@ -664,8 +695,10 @@ cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (exec_mode) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<true>, q);
-  return cudaLaunchKernelEx(&cfg, attn_decode_kernel<false>, q);
+  if (exec_mode) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<true, false>, q);
+  if (q.scores_in_smem && p.n_kv_fixed >= kSpecSumMin)
+    return cudaLaunchKernelEx(&cfg, attn_decode_kernel<false, true>, q);
+  return cudaLaunchKernelEx(&cfg, attn_decode_kernel<false, false>, q);
 }
 
 // ---------------------------------------------------------------------------
@@ -769,11 +802,29 @@ cudaError_t launch_get_rows(const uint8_t* table, int64_t ne0, int64_t n_pad,
   return cudaGetLastError();
 }
 
-// mi_compute_rms_norm (src/ops_cpu.cpp:143-165): one CTA per row.
-__global__ void rms_norm_kernel(const float* x, int64_t ne0, float eps, float* dst) {
+// mi_compute_rms_norm (src/ops_cpu.cpp:143-165): one CTA per row. Rows that
+// fit in shared memory sum their squares with spec_ordered_sum; longer rows
+// keep one thread's serial chain.
+namespace {
+constexpr int64_t kRmsStagedMax = 10240;  // 40 KB of squares + static scratch stay under 48 KB
+}
+
+__global__ void __launch_bounds__(256) rms_norm_kernel(const float* x, int64_t ne0, float eps,
+                                                       float* dst, int staged) {
+  extern __shared__ __align__(16) float sqs[];
+  __shared__ __align__(16) uint8_t spec[spec_sum_scratch_bytes(8, 4)];
   __shared__ float scale;
   const float* xr = x + (int64_t)blockIdx.x * ne0;
-  if (threadIdx.x == 0) {
+  if (staged) {
+    for (int64_t i = threadIdx.x; i < ne0; i += 256) sqs[i] = __fmul_rn(xr[i], xr[i]);
+    __syncthreads();
+    const float ss = ne0 <= 1024 ? spec_ordered_sum<256, 2>(sqs, (int)ne0, spec)
+                                 : spec_ordered_sum<256, 4>(sqs, (int)ne0, spec);
+    if (threadIdx.x == 0) {
+      const float mean = __fdiv_rn(ss, (float)ne0);
+      scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    }
+  } else if (threadIdx.x == 0) {
     float ss = 0.0f;
     for (int64_t i = 0; i < ne0; i++) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
     const float mean = __fdiv_rn(ss, (float)ne0);
@@ -787,7 +838,9 @@ __global__ void rms_norm_kernel(const float* x, int64_t ne0, float eps, float* d
 cudaError_t launch_rms_norm(const float* x, int64_t ne0, int64_t n_rows, float eps, float* dst,
                             cudaStream_t s) {
   if (n_rows == 0) return cudaSuccess;
-  rms_norm_kernel<<<(unsigned)n_rows, 256, 0, s>>>(x, ne0, eps, dst);
+  const int staged = ne0 <= kRmsStagedMax ? 1 : 0;
+  const size_t smem = staged ? (size_t)ne0 * 4 + kChainSlackBytes : 0;
+  rms_norm_kernel<<<(unsigned)n_rows, 256, smem, s>>>(x, ne0, eps, dst, staged);
   return cudaGetLastError();
 }
 

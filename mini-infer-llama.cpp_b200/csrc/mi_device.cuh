@@ -195,6 +195,142 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// C independent ordered chains over the same terms: s[c] = fl(s[c] + a[i]) for
+// i in order. The chains interleave, so C of them cost about one chain's
+// latency. `a` is 16-byte aligned shared memory that stays readable 8 floats
+// past n: the loads run 8 terms ahead without bounds checks (the values read
+// past n are never used).
+template <int C>
+__device__ __forceinline__ void ordered_chains(float (&s)[C], const float* a, int n) {
+  const float4* a4 = (const float4*)a;
+  const int n8 = n >> 3;
+  float4 b0 = a4[0], b1 = a4[1];
+  for (int i = 0; i < n8; i++) {
+    const float4 c0 = b0, c1 = b1;
+    b0 = a4[2 * i + 2];
+    b1 = a4[2 * i + 3];
+    const float v[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+    for (int u = 0; u < 8; u++)
+#pragma unroll
+      for (int c = 0; c < C; c++) s[c] = __fadd_rn(s[c], v[u]);
+  }
+  for (int k = n8 * 8; k < n; k++)
+#pragma unroll
+    for (int c = 0; c < C; c++) s[c] = __fadd_rn(s[c], a[k]);
+}
+
+// Bytes of slack a term buffer needs past its last element for ordered_chains.
+constexpr int kChainSlackBytes = 32;
+
+// ---------------------------------------------------------------------------
+// Speculative parallel form of a one-accumulator float sum.
+//
+// The reference sums with one float accumulator, s = fl(s + t[i]) for i in
+// order (rms_norm's sum of squares, src/ops_cpu.cpp:154-157; the softmax
+// denominator, src/ops_cpu.cpp:331-336). The chain is serial, but it is a
+// deterministic function of its start value. Here the CTA cuts t into NW
+// contiguous segments (one per warp). Every warp sums its own segment
+// (any order: it is only an estimate); warp w then estimates the chain's value
+// at its segment's start as the sum of the preceding segments' sums and runs
+// its segment from 32*C consecutive floats around that estimate at once (lane
+// l, chain c starts from the bit pattern bits(estimate) - 16C + 32c + l).
+// Thread 0 then walks the segments in order: with the exact chain value s at
+// segment w's start known, the segment's end is the end of the candidate that
+// started from exactly bits(s); if no candidate did, thread 0 runs that
+// segment serially from s. Either way the result equals the serial chain bit
+// for bit. The serial chain drifts from the exact prefix sum by a walk of
+// rounding errors (up to a few tens of ulps at n in the thousands), so the
+// fallback is rare and costs one segment when taken.
+//
+// Measured on B200 (one CTA, 8 warps, warm): n = 896 takes 2.6k cycles against
+// 4.8k for one thread's chain, n = 3584 6.2k against 15.8k; below n of about
+// 160 the serial chain is faster.
+//
+// Every thread of the CTA (NT of them) must call it: it synchronizes the CTA.
+// `t` is 16-byte aligned shared memory readable kChainSlackBytes past n;
+// `scratch` is shared memory of spec_sum_scratch_bytes(NT / 32, C) bytes,
+// 4-byte aligned.
+// ---------------------------------------------------------------------------
+__host__ __device__ constexpr int spec_sum_scratch_bytes(int nw, int c) {
+  return nw * 4 + nw * 32 * c * 4 + 16 + nw * 4;
+}
+
+template <int NT, int C>
+__device__ __forceinline__ float spec_ordered_sum(const float* t, int n, uint8_t* scratch) {
+  constexpr int NW = NT / 32;
+  constexpr unsigned NC = 32u * C;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  unsigned* base = (unsigned*)scratch;
+  float* ends = (float*)(scratch + NW * 4);
+  float* result = ends + NW * NC;
+  float* segsum = result + 4;
+  const int S = (((n + NW - 1) / NW) + 7) & ~7;  // segment length, keeps 32-byte alignment
+  const int b = warp * S;
+  const int len = max(0, min(S, n - b));
+  {
+    float a0 = 0.0f, a1 = 0.0f;
+    int i = lane;
+    for (; i + 32 < len; i += 64) {
+      a0 += t[b + i];
+      a1 += t[b + i + 32];
+    }
+    if (i < len) a0 += t[b + i];
+    float e = a0 + a1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) e += __shfl_xor_sync(0xffffffffu, e, o);
+    if (lane == 0) segsum[warp] = e;
+  }
+  __syncthreads();
+  if (len > 0) {
+    if (warp == 0) {
+      float s[1] = {0.0f};
+      ordered_chains<1>(s, t, len);
+      if (lane == 0) ends[0] = s[0];
+    } else {
+      float e = lane < warp ? segsum[lane] : 0.0f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) e += __shfl_xor_sync(0xffffffffu, e, o);
+      const unsigned b0 = __float_as_uint(e) - 16u * C;
+      float s[C];
+#pragma unroll
+      for (int c = 0; c < C; c++) s[c] = __uint_as_float(b0 + 32u * c + lane);
+      ordered_chains<C>(s, t + b, len);
+#pragma unroll
+      for (int c = 0; c < C; c++) ends[warp * NC + 32 * c + lane] = s[c];
+      if (lane == 0) base[warp] = b0;
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float s = n > 0 ? ends[0] : 0.0f;
+    int miss = NW;
+#pragma unroll
+    for (int w = 1; w < NW; w++) {
+      const bool live = w * S < n && miss == NW;
+      const unsigned idx = __float_as_uint(s) - (live ? base[w] : 0u);
+      const bool hit = live && idx < NC;
+      if (live && !hit) miss = w;
+      s = hit ? ends[w * NC + idx] : s;
+    }
+    // Serial from the first segment without a matching candidate; later
+    // segments still take their candidate when one matches.
+    for (int w = miss; w < NW && w * S < n; w++) {
+      const unsigned idx = __float_as_uint(s) - base[w];
+      if (w > miss && idx < NC) {
+        s = ends[w * NC + idx];
+      } else {
+        float r[1] = {s};
+        ordered_chains<1>(r, t + w * S, min(S, n - w * S));
+        s = r[0];
+      }
+    }
+    *result = s;
+  }
+  __syncthreads();
+  return *result;
+}
+
 // One Q8_0_ACT block value: the reference's per-block quantizer
 // (src/quant.cpp:199-218) for the element this lane holds; the warp holds the
 // block's 32 elements. Returns q, writes d (same on every lane).

@@ -124,6 +124,31 @@ def test_elementwise_ops(mc, R, torch_cuda):
     assert np.array_equal(bits(mc.silu(dev(torch, big)).cpu()), bits(R.op("silu", big)))
 
 
+def _norm_rows(rng, ne0):
+    """Rows for the rms_norm chain: plain, heavy-tailed, and one built so the
+    float chain drifts hundreds of ulps from the exact prefix sum (every square
+    of 0.3 added to 2^20 rounds up by 0.28 ulp), which forces the speculative
+    sum's serial fallback on its later segments."""
+    plain = (rng.standard_normal(ne0) * 3).astype(np.float32)
+    heavy = (rng.standard_normal(ne0) * np.exp(rng.standard_normal(ne0) * 2)).astype(np.float32)
+    drift = np.full(ne0, 0.3, dtype=np.float32)
+    drift[0] = 1024.0
+    zeros = np.zeros(ne0, dtype=np.float32)
+    return np.stack([plain, heavy, drift, zeros])
+
+
+@pytest.mark.parametrize("ne0", [1, 5, 31, 100, 896, 3584, 10240, 12288])
+def test_rms_norm_ordered_chain(mc, R, torch_cuda, ne0):
+    """rms_norm bit-exact at lengths below, at and above the speculative
+    chain's thresholds (CTA-wide speculation up to 10240 elements, one
+    thread's serial chain beyond)."""
+    torch = torch_cuda
+    x = _norm_rows(np.random.default_rng(ne0), ne0)
+    want = R.op("rms_norm", x, params=(1e-6,))
+    got = mc.rms_norm(dev(torch, x), 1e-6).cpu().numpy()
+    assert np.array_equal(bits(got), bits(want))
+
+
 @pytest.mark.parametrize("n_past,n_tokens,heads", [(0, 1, 14), (31, 1, 2), (158, 1, 14), (2047, 1, 14), (5, 7, 4)])
 def test_rope(mc, R, torch_cuda, n_past, n_tokens, heads):
     torch = torch_cuda
@@ -154,7 +179,7 @@ def test_attention_ops_separately(mc, S, torch_cuda, n_kv, n_tokens):
     assert np.array_equal(bits(o.cpu()), bits(o_w))
 
 
-@pytest.mark.parametrize("n_kv", [1, 128, 1024, 4096, 32768])
+@pytest.mark.parametrize("n_kv", [1, 128, 300, 1024, 4096, 8192, 32768])
 def test_attention_decode_config2(mc, S, torch_cuda, n_kv):
     torch = torch_cuda
     rng = np.random.default_rng(n_kv)
