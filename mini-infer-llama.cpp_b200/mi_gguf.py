@@ -23,6 +23,7 @@ import dataclasses
 import mmap
 import os
 import struct
+import subprocess
 
 import numpy as np
 
@@ -133,10 +134,8 @@ def _nbytes(typ: int, ne) -> int:
     return n * 4 if typ == GGML_F32 else n * 2 if typ == GGML_F16 else n // 32 * 34
 
 
-def write_qwen2_gguf(path: str, shape: Qwen2Shape, seed: int, std: float = 0.02,
-                     alignment: int = 32, chunk_rows: int = 8192) -> None:
-    """Write a random-init Q8_0 Qwen2 GGUF v3 file (deterministic in `seed`)."""
-    rng = np.random.Generator(np.random.PCG64(seed))
+def _header(shape: Qwen2Shape, alignment: int):
+    """GGUF v3 header bytes (padded to `alignment`) and [(name, type, ne, data offset)]."""
     plan = _tensor_plan(shape)
     kvs = [
         _kv("general.architecture", T_STR, "qwen2"),
@@ -154,19 +153,29 @@ def write_qwen2_gguf(path: str, shape: Qwen2Shape, seed: int, std: float = 0.02,
         _kv("tokenizer.ggml.tokens", T_ARR, (T_STR, [f"t{i}" for i in range(shape.n_vocab)])),
         _kv("tokenizer.ggml.token_type", T_ARR, (T_I32, [1] * shape.n_vocab)),
     ]
-    infos, offset = [], 0
+    infos, offsets, offset = [], [], 0
     for name, typ, ne in plan:
         infos.append(_str(name) + struct.pack("<I", len(ne)) + struct.pack(f"<{len(ne)}Q", *ne)
                      + struct.pack("<IQ", typ, offset))
+        offsets.append(offset)
         offset += _nbytes(typ, ne)
         offset = (offset + alignment - 1) // alignment * alignment
     header = GGUF_MAGIC + struct.pack("<IQQ", 3, len(plan), len(kvs)) + b"".join(kvs) + b"".join(infos)
-    pad = (-len(header)) % alignment
+    header += b"\0" * ((-len(header)) % alignment)
+    return header, [(n, t, ne, o) for (n, t, ne), o in zip(plan, offsets)], offset
+
+
+def write_qwen2_gguf(path: str, shape: Qwen2Shape, seed: int, std: float = 0.02,
+                     alignment: int = 32, chunk_rows: int = 8192) -> None:
+    """Write a random-init Q8_0 Qwen2 GGUF v3 file (deterministic in `seed`):
+    numpy PCG64 stream, norm weights 1.0, every other value N(0, std)."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    header, plan, _ = _header(shape, alignment)
     tmp = path + ".tmp"
     with open(tmp, "wb") as f:
-        f.write(header + b"\0" * pad)
+        f.write(header)
         written = 0
-        for name, typ, ne in plan:
+        for name, typ, ne, _off in plan:
             if typ == GGML_F32:
                 if name.endswith("norm.weight"):
                     data = np.ones(ne, dtype=np.float32)
@@ -186,13 +195,44 @@ def write_qwen2_gguf(path: str, shape: Qwen2Shape, seed: int, std: float = 0.02,
     os.replace(tmp, path)
 
 
-def ensure_qwen2_gguf(path: str, shape: Qwen2Shape, seed: int) -> str:
-    """Write the model once; later calls reuse the file if it is complete."""
+GEN_BIN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "mi_gguf_gen")
+
+
+def write_qwen2_gguf_fast(path: str, shape: Qwen2Shape, seed: int, std: float = 0.02,
+                          alignment: int = 32, threads: int | None = None) -> None:
+    """The same file layout as write_qwen2_gguf, with the tensor data filled by
+    the multithreaded lib/mi_gguf_gen (its own seeded per-row streams, so the
+    values differ from the numpy writer's; the bytes do not depend on the
+    thread count). A 7B-shape file takes seconds instead of tens of minutes."""
+    if not os.path.exists(GEN_BIN):
+        raise FileNotFoundError(f"{GEN_BIN} is missing: run __graft_entry__.build()")
+    header, plan, data_bytes = _header(shape, alignment)
+    tmp = path + ".tmp"
+    with open(tmp, "wb") as f:
+        f.write(header)
+        f.truncate(len(header) + data_bytes)
+    plan_path = tmp + ".plan"
+    with open(plan_path, "w") as f:
+        for i, (name, typ, ne, off) in enumerate(plan):
+            ne0, ne1 = (ne[0], ne[1]) if len(ne) == 2 else (ne[0], 1)
+            ones = 1 if name.endswith("norm.weight") else 0
+            f.write(f"{i} {typ} {ne0} {ne1} {len(header) + off} {ones}\n")
+    n = threads or os.cpu_count() or 1
+    try:
+        subprocess.run([GEN_BIN, tmp, plan_path, str(seed), repr(float(std)), str(n)], check=True)
+    finally:
+        os.remove(plan_path)
+    os.replace(tmp, path)
+
+
+def ensure_qwen2_gguf(path: str, shape: Qwen2Shape, seed: int, fast: bool = False) -> str:
+    """Write the model once; later calls reuse the file if it is complete.
+    fast=True uses write_qwen2_gguf_fast (a different, equally seeded file)."""
     if not os.path.exists(path):
         d = os.path.dirname(path)
         if d:
             os.makedirs(d, exist_ok=True)
-        write_qwen2_gguf(path, shape, seed)
+        (write_qwen2_gguf_fast if fast else write_qwen2_gguf)(path, shape, seed)
     return path
 
 
