@@ -195,6 +195,22 @@ typedef struct {
  * Q8_0 projection/embedding weights, F32 norms/biases), uploads every weight
  * to HBM once on `device`, and keeps nothing mapped afterwards. */
 int mi_cuda_qwen2_model_load(const char* gguf_path, int device, mi_cuda_model** out);
+
+/* Tensor parallelism over the GPUs of one node, one process per GPU
+ * (world <= 8). No reference counterpart: the reference is one process on one
+ * CPU. Each rank uploads its rows of every projection (stacked QKV, O, the
+ * FFN in whole 32-element activation blocks, down, LM head); norms, RoPE and
+ * attention are replicated. Row-sharding keeps every output row's arithmetic
+ * that of the unsharded GEMV (ref src/ops_cpu.cpp:226-237), so results are
+ * bit-identical to world == 1. */
+int mi_cuda_qwen2_model_load_shard(const char* gguf_path, int device, int rank, int world,
+                                   mi_cuda_model** out);
+/* The split used for every matrix: rank r owns units [first, first + count)
+ * of n_units (8-row groups; FFN activation blocks). Host-only arithmetic. */
+int mi_cuda_tp_shard_range(int64_t n_units, int rank, int world, int64_t* first, int64_t* count);
+/* Bytes of one exchange handle (a CUDA IPC memory handle). */
+int32_t mi_cuda_ipc_handle_bytes(void);
+
 void mi_cuda_qwen2_model_free(mi_cuda_model* model);
 int mi_cuda_qwen2_get_hparams(const mi_cuda_model* model, mi_cuda_qwen2_hparams* out);
 /* Bytes of weights resident in HBM. */
@@ -205,6 +221,16 @@ size_t mi_cuda_qwen2_weight_bytes(const mi_cuda_model* model);
  * captured decode-step graphs. */
 int mi_cuda_kv_cache_init(mi_cuda_model* model, int32_t n_ctx, mi_cuda_kv_cache** out);
 void mi_cuda_kv_cache_free(mi_cuda_kv_cache* kv);
+
+/* KV cache of a sharded model: mi_cuda_kv_cache_init allocates its exchange
+ * buffer (words that every rank's GEMV epilogues store into over NVLink) but
+ * captures no step graph. Send this rank's handle to every rank, then call
+ * mi_cuda_tp_connect with all ranks' handles concatenated in rank order: it
+ * maps the peers' buffers and captures the graphs. From then on every rank
+ * must issue the same sequence of steps; a rank that stops makes the others'
+ * bounded device waits expire (MI_CUDA_ERR_TIMEOUT). */
+int mi_cuda_tp_exchange_handle(mi_cuda_kv_cache* kv, void* handle_out);
+int mi_cuda_tp_connect(mi_cuda_kv_cache* kv, const void* handles);
 
 /* mi_qwen2_forward (ref src/model_qwen2.cpp:609-688): runs n_tokens tokens
  * starting at position n_past, writes their K/V rows, and copies logits to

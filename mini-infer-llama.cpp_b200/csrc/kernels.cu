@@ -70,7 +70,7 @@ __host__ __device__ inline GemvSmem gemv_smem(int64_t K, int32_t rows_per_cta, i
 // the embedding lookup and rms_norm), the warps consume the stages, and the
 // epilogue applies bias / residual / SiLU*up / argmax.
 // ---------------------------------------------------------------------------
-template <int NT, int TPR>
+template <int NT, int TPR, bool TP>
 __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int NW = NT / 32;
@@ -117,7 +117,17 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
   trace_mark(p.trace, p.trace_slot, 1);
 
   // ---- prologue: the quantized activation in shared memory ----
-  if (p.pro == PRO_ACT) {
+  if (TP && p.pro == PRO_ACT && p.act_ll) {
+    // Q8_0_ACT blocks as exchange words: word 0 the scale, 1..8 the quants.
+    const uint32_t tag = *p.epoch;
+    bool dead = false;
+    for (int e = tid; e < nb * 9; e += NT) {
+      const int b = e / 9, w = e - b * 9;
+      const uint32_t v = ll_wait(p.act_ll + e, tag, p.err, dead);
+      if (w == 0) ad[b] = __uint_as_float(v);
+      else ((uint32_t*)(aq + 32 * b))[w - 1] = v;
+    }
+  } else if (p.pro == PRO_ACT) {
     for (int b = tid; b < nb; b += NT) {
       const uint8_t* src = p.act + (size_t)b * 36;
       ad[b] = *(const float*)src;
@@ -143,6 +153,10 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
         xs[k] = v;
         if (blockIdx.x == 0) p.x_out[k] = v;
       }
+    } else if (TP && p.x_ll) {
+      const uint32_t tag = *p.epoch;
+      bool dead = false;
+      for (int64_t k = tid; k < K; k += NT) xs[k] = __uint_as_float(ll_wait(p.x_ll + k, tag, p.err, dead));
     } else if (p.pro >= PRO_NORM_QUANT || p.stage_x) {
       // All loads of x in flight at once (K is a multiple of 32).
       const float4* x4 = (const float4*)p.x;
@@ -270,9 +284,24 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
       const float v = __fmul_rn(silu_exact(res[lr], p.et), res[lr + 4]);
       float d;
       const int8_t q = quantize_lane(v, &d);
-      uint8_t* blk = p.act_out + (size_t)(r0 >> 6) * 36;
-      ((int8_t*)blk)[4 + lane] = q;
-      if (lane == 0) *(float*)blk = d;
+      if (TP && p.out_ll[0]) {
+        // the block as 9 exchange words, into every rank's copy
+        const uint32_t b0 = (uint8_t)q;
+        const uint32_t b1 = __shfl_down_sync(FULL, b0, 1), b2 = __shfl_down_sync(FULL, b0, 2),
+                       b3 = __shfl_down_sync(FULL, b0, 3);
+        const uint32_t word = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        const int64_t blk = (p.row0 + r0) >> 6;
+        const uint32_t tag = *p.epoch;
+        for (int rk = 0; rk < p.n_ranks; rk++) {
+          uint64_t* dst = p.out_ll[rk] + blk * 9;
+          if (lane == 0) ll_store(dst, __float_as_uint(d), tag);
+          if ((lane & 3) == 0) ll_store(dst + 1 + (lane >> 2), word, tag);
+        }
+      } else {
+        uint8_t* blk = p.act_out + (size_t)(r0 >> 6) * 36;
+        ((int8_t*)blk)[4 + lane] = q;
+        if (lane == 0) *(float*)blk = d;
+      }
     }
     return;
   }
@@ -282,6 +311,25 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
       if ((r & 7) >= 4 || r >= p.N) continue;
       const float g = res[lr], u = res[lr + 4];
       p.out[(r >> 3) * 4 + (r & 7)] = __fmul_rn(silu_exact(g, p.et), u);  // mul(silu(gate), up)
+    }
+    return;
+  }
+  if (TP && p.epi != EPI_ARGMAX && p.out_ll[0]) {
+    // rows [row0 + r0, ...) of the full vector, into every rank's copy
+    const uint32_t tag = *p.epoch;
+    bool dead = false;
+    for (int lr = tid; lr < nrows; lr += NT) {
+      const int64_t r = r0 + lr;
+      if (r >= p.N) continue;
+      const int64_t g = p.row0 + r;
+      float v = res[lr];
+      if (p.epi == EPI_BIAS) {
+        v = __fadd_rn(v, p.bias[r]);
+      } else if (p.epi == EPI_RESID) {
+        const float rv = p.resid_ll ? __uint_as_float(ll_wait(p.resid_ll + g, tag, p.err, dead)) : p.resid[g];
+        v = __fadd_rn(rv, v);
+      }
+      for (int rk = 0; rk < p.n_ranks; rk++) ll_store(p.out_ll[rk] + g, __float_as_uint(v), tag);
     }
     return;
   }
@@ -308,7 +356,7 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
     p.out[r] = v;
     if (v > bv || bi == 0x7fffffff) {
       bv = v;
-      bi = (int32_t)r;
+      bi = (int32_t)(TP ? p.row0 + r : r);
     }
   }
   __shared__ float red_v[NW];
@@ -353,6 +401,26 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
         best = v;
         besti = i;
       }
+    }
+    if (TP && p.out_ll[0]) {
+      // This rank's winner to every rank; then the first maximum over the
+      // ranks, whose row ranges are in rank order.
+      const uint32_t tag = *p.epoch;
+      for (int rk = 0; rk < p.n_ranks; rk++) {
+        ll_store(p.out_ll[rk] + 2 * p.rank, __float_as_uint(best), tag);
+        ll_store(p.out_ll[rk] + 2 * p.rank + 1, (uint32_t)besti, tag);
+      }
+      const uint64_t* own = p.out_ll[p.rank];
+      bool dead = false;
+      for (int rk = 0; rk < p.n_ranks; rk++) {
+        const float v = __uint_as_float(ll_wait(own + 2 * rk, tag, p.err, dead));
+        const int32_t i = (int32_t)ll_wait(own + 2 * rk + 1, tag, p.err, dead);
+        if (rk == 0 || v > best || (v == best && i < besti)) {
+          best = v;
+          besti = i;
+        }
+      }
+      *p.epoch_rw = tag + 1u;
     }
     *p.next_token = besti;
     const int32_t pos = *p.pos_rw;
@@ -404,12 +472,12 @@ GemvPlan plan_gemv(int64_t k, int64_t n, int num_sms, int pro, int32_t rows_per_
 }
 
 namespace {
-template <int TPR>
+template <int TPR, bool TP>
 cudaError_t set_gemv_smem(int optin) {
   cudaFuncAttributes f{};
-  cudaError_t e = cudaFuncGetAttributes(&f, gemv_q8_kernel<256, TPR>);
+  cudaError_t e = cudaFuncGetAttributes(&f, gemv_q8_kernel<256, TPR, TP>);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(gemv_q8_kernel<256, TPR>,
+    e = cudaFuncSetAttribute(gemv_q8_kernel<256, TPR, TP>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              optin - (int)f.sharedSizeBytes);
   return e;
@@ -420,8 +488,10 @@ cudaError_t prepare_kernels() {
   int dev = 0, optin = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  if (e == cudaSuccess) e = set_gemv_smem<8>(optin);
-  if (e == cudaSuccess) e = set_gemv_smem<2>(optin);
+  if (e == cudaSuccess) e = set_gemv_smem<8, false>(optin);
+  if (e == cudaSuccess) e = set_gemv_smem<2, false>(optin);
+  if (e == cudaSuccess) e = set_gemv_smem<8, true>(optin);
+  if (e == cudaSuccess) e = set_gemv_smem<2, true>(optin);
   if (e == cudaSuccess) e = prepare_attn_kernels(optin);
   return e;
 }
@@ -430,7 +500,8 @@ cudaError_t prepare_kernels() {
 // mapping: consecutive GEMVs of a step then run the same code, which is still
 // in the SMs' instruction caches (measured: per-variant instantiations made
 // the decode step about 2.5% slower).
-cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& plan, cudaStream_t s, bool pdl) {
+cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& plan, cudaStream_t s, bool pdl,
+                        bool tp) {
   GemvParams q = p;
   q.rows_per_cta = plan.rows_per_cta;
   q.stage_rows = plan.stage_rows;
@@ -446,8 +517,11 @@ cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& plan, cudaStream_t 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (plan.tpr == 2) return cudaLaunchKernelEx(&cfg, gemv_q8_kernel<256, 2>, q);
-  return cudaLaunchKernelEx(&cfg, gemv_q8_kernel<256, 8>, q);
+  if (tp)
+    return plan.tpr == 2 ? cudaLaunchKernelEx(&cfg, gemv_q8_kernel<256, 2, true>, q)
+                         : cudaLaunchKernelEx(&cfg, gemv_q8_kernel<256, 8, true>, q);
+  if (plan.tpr == 2) return cudaLaunchKernelEx(&cfg, gemv_q8_kernel<256, 2, false>, q);
+  return cudaLaunchKernelEx(&cfg, gemv_q8_kernel<256, 8, false>, q);
 }
 
 // ---------------------------------------------------------------------------
@@ -465,7 +539,7 @@ cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& plan, cudaStream_t 
 // Every chain keeps the reference's order: d ascending in QK, the softmax
 // denominator over positions in order, t ascending in KV.
 // ---------------------------------------------------------------------------
-template <bool EXEC, bool SPEC>
+template <bool EXEC, bool SPEC, bool TP>
 __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnParams p) {
   extern __shared__ __align__(16) float sm[];
   __shared__ float qr[256], kr[256], vr[256];
@@ -530,18 +604,35 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnParams p) {
   trace_mark(p.trace, p.trace_slot, 1);
   if (EXEC) {
     const float2* cs = p.rope_cs + (size_t)n_past * half;
-    const float* q = p.qkv + (size_t)h * D;
-    const float* k = p.qkv + (size_t)p.n_head * D + (size_t)kvh * D;
-    const float* v = p.qkv + (size_t)(p.n_head + HKV) * D + (size_t)kvh * D;
+    const size_t qo = (size_t)h * D, ko = (size_t)p.n_head * D + (size_t)kvh * D,
+                 vo = (size_t)(p.n_head + HKV) * D + (size_t)kvh * D;
+    const float* q = p.qkv + qo;
+    const float* k = p.qkv + ko;
+    const float* v = p.qkv + vo;
+    uint32_t tag = 0u;
+    bool dead = false;
+    if (TP) tag = *p.epoch;
     for (int i = tid; i < half; i += NT) {
       const float2 c = cs[i];
-      const float q0 = q[i], q1 = q[i + half], k0 = k[i], k1 = k[i + half];
+      float q0, q1, k0, k1;
+      if (TP) {
+        q0 = __uint_as_float(ll_wait(p.qkv_ll + qo + i, tag, p.err, dead));
+        q1 = __uint_as_float(ll_wait(p.qkv_ll + qo + i + half, tag, p.err, dead));
+        k0 = __uint_as_float(ll_wait(p.qkv_ll + ko + i, tag, p.err, dead));
+        k1 = __uint_as_float(ll_wait(p.qkv_ll + ko + i + half, tag, p.err, dead));
+      } else {
+        q0 = q[i];
+        q1 = q[i + half];
+        k0 = k[i];
+        k1 = k[i + half];
+      }
       qr[i] = __fsub_rn(__fmul_rn(q0, c.x), __fmul_rn(q1, c.y));
       qr[i + half] = __fadd_rn(__fmul_rn(q0, c.y), __fmul_rn(q1, c.x));
       kr[i] = __fsub_rn(__fmul_rn(k0, c.x), __fmul_rn(k1, c.y));
       kr[i + half] = __fadd_rn(__fmul_rn(k0, c.y), __fmul_rn(k1, c.x));
     }
-    for (int i = tid; i < D; i += NT) vr[i] = v[i];
+    for (int i = tid; i < D; i += NT)
+      vr[i] = TP ? __uint_as_float(ll_wait(p.qkv_ll + vo + i, tag, p.err, dead)) : v[i];
     __syncthreads();
     if (h % (p.n_head / HKV) == 0) {
       float* kd = p.cache_k + ((size_t)n_past * HKV + kvh) * D;
@@ -655,12 +746,12 @@ constexpr int kScoresSmemMax = 8192;         // scores kept on chip up to this m
 }  // namespace
 
 namespace {
-template <bool EXEC, bool SPEC>
+template <bool EXEC, bool SPEC, bool TP>
 cudaError_t set_attn_smem(int optin) {
   cudaFuncAttributes f{};
-  cudaError_t e = cudaFuncGetAttributes(&f, attn_decode_kernel<EXEC, SPEC>);
+  cudaError_t e = cudaFuncGetAttributes(&f, attn_decode_kernel<EXEC, SPEC, TP>);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(attn_decode_kernel<EXEC, SPEC>,
+    e = cudaFuncSetAttribute(attn_decode_kernel<EXEC, SPEC, TP>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              optin - (int)f.sharedSizeBytes);
   return e;
@@ -668,13 +759,15 @@ cudaError_t set_attn_smem(int optin) {
 }  // namespace
 
 cudaError_t prepare_attn_kernels(int optin) {
-  cudaError_t e = set_attn_smem<true, false>(optin);
-  if (e == cudaSuccess) e = set_attn_smem<false, false>(optin);
-  if (e == cudaSuccess) e = set_attn_smem<false, true>(optin);
+  cudaError_t e = set_attn_smem<true, false, false>(optin);
+  if (e == cudaSuccess) e = set_attn_smem<true, false, true>(optin);
+  if (e == cudaSuccess) e = set_attn_smem<false, false, false>(optin);
+  if (e == cudaSuccess) e = set_attn_smem<false, true, false>(optin);
   return e;
 }
 
-cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t s, bool pdl) {
+cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t s, bool pdl,
+                               bool tp) {
   AttnParams q = p;
   // Positions the scores may need: n_ctx in executor mode, n_kv otherwise.
   const int64_t max_kv = exec_mode ? p.n_ctx : p.n_kv_fixed;
@@ -695,10 +788,11 @@ cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (exec_mode) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<true, false>, q);
+  if (exec_mode && tp) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<true, false, true>, q);
+  if (exec_mode) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<true, false, false>, q);
   if (q.scores_in_smem && p.n_kv_fixed >= kSpecSumMin)
-    return cudaLaunchKernelEx(&cfg, attn_decode_kernel<false, true>, q);
-  return cudaLaunchKernelEx(&cfg, attn_decode_kernel<false, false>, q);
+    return cudaLaunchKernelEx(&cfg, attn_decode_kernel<false, true, false>, q);
+  return cudaLaunchKernelEx(&cfg, attn_decode_kernel<false, false, false>, q);
 }
 
 // ---------------------------------------------------------------------------
@@ -1088,13 +1182,16 @@ cudaError_t launch_argmax(const float* x, int64_t n, float* part_val, int32_t* p
   return cudaGetLastError();
 }
 
-__global__ void advance_kernel(int32_t* pos) {
+__global__ void advance_kernel(int32_t* pos, uint32_t* epoch) {
   pdl_trigger();
   pdl_wait();
-  if (threadIdx.x == 0) *pos += 1;
+  if (threadIdx.x == 0) {
+    *pos += 1;
+    if (epoch) *epoch += 1u;
+  }
 }
 
-cudaError_t launch_advance(int32_t* pos, cudaStream_t s, bool pdl) {
+cudaError_t launch_advance(int32_t* pos, cudaStream_t s, bool pdl, uint32_t* epoch) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1);
   cfg.blockDim = dim3(32);
@@ -1104,7 +1201,7 @@ cudaError_t launch_advance(int32_t* pos, cudaStream_t s, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, advance_kernel, pos);
+  return cudaLaunchKernelEx(&cfg, advance_kernel, pos, epoch);
 }
 
 __global__ void set_pos_kernel(int32_t* pos, int32_t value) {

@@ -94,6 +94,39 @@ __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-parallel exchange words: value bits | tag << 32, written with one
+// 64-bit store (single-copy atomic), so a reader that sees the step's tag
+// sees that step's value. Peer buffers are written through peer pointers
+// (NVLink); readers poll their own copy with volatile loads.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t ll_load(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void ll_store(uint64_t* p, uint32_t bits, uint32_t tag) {
+  const uint64_t v = ((uint64_t)tag << 32) | bits;
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// The value bits of *p once it carries `tag`. Bounded: after kSpinLimit polls
+// it records MI_CUDA_ERR_TIMEOUT in *err, sets `dead` (later waits of the
+// thread then return at once) and returns 0.
+__device__ __forceinline__ uint32_t ll_wait(const uint64_t* p, uint32_t tag, int32_t* err, bool& dead) {
+  uint64_t v = ll_load(p);
+  if ((uint32_t)(v >> 32) == tag) return (uint32_t)v;
+  if (dead) return 0u;
+  for (uint32_t it = 0; it < kSpinLimit; it++) {
+    v = ll_load(p);
+    if ((uint32_t)(v >> 32) == tag) return (uint32_t)v;
+  }
+  dead = true;
+  if (err) atomicExch(err, 5 /* MI_CUDA_ERR_TIMEOUT */);
+  return 0u;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

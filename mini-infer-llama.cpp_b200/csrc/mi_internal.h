@@ -36,6 +36,13 @@ enum GemvEpilogue : int32_t {
                           // quantized to Q8_0_ACT at act_out (the down GEMV's input)
 };
 
+// Tensor parallelism: ranks (one per GPU) exchange vectors through buffers of
+// 8-byte words, value bits | tag << 32, that producers store into every
+// rank's copy over NVLink (peer pointers). A consumer waits, bounded, until a
+// word carries the current step's tag; no separate flag or fence is needed
+// because each word is written by one 64-bit store.
+constexpr int kMaxRanks = 8;
+
 struct GemvParams {
   const uint8_t* w;
   int64_t K, N, n_pad;
@@ -70,6 +77,17 @@ struct GemvParams {
   int32_t* err;
   uint64_t* trace;     // optional step trace (4 stamps per kernel slot)
   int32_t trace_slot;
+  // Tensor parallelism (the TP kernel instantiation only): this GEMV computes
+  // rows [row0, row0 + N) of the full output (Q8_0_ACT blocks: row0 / 64 for
+  // the gate/up epilogue). _ll inputs are indexed by full-vector position.
+  int32_t n_ranks, rank;
+  int64_t row0;
+  const uint32_t* epoch;        // the step's tag
+  const uint64_t* x_ll;         // F32 input vector (PRO_QUANT / PRO_NORM_QUANT)
+  const uint64_t* act_ll;       // Q8_0_ACT input, 9 words per block (PRO_ACT)
+  const uint64_t* resid_ll;     // EPI_RESID residual
+  uint64_t* out_ll[kMaxRanks];  // every rank's copy of the output (EPI_ARGMAX: candidates)
+  uint32_t* epoch_rw;           // EPI_ARGMAX: advanced once the step's token is known
 };
 
 struct GemvPlan {
@@ -84,7 +102,8 @@ GemvPlan plan_gemv(int64_t k, int64_t n, int num_sms, int pro, int32_t rows_per_
 // Per-device kernel attributes (dynamic shared memory limit); called once per
 // device at context creation, outside any stream capture.
 cudaError_t prepare_kernels();
-cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& plan, cudaStream_t s, bool pdl);
+cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& plan, cudaStream_t s, bool pdl,
+                        bool tp = false);
 
 // ---------------------------------------------------------------------------
 // Decode attention (one query token per head)
@@ -109,8 +128,11 @@ struct AttnParams {
   int32_t scores_in_smem;  // set by the launcher
   uint64_t* trace;         // optional step trace (4 stamps per kernel slot)
   int32_t trace_slot;
+  const uint64_t* qkv_ll;  // tensor parallelism: q | k | v as exchange words (instead of qkv)
+  const uint32_t* epoch;
 };
-cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t s, bool pdl);
+cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t s, bool pdl,
+                               bool tp = false);
 
 // ---------------------------------------------------------------------------
 // Small ops
@@ -146,7 +168,8 @@ cudaError_t launch_attn_kqv(const float* p, const float* v, int64_t hd, int64_t 
                             int64_t n_kv, int64_t nt, float* dst, cudaStream_t s);
 cudaError_t launch_argmax(const float* x, int64_t n, float* part_val, int32_t* part_idx,
                           uint32_t* counter, int32_t* out, cudaStream_t s);
-cudaError_t launch_advance(int32_t* pos, cudaStream_t s, bool pdl);
+// pos += 1 (and *epoch += 1 when given) after the preceding kernel.
+cudaError_t launch_advance(int32_t* pos, cudaStream_t s, bool pdl, uint32_t* epoch = nullptr);
 cudaError_t launch_set_pos(int32_t* pos, int32_t value, cudaStream_t s);
 
 // ---------------------------------------------------------------------------

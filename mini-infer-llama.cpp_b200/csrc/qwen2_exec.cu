@@ -74,10 +74,22 @@ size_t a256(size_t v) { return (v + 255) / 256 * 256; }
 
 }  // namespace
 
+// Rows of every GEMV this rank computes (tensor parallelism; the full
+// matrices when world == 1). Units: 8 rows, except the FFN whose unit is one
+// 32-element block of its activation (64 packed gate/up rows).
+struct Shard {
+  int64_t qkv0 = 0, nqkv = 0;  // rows of the stacked [q | k | v] projection
+  int64_t o0 = 0, no = 0;      // rows of n_embd outputs (O and down projections)
+  int64_t ff0 = 0, nff = 0;    // FFN activation blocks
+  int64_t v0 = 0, nv = 0;      // vocabulary rows of the LM head
+};
+
 struct mi_cuda_model {
   int device = 0;
   DeviceCtx* ctx = nullptr;
   mi_cuda_qwen2_hparams hp{};
+  int rank = 0, world = 1;
+  Shard sh;
   bool tied = true;
   uint8_t* buf = nullptr;
   size_t bytes = 0;
@@ -110,21 +122,36 @@ struct mi_cuda_kv_cache {
   uint64_t* trace = nullptr;  // [slot][4] globaltimer stamps of the last step
   int32_t trace_slots = 0;
   bool pdl = true;
+  // Tensor parallelism: exchange words (see mi_internal.h) in one allocation
+  // that every peer maps; offsets in words. epoch = the current step's tag.
+  uint64_t* xbuf = nullptr;
+  size_t xwords = 0;
+  size_t x_qkv = 0, x_h1 = 0, x_act = 0, x_h2 = 0, x_cand = 0;
+  uint64_t* peer[kMaxRanks] = {};
+  bool connected = false;
+  uint32_t* epoch = nullptr;
   GemvPlan plan_qkv{}, plan_o{}, plan_gu{}, plan_down{}, plan_head{};
   cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
 };
 
 namespace {
 
-// Uploads n GGUF Q8_0 rows of `t` into packed matrix `dst` (rows mapped by
-// row_offset / group_stride, see launch_pack_q8_0) through pinned staging.
-int upload_q8(const GgufTensor* t, const Mat& dst, int64_t row_offset, int64_t gstride,
-              uint8_t* d_stage, uint8_t* h_stage, size_t stage_bytes, cudaStream_t s) {
-  const int64_t K = t->ne[0], n = t->ne[1];
+// Uploads GGUF Q8_0 rows [s0, s1) of `t` into packed matrix `dst` through
+// pinned staging; source row i lands on packed row (i/4)*gstride + row_offset
+// + i%4 (see launch_pack_q8_0), which the caller keeps inside dst.
+int upload_q8_rows(const GgufTensor* t, int64_t s0, int64_t s1, const Mat& dst, int64_t row_offset,
+                   int64_t gstride, uint8_t* d_stage, uint8_t* h_stage, size_t stage_bytes,
+                   cudaStream_t s) {
+  const int64_t K = t->ne[0];
+  if (s1 <= s0) return MI_CUDA_OK;
+  const int64_t lo = (s0 >> 2) * gstride + row_offset + (s0 & 3);
+  const int64_t hi = ((s1 - 1) >> 2) * gstride + row_offset + ((s1 - 1) & 3);
+  if (s0 < 0 || s1 > t->ne[1] || lo < 0 || hi >= dst.npad || row_offset % 4 != 0)
+    return fail(MI_CUDA_ERR_ARG, "internal: packed row range outside its matrix");
   const size_t row = (size_t)(K / 32 * 34);
   const int64_t rows_per = std::max<int64_t>(4, (int64_t)(stage_bytes / row) / 4 * 4);
-  for (int64_t r0 = 0; r0 < n; r0 += rows_per) {
-    const int64_t rn = std::min(rows_per, n - r0);
+  for (int64_t r0 = s0; r0 < s1; r0 += rows_per) {
+    const int64_t rn = std::min(rows_per, s1 - r0);
     CK(cudaStreamSynchronize(s));
     std::memcpy(h_stage, t->data + (size_t)r0 * row, (size_t)rn * row);
     CK(cudaMemcpyAsync(d_stage, h_stage, (size_t)rn * row, cudaMemcpyHostToDevice, s));
@@ -133,18 +160,38 @@ int upload_q8(const GgufTensor* t, const Mat& dst, int64_t row_offset, int64_t g
   return MI_CUDA_OK;
 }
 
+int upload_q8(const GgufTensor* t, const Mat& dst, int64_t row_offset, int64_t gstride,
+              uint8_t* d_stage, uint8_t* h_stage, size_t stage_bytes, cudaStream_t s) {
+  return upload_q8_rows(t, 0, t->ne[1], dst, row_offset, gstride, d_stage, h_stage, stage_bytes, s);
+}
+
 int upload_f32(const GgufTensor* t, float* dst, cudaStream_t s) {
   CK(cudaMemcpyAsync(dst, t->data, t->nbytes, cudaMemcpyHostToDevice, s));
   CK(cudaStreamSynchronize(s));
   return MI_CUDA_OK;
 }
 
+// Elements [e0, e1) of an F32 tensor to dst.
+int upload_f32_range(const GgufTensor* t, int64_t e0, int64_t e1, float* dst, cudaStream_t s) {
+  if (e1 <= e0) return MI_CUDA_OK;
+  CK(cudaMemcpyAsync(dst, t->data + e0 * 4, (size_t)(e1 - e0) * 4, cudaMemcpyHostToDevice, s));
+  CK(cudaStreamSynchronize(s));
+  return MI_CUDA_OK;
+}
+
+void shard_range(int64_t units, int rank, int world, int64_t* first, int64_t* count) {
+  *first = units * rank / world;
+  *count = units * (rank + 1) / world - *first;
+}
+
 }  // namespace
 
-extern "C" {
+namespace {
 
-int mi_cuda_qwen2_model_load(const char* gguf_path, int device, mi_cuda_model** out) {
+int load_model(const char* gguf_path, int device, int rank, int world, mi_cuda_model** out) {
   if (!gguf_path || !out) return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_model_load: null argument");
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
+    return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_model_load_shard: rank / world out of range (world <= 8)");
   *out = nullptr;
   std::string err;
   DeviceCtx* ctx = device_ctx(device, &err);
@@ -209,12 +256,31 @@ int mi_cuda_qwen2_model_load(const char* gguf_path, int device, mi_cuda_model** 
   rc = need("output_norm.weight", kGgmlF32, E, 1, &tnorm);
     if (rc) return rc;
 
+  // This rank's rows of every GEMV (all rows when world == 1).
+  m->rank = rank;
+  m->world = world;
+  Shard& sh = m->sh;
+  shard_range((E + 2 * kvd) / 8, rank, world, &sh.qkv0, &sh.nqkv);
+  shard_range(E / 8, rank, world, &sh.o0, &sh.no);
+  shard_range(FF / 32, rank, world, &sh.ff0, &sh.nff);
+  shard_range((hp.n_vocab + 7) / 8, rank, world, &sh.v0, &sh.nv);
+  sh.qkv0 *= 8;
+  sh.nqkv *= 8;
+  sh.o0 *= 8;
+  sh.no *= 8;
+  sh.v0 *= 8;
+  sh.nv = std::min<int64_t>(sh.nv * 8, hp.n_vocab - sh.v0);
+  if (world > 1 && (sh.nqkv == 0 || sh.no == 0 || sh.nff == 0 || sh.nv <= 0))
+    return fail(MI_CUDA_ERR_ARG, "model too small for this many ranks");
+  // A sharded model keeps its own rows of the LM head (tied or not).
+  const bool own_head = !m->tied || world > 1;
+
   // One device allocation for every weight (256-byte aligned sub-buffers).
   size_t total = a256(packed_bytes(E, hp.n_vocab)) + a256(E * 4);
-  if (!m->tied) total += a256(packed_bytes(E, hp.n_vocab));
-  const size_t per_layer = a256(packed_bytes(E, E + 2 * kvd)) + a256((E + 2 * kvd) * 4) +
-                           a256(packed_bytes(E, E)) + a256(packed_bytes(E, 2 * FF)) +
-                           a256(packed_bytes(FF, E)) + 2 * a256(E * 4);
+  if (own_head) total += a256(packed_bytes(E, sh.nv));
+  const size_t per_layer = a256(packed_bytes(E, sh.nqkv)) + a256(sh.nqkv * 4) +
+                           a256(packed_bytes(E, sh.no)) + a256(packed_bytes(E, 64 * sh.nff)) +
+                           a256(packed_bytes(FF, sh.no)) + 2 * a256(E * 4);
   total += per_layer * (size_t)hp.n_layer;
   CK(cudaMalloc(&m->buf, total));
   m->bytes = total;
@@ -233,15 +299,15 @@ int mi_cuda_qwen2_model_load(const char* gguf_path, int device, mi_cuda_model** 
     return x;
   };
   m->embed = mat(E, hp.n_vocab);
-  m->lm_head = m->tied ? m->embed : mat(E, hp.n_vocab);
+  m->lm_head = own_head ? mat(E, sh.nv) : m->embed;
   m->output_norm = (float*)take(E * 4);
   m->layers.resize((size_t)hp.n_layer);
   for (auto& L : m->layers) {
-    L.qkv = mat(E, E + 2 * kvd);
-    L.bqkv = (float*)take((E + 2 * kvd) * 4);
-    L.o = mat(E, E);
-    L.gateup = mat(E, 2 * FF);
-    L.down = mat(FF, E);
+    L.qkv = mat(E, sh.nqkv);
+    L.bqkv = (float*)take(sh.nqkv * 4);
+    L.o = mat(E, sh.no);
+    L.gateup = mat(E, 64 * sh.nff);
+    L.down = mat(FF, sh.no);
     L.attn_norm = (float*)take(E * 4);
     L.ffn_norm = (float*)take(E * 4);
   }
@@ -265,8 +331,12 @@ int mi_cuda_qwen2_model_load(const char* gguf_path, int device, mi_cuda_model** 
     return fail(MI_CUDA_ERR_CUDA, "staging allocation failed");
   }
   rc = upload_q8(te, m->embed, 0, 4, d_stage, h_stage, stage, s);
-  if (!rc && !m->tied) rc = upload_q8(tout, m->lm_head, 0, 4, d_stage, h_stage, stage, s);
+  if (!rc && own_head)
+    rc = upload_q8_rows(m->tied ? te : tout, sh.v0, sh.v0 + sh.nv, m->lm_head, -sh.v0, 4, d_stage,
+                        h_stage, stage, s);
   if (!rc) rc = upload_f32(tnorm, m->output_norm, s);
+  const int64_t q0 = sh.qkv0, q1 = sh.qkv0 + sh.nqkv, r0 = sh.o0, r1 = sh.o0 + sh.no;
+  const int64_t a0 = 32 * sh.ff0, a1 = 32 * (sh.ff0 + sh.nff);
   for (int l = 0; !rc && l < hp.n_layer; l++) {
     Layer& L = m->layers[(size_t)l];
     const std::string b = "blk." + std::to_string(l) + ".";
@@ -295,30 +365,34 @@ int mi_cuda_qwen2_model_load(const char* gguf_path, int device, mi_cuda_model** 
     if (rc) break;
     rc = need(b + "ffn_down.weight", kGgmlQ8_0, FF, E, &wd);
     if (rc) break;
-    // Q | K | V stacked in one matrix; gate/up interleaved by groups of 4 rows.
-    rc = upload_q8(wq, L.qkv, 0, 4, d_stage, h_stage, stage, s);
+    // Q | K | V stacked in one matrix (this rank's rows [q0, q1) of it);
+    // gate/up interleaved by groups of 4 rows.
+    const int64_t qa = std::max<int64_t>(0, q0), qb = std::min<int64_t>(E, q1);
+    const int64_t ka = std::max<int64_t>(0, q0 - E), kb = std::min<int64_t>(kvd, q1 - E);
+    const int64_t va = std::max<int64_t>(0, q0 - E - kvd), vb = std::min<int64_t>(kvd, q1 - E - kvd);
+    rc = upload_q8_rows(wq, qa, qb, L.qkv, -q0, 4, d_stage, h_stage, stage, s);
     if (rc) break;
-    rc = upload_q8(wk, L.qkv, E, 4, d_stage, h_stage, stage, s);
+    rc = upload_q8_rows(wk, ka, kb, L.qkv, E - q0, 4, d_stage, h_stage, stage, s);
     if (rc) break;
-    rc = upload_q8(wv, L.qkv, E + kvd, 4, d_stage, h_stage, stage, s);
+    rc = upload_q8_rows(wv, va, vb, L.qkv, E + kvd - q0, 4, d_stage, h_stage, stage, s);
     if (rc) break;
-    rc = upload_q8(wo, L.o, 0, 4, d_stage, h_stage, stage, s);
+    rc = upload_q8_rows(wo, r0, r1, L.o, -r0, 4, d_stage, h_stage, stage, s);
     if (rc) break;
-    rc = upload_q8(wg, L.gateup, 0, 8, d_stage, h_stage, stage, s);
+    rc = upload_q8_rows(wg, a0, a1, L.gateup, -2 * a0, 8, d_stage, h_stage, stage, s);
     if (rc) break;
-    rc = upload_q8(wu, L.gateup, 4, 8, d_stage, h_stage, stage, s);
+    rc = upload_q8_rows(wu, a0, a1, L.gateup, 4 - 2 * a0, 8, d_stage, h_stage, stage, s);
     if (rc) break;
-    rc = upload_q8(wd, L.down, 0, 4, d_stage, h_stage, stage, s);
+    rc = upload_q8_rows(wd, r0, r1, L.down, -r0, 4, d_stage, h_stage, stage, s);
     if (rc) break;
     rc = upload_f32(an, L.attn_norm, s);
     if (rc) break;
     rc = upload_f32(fn, L.ffn_norm, s);
     if (rc) break;
-    rc = upload_f32(bq, L.bqkv, s);
+    rc = upload_f32_range(bq, qa, qb, L.bqkv + (qa - q0), s);
     if (rc) break;
-    rc = upload_f32(bk, L.bqkv + E, s);
+    rc = upload_f32_range(bk, ka, kb, L.bqkv + (E + ka - q0), s);
     if (rc) break;
-    rc = upload_f32(bv, L.bqkv + E + kvd, s);
+    rc = upload_f32_range(bv, va, vb, L.bqkv + (E + kvd + va - q0), s);
     if (rc) break;
   }
   cleanup();
@@ -328,6 +402,26 @@ int mi_cuda_qwen2_model_load(const char* gguf_path, int device, mi_cuda_model** 
     return rc;
   }
   *out = m.release();
+  return MI_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mi_cuda_qwen2_model_load(const char* gguf_path, int device, mi_cuda_model** out) {
+  return load_model(gguf_path, device, 0, 1, out);
+}
+
+int mi_cuda_qwen2_model_load_shard(const char* gguf_path, int device, int rank, int world,
+                                   mi_cuda_model** out) {
+  return load_model(gguf_path, device, rank, world, out);
+}
+
+int mi_cuda_tp_shard_range(int64_t n_units, int rank, int world, int64_t* first, int64_t* count) {
+  if (n_units < 0 || world < 1 || rank < 0 || rank >= world || !first || !count)
+    return fail(MI_CUDA_ERR_ARG, "mi_cuda_tp_shard_range: bad arguments");
+  shard_range(n_units, rank, world, first, count);
   return MI_CUDA_OK;
 }
 
@@ -352,17 +446,33 @@ namespace {
 
 // Enqueues one decode step (n_tokens = 1) on kv->stream; with_head adds the
 // LM head + greedy argmax, otherwise the step only advances the position.
+// With a sharded model (world > 1) every GEMV computes this rank's rows and
+// stores them into every rank's exchange words; the consumers read those.
 int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
   mi_cuda_model* m = kv->model;
   const mi_cuda_qwen2_hparams& hp = m->hp;
+  const Shard& sh = m->sh;
   const int64_t E = hp.n_embd, D = hp.head_dim, kvd = (int64_t)hp.n_head_kv * D, FF = hp.n_ff;
+  const int64_t nqkv_full = E + 2 * kvd, act_words = FF / 32 * 9;
+  const bool tp = m->world > 1;
   const ExpTab et = m->ctx->et;
   int32_t* err = &kv->state->err;
   const size_t layer_floats = (size_t)2 * kv->n_ctx * kvd;
+  // exchange words of output `off` (+ layer offset) on every rank
+  auto outs = [&](GemvParams& g, size_t off) {
+    g.n_ranks = m->world;
+    g.rank = m->rank;
+    g.epoch = kv->epoch;
+    for (int r = 0; r < m->world; r++) g.out_ll[r] = kv->peer[r] + off;
+  };
+  auto local = [&](size_t off) -> const uint64_t* { return kv->xbuf + off; };
   int count = 0;
   bool pdl = false;  // the first kernel of a step has no in-graph predecessor
   for (int l = 0; l < hp.n_layer; l++) {
     const Layer& L = m->layers[(size_t)l];
+    const size_t o_qkv = kv->x_qkv + (size_t)l * nqkv_full, o_h1 = kv->x_h1 + (size_t)l * E,
+                 o_act = kv->x_act + (size_t)l * act_words, o_h2 = kv->x_h2 + (size_t)l * E,
+                 o_prev = l > 0 ? kv->x_h2 + (size_t)(l - 1) * E : 0;
     GemvParams p{};
     p.w = L.qkv.w;
     p.K = E;
@@ -386,7 +496,12 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     p.err = err;
     p.trace = kv->trace;
     p.trace_slot = count;
-    CK(launch_gemv(p, kv->plan_qkv, kv->stream, pdl));
+    if (tp) {
+      p.row0 = sh.qkv0;
+      if (l > 0) p.x_ll = local(o_prev);
+      outs(p, o_qkv);
+    }
+    CK(launch_gemv(p, kv->plan_qkv, kv->stream, pdl, tp));
     pdl = kv->pdl;
     count++;
 
@@ -409,13 +524,17 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     a.err = err;
     a.trace = kv->trace;
     a.trace_slot = count;
-    CK(launch_attn_decode(a, true, kv->stream, pdl));
+    if (tp) {
+      a.qkv_ll = local(o_qkv);
+      a.epoch = kv->epoch;
+    }
+    CK(launch_attn_decode(a, true, kv->stream, pdl, tp));
     count++;
 
     GemvParams o{};
     o.w = L.o.w;
     o.K = E;
-    o.N = E;
+    o.N = L.o.N;
     o.n_pad = L.o.npad;
     o.pro = kv->quant_attn ? PRO_ACT : PRO_QUANT;
     o.act = kv->attn_q;
@@ -427,13 +546,18 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     o.err = err;
     o.trace = kv->trace;
     o.trace_slot = count;
-    CK(launch_gemv(o, kv->plan_o, kv->stream, pdl));
+    if (tp) {
+      o.row0 = sh.o0;
+      if (l > 0) o.resid_ll = local(o_prev);
+      outs(o, o_h1);
+    }
+    CK(launch_gemv(o, kv->plan_o, kv->stream, pdl, tp));
     count++;
 
     GemvParams gu{};
     gu.w = L.gateup.w;
     gu.K = E;
-    gu.N = 2 * FF;
+    gu.N = L.gateup.N;
     gu.n_pad = L.gateup.npad;
     gu.pro = PRO_NORM_QUANT;
     gu.x = kv->x2;
@@ -445,13 +569,18 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     gu.err = err;
     gu.trace = kv->trace;
     gu.trace_slot = count;
-    CK(launch_gemv(gu, kv->plan_gu, kv->stream, pdl));
+    if (tp) {
+      gu.row0 = 64 * sh.ff0;
+      gu.x_ll = local(o_h1);
+      outs(gu, o_act);
+    }
+    CK(launch_gemv(gu, kv->plan_gu, kv->stream, pdl, tp));
     count++;
 
     GemvParams dn{};
     dn.w = L.down.w;
     dn.K = FF;
-    dn.N = E;
+    dn.N = L.down.N;
     dn.n_pad = L.down.npad;
     dn.pro = PRO_ACT;
     dn.act = kv->act_q;
@@ -462,14 +591,20 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     dn.err = err;
     dn.trace = kv->trace;
     dn.trace_slot = count;
-    CK(launch_gemv(dn, kv->plan_down, kv->stream, pdl));
+    if (tp) {
+      dn.row0 = sh.o0;
+      dn.act_ll = local(o_act);
+      dn.resid_ll = local(o_h1);
+      outs(dn, o_h2);
+    }
+    CK(launch_gemv(dn, kv->plan_down, kv->stream, pdl, tp));
     count++;
   }
   if (with_head) {
     GemvParams h{};
     h.w = m->lm_head.w;
     h.K = E;
-    h.N = hp.n_vocab;
+    h.N = m->lm_head.N;
     h.n_pad = m->lm_head.npad;
     h.pro = PRO_NORM_QUANT;
     h.x = kv->x;
@@ -489,9 +624,15 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     h.err = err;
     h.trace = kv->trace;
     h.trace_slot = count;
-    CK(launch_gemv(h, kv->plan_head, kv->stream, pdl));
+    if (tp) {
+      h.row0 = sh.v0;
+      h.x_ll = local(kv->x_h2 + (size_t)(hp.n_layer - 1) * E);
+      outs(h, kv->x_cand);
+      h.epoch_rw = kv->epoch;
+    }
+    CK(launch_gemv(h, kv->plan_head, kv->stream, pdl, tp));
   } else {
-    CK(launch_advance(&kv->state->pos, kv->stream, pdl));
+    CK(launch_advance(&kv->state->pos, kv->stream, pdl, tp ? kv->epoch : nullptr));
   }
   count++;
   if (n_kernels) *n_kernels = count;
@@ -511,6 +652,13 @@ int capture(mi_cuda_kv_cache* kv, bool with_head, cudaGraphExec_t* out, int32_t*
   e = cudaGraphInstantiate(out, g, 0);
   cudaGraphDestroy(g);
   if (e != cudaSuccess) return fail(MI_CUDA_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+  return MI_CUDA_OK;
+}
+
+// The step graphs exist (a sharded model's KV cache gets them at connect).
+int graphs_ready(mi_cuda_kv_cache* kv) {
+  if (!kv->g_head || !kv->g_nohead)
+    return fail(MI_CUDA_ERR_STATE, "sharded model: call mi_cuda_tp_connect before running steps");
   return MI_CUDA_OK;
 }
 
@@ -545,12 +693,13 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
   if (const char* e = std::getenv("MI_CUDA_NO_PDL")) kv->pdl = std::atoi(e) == 0;
   const int sms = m->ctx->num_sms;
   kv->quant_attn = D % 32 == 0;
-  kv->plan_qkv = plan_gemv(E, E + 2 * kvd, sms, PRO_EMBED_NORM);
-  kv->plan_o = plan_gemv(E, E, sms, kv->quant_attn ? PRO_ACT : PRO_QUANT);
+  const Shard& sh = m->sh;
+  kv->plan_qkv = plan_gemv(E, sh.nqkv, sms, PRO_EMBED_NORM);
+  kv->plan_o = plan_gemv(E, sh.no, sms, kv->quant_attn ? PRO_ACT : PRO_QUANT);
   // one 32-element block of the FFN activation (64 packed gate/up rows) per CTA
-  kv->plan_gu = plan_gemv(E, 2 * FF, sms, PRO_NORM_QUANT, 64);
-  kv->plan_down = plan_gemv(FF, E, sms, PRO_ACT);
-  kv->plan_head = plan_gemv(E, hp.n_vocab, sms, PRO_NORM_QUANT);
+  kv->plan_gu = plan_gemv(E, 64 * sh.nff, sms, PRO_NORM_QUANT, 64);
+  kv->plan_down = plan_gemv(FF, sh.no, sms, PRO_ACT);
+  kv->plan_head = plan_gemv(E, sh.nv, sms, PRO_NORM_QUANT);
 
   const size_t cache_bytes = (size_t)hp.n_layer * 2 * n_ctx * kvd * 4;
   const size_t rope_bytes = (size_t)n_ctx * (D / 2) * 8;
@@ -567,7 +716,7 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
                o_pi = slot(1024 * 4), o_tok = slot((size_t)(n_ctx + 1) * 4),
                o_state = slot(sizeof(StepState)), o_attnq = slot(E / 32 * 36),
                o_actq = slot(FF / 32 * 36),
-               o_trace = slot((size_t)(5 * hp.n_layer + 1) * kTraceStamps * 8);
+               o_trace = slot((size_t)(5 * hp.n_layer + 1) * kTraceStamps * 8), o_epoch = slot(4);
   CK(cudaMalloc(&kv->buf, off));
   CK(cudaMemset(kv->buf, 0, off));
   kv->cache = (float*)(kv->buf + o_cache);
@@ -587,6 +736,9 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
   kv->act_q = kv->buf + o_actq;
   kv->trace = (uint64_t*)(kv->buf + o_trace);
   kv->trace_slots = 5 * hp.n_layer + 1;
+  kv->epoch = (uint32_t*)(kv->buf + o_epoch);
+  const uint32_t one = 1u;  // exchange words start zeroed: tag 0 is never current
+  CK(cudaMemcpy(kv->epoch, &one, 4, cudaMemcpyHostToDevice));
   if (kv->plan_head.grid > 1024) return fail(MI_CUDA_ERR_ARG, "LM head grid too large");
 
   std::vector<float> cs((size_t)n_ctx * (D / 2) * 2);
@@ -597,6 +749,21 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
   CK(cudaStreamCreateWithFlags(&kv->stream, cudaStreamNonBlocking));
   for (auto& e : kv->ev) CK(cudaEventCreate(&e));
 
+  if (m->world > 1) {
+    // Exchange words; the step graphs are captured by mi_cuda_tp_connect once
+    // every rank's buffer is mapped.
+    kv->x_qkv = 0;
+    kv->x_h1 = kv->x_qkv + (size_t)hp.n_layer * (E + 2 * kvd);
+    kv->x_act = kv->x_h1 + (size_t)hp.n_layer * E;
+    kv->x_h2 = kv->x_act + (size_t)hp.n_layer * (FF / 32 * 9);
+    kv->x_cand = kv->x_h2 + (size_t)hp.n_layer * E;
+    kv->xwords = kv->x_cand + 2 * kMaxRanks;
+    CK(cudaMalloc(&kv->xbuf, kv->xwords * 8));
+    CK(cudaMemset(kv->xbuf, 0, kv->xwords * 8));
+    CK(cudaDeviceSynchronize());
+    *out = kv.release();
+    return MI_CUDA_OK;
+  }
   int rc = capture(kv.get(), true, &kv->g_head, &kv->kernels_per_step);
   if (!rc) rc = capture(kv.get(), false, &kv->g_nohead, nullptr);
   if (rc) {
@@ -613,10 +780,51 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
   return MI_CUDA_OK;
 }
 
+int mi_cuda_tp_exchange_handle(mi_cuda_kv_cache* kv, void* handle_out) {
+  if (!kv || !handle_out || !kv->xbuf)
+    return fail(MI_CUDA_ERR_ARG, "mi_cuda_tp_exchange_handle: not a sharded model's KV cache");
+  CK(cudaSetDevice(kv->model->device));
+  cudaIpcMemHandle_t h;
+  CK(cudaIpcGetMemHandle(&h, kv->xbuf));
+  std::memcpy(handle_out, &h, sizeof(h));
+  return MI_CUDA_OK;
+}
+
+int mi_cuda_tp_connect(mi_cuda_kv_cache* kv, const void* handles) {
+  if (!kv || !handles || !kv->xbuf || kv->connected)
+    return fail(MI_CUDA_ERR_ARG, "mi_cuda_tp_connect: bad arguments or already connected");
+  mi_cuda_model* m = kv->model;
+  CK(cudaSetDevice(m->device));
+  for (int r = 0; r < m->world; r++) {
+    if (r == m->rank) {
+      kv->peer[r] = kv->xbuf;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, (const uint8_t*)handles + (size_t)r * sizeof(h), sizeof(h));
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess)
+      return fail(MI_CUDA_ERR_CUDA, std::string("cudaIpcOpenMemHandle (rank ") + std::to_string(r) +
+                                        "): " + cudaGetErrorString(e));
+    kv->peer[r] = (uint64_t*)p;
+  }
+  int rc = capture(kv, true, &kv->g_head, &kv->kernels_per_step);
+  if (!rc) rc = capture(kv, false, &kv->g_nohead, nullptr);
+  if (rc) return rc;
+  kv->connected = true;
+  return MI_CUDA_OK;
+}
+
+int32_t mi_cuda_ipc_handle_bytes(void) { return (int32_t)sizeof(cudaIpcMemHandle_t); }
+
 void mi_cuda_kv_cache_free(mi_cuda_kv_cache* kv) {
   if (!kv) return;
   cudaSetDevice(kv->model->device);
   if (kv->stream) cudaStreamSynchronize(kv->stream);
+  for (int r = 0; r < kMaxRanks; r++)
+    if (kv->peer[r] && kv->peer[r] != kv->xbuf) cudaIpcCloseMemHandle(kv->peer[r]);
+  if (kv->xbuf) cudaFree(kv->xbuf);
   if (kv->g_head) cudaGraphExecDestroy(kv->g_head);
   if (kv->g_nohead) cudaGraphExecDestroy(kv->g_nohead);
   for (auto& e : kv->ev)
@@ -649,6 +857,7 @@ int mi_cuda_qwen2_decode_steps(mi_cuda_kv_cache* kv, int32_t n_steps, int32_t po
                                int32_t period) {
   if (!kv || n_steps < 0 || period < 0 || pos0 < 0 || pos0 >= kv->n_ctx)
     return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_decode_steps: bad arguments");
+  if (int rc = graphs_ready(kv)) return rc;
   CK(cudaSetDevice(kv->model->device));
   for (int32_t i = 0; i < n_steps; i++) {
     if (period > 0 && i > 0 && i % period == 0) CK(launch_set_pos(&kv->state->pos, pos0, kv->stream));
@@ -692,6 +901,7 @@ int mi_cuda_qwen2_forward(mi_cuda_model* m, mi_cuda_kv_cache* kv, const int32_t*
     return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_forward: bad arguments");
   if (n_past + n_tokens > kv->n_ctx)
     return fail(MI_CUDA_ERR_STATE, "mi_cuda_qwen2_forward: n_past + n_tokens exceeds n_ctx");
+  if (int rc = graphs_ready(kv)) return rc;
   for (int32_t i = 0; i < n_tokens; i++)
     if (h_tokens[i] < 0 || h_tokens[i] >= m->hp.n_vocab)
       return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_forward: token id out of range");
@@ -709,8 +919,9 @@ int mi_cuda_qwen2_forward(mi_cuda_model* m, mi_cuda_kv_cache* kv, const int32_t*
     const bool head = !last_logits_only || t == n_tokens - 1;
     CK(cudaGraphLaunch(head ? kv->g_head : kv->g_nohead, kv->stream));
     if (head && h_logits_out) {
-      float* dst = h_logits_out + (last_logits_only ? 0 : (size_t)t * V);
-      CK(cudaMemcpyAsync(dst, kv->logits, V * 4, cudaMemcpyDeviceToHost, kv->stream));
+      // a sharded model fills its rows [v0, v0 + nv) of each logits row
+      float* dst = h_logits_out + (last_logits_only ? 0 : (size_t)t * V) + m->sh.v0;
+      CK(cudaMemcpyAsync(dst, kv->logits, (size_t)m->sh.nv * 4, cudaMemcpyDeviceToHost, kv->stream));
     }
   }
   return check_state_error(kv);
@@ -743,6 +954,7 @@ int mi_cuda_qwen2_generate(mi_cuda_model* m, mi_cuda_kv_cache* kv, const int32_t
   if (!m || !kv || kv->model != m || !h_prompt || n_prompt <= 0 || n_predict <= 0 || !h_tokens_out)
     return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_generate: bad arguments");
   if (n_prompt > kv->n_ctx) return fail(MI_CUDA_ERR_STATE, "prompt longer than n_ctx");
+  if (int rc = graphs_ready(kv)) return rc;
   for (int32_t i = 0; i < n_prompt; i++)
     if (h_prompt[i] < 0 || h_prompt[i] >= m->hp.n_vocab)
       return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_generate: token id out of range");

@@ -86,6 +86,11 @@ _SIGS = {
     "mi_cuda_qwen2_stream": (P, [P]),
     "mi_cuda_qwen2_kernels_per_step": (I32, [P]),
     "mi_cuda_qwen2_step_trace": (I32, [P, P, I32, P]),
+    "mi_cuda_qwen2_model_load_shard": (I32, [C.c_char_p, I32, I32, I32, P]),
+    "mi_cuda_tp_shard_range": (I32, [I64, I32, I32, P, P]),
+    "mi_cuda_ipc_handle_bytes": (I32, []),
+    "mi_cuda_tp_exchange_handle": (I32, [P, P]),
+    "mi_cuda_tp_connect": (I32, [P, P]),
 }
 
 _lib = None
@@ -299,14 +304,27 @@ def sample_greedy(logits: np.ndarray) -> int:
     return int(lib().mi_cuda_qwen2_sample_greedy(a.ctypes.data, a.size))
 
 
-class Qwen2Model:
-    """mi_qwen2_model_load: GGUF -> weights resident in HBM."""
+def shard_range(n_units: int, rank: int, world: int) -> tuple[int, int]:
+    """(first, count) of the units rank `rank` owns (mi_cuda_tp_shard_range)."""
+    first, count = C.c_int64(), C.c_int64()
+    check(lib().mi_cuda_tp_shard_range(n_units, rank, world, C.byref(first), C.byref(count)))
+    return first.value, count.value
 
-    def __init__(self, gguf_path: str, device: int = 0):
+
+class Qwen2Model:
+    """mi_qwen2_model_load: GGUF -> weights resident in HBM. With world > 1
+    only this rank's rows of every projection are loaded (tensor
+    parallelism; see mi_cuda_qwen2_model_load_shard)."""
+
+    def __init__(self, gguf_path: str, device: int = 0, rank: int = 0, world: int = 1):
         h = P()
-        check(lib().mi_cuda_qwen2_model_load(gguf_path.encode(), device, C.byref(h)))
+        if world == 1:
+            check(lib().mi_cuda_qwen2_model_load(gguf_path.encode(), device, C.byref(h)))
+        else:
+            check(lib().mi_cuda_qwen2_model_load_shard(gguf_path.encode(), device, rank, world, C.byref(h)))
         self.h = h
         self.device = device
+        self.rank, self.world = rank, world
         hp = Hparams()
         check(lib().mi_cuda_qwen2_get_hparams(self.h, C.byref(hp)))
         self.hparams = hp
@@ -332,6 +350,19 @@ class KVCache:
         self.model = model
         self.n_ctx = n_ctx
         self.n_past = 0
+
+    def exchange_handle(self) -> bytes:
+        """This rank's exchange-buffer handle (sharded models)."""
+        buf = (C.c_uint8 * int(lib().mi_cuda_ipc_handle_bytes()))()
+        check(lib().mi_cuda_tp_exchange_handle(self.h, buf))
+        return bytes(buf)
+
+    def connect(self, handles: list[bytes]):
+        """Map every rank's exchange buffer (handles in rank order) and capture
+        the step graphs."""
+        blob = b"".join(handles)
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        check(lib().mi_cuda_tp_connect(self.h, buf))
 
     def forward(self, tokens, n_past: int, last_logits_only: bool = False, want_logits: bool = True):
         """mi_qwen2_forward: returns logits [rows, n_vocab] (rows = 1 with last_logits_only)."""
@@ -390,3 +421,17 @@ class KVCache:
         if self.h:
             lib().mi_cuda_kv_cache_free(self.h)
             self.h = None
+
+
+def gather_handles(handle: bytes, group=None) -> list[bytes]:
+    """Every rank's exchange handle, in rank order, over torch.distributed
+    (any backend; the handles are small host objects)."""
+    import torch.distributed as dist
+    out = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, handle, group=group)
+    return out
+
+
+def tp_connect(kv: "KVCache", group=None):
+    """Exchange-buffer handshake of a sharded model's KV cache on every rank."""
+    kv.connect(gather_handles(kv.exchange_handle(), group))

@@ -62,6 +62,9 @@ QWEN2_7B = Qwen2Shape(n_layer=28, n_embd=3584, n_head=28, n_head_kv=4, n_ff=1894
 # Small shapes for parity tests that the CPU oracle finishes in seconds.
 TINY = Qwen2Shape(n_layer=2, n_embd=64, n_head=4, n_head_kv=2, n_ff=128, n_vocab=256)
 SMALL = Qwen2Shape(n_layer=4, n_embd=256, n_head=4, n_head_kv=2, n_ff=512, n_vocab=2048)
+# The 7B shape's widths (head_dim 128, FFN 18944, untied LM head) in two layers.
+MID7B = Qwen2Shape(n_layer=2, n_embd=3584, n_head=28, n_head_kv=4, n_ff=18944, n_vocab=4096,
+                   tied=False)
 
 
 def quantize_q8_0(x: np.ndarray) -> np.ndarray:

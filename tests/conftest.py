@@ -30,10 +30,11 @@ def model_path():
     """Path of a seeded random-init Qwen2 GGUF of the given shape (cached)."""
     import mi_gguf
 
-    def make(shape_name: str, seed: int) -> str:
+    def make(shape_name: str, seed: int, fast: bool = False) -> str:
         shape = getattr(mi_gguf, shape_name)
-        path = os.path.join(MODEL_DIR, f"{shape_name.lower()}_seed{seed}.gguf")
-        return mi_gguf.ensure_qwen2_gguf(path, shape, seed)
+        tag = "_fast" if fast else ""
+        path = os.path.join(MODEL_DIR, f"{shape_name.lower()}_seed{seed}{tag}.gguf")
+        return mi_gguf.ensure_qwen2_gguf(path, shape, seed, fast=fast)
 
     return make
 

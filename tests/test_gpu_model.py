@@ -144,3 +144,27 @@ def test_qwen2_05b_decode_matches_reference(mc, model_path):
     ref.close()
     kv.free()
     model.free()
+
+
+def test_7b_widths_bitexact(mc, model_path):
+    """Config 4's layer widths (n_embd 3584, 28 heads over 4 KV heads,
+    head_dim 128, FFN 18944, untied LM head) in two layers: prefill and decode
+    logits bit-identical to the reference, greedy tokens identical."""
+    path = model_path("MID7B", 21, fast=True)
+    ref = mi_oracle.ReferenceModel(path, n_ctx=128, n_threads=os.cpu_count() or 1)
+    model = mc.Qwen2Model(path)
+    assert model.hparams.head_dim == 128
+    kv = mc.KVCache(model, 128)
+    prompt = np.random.default_rng(21).integers(0, ref.n_vocab, 12).astype(np.int32)
+    want = ref.forward(prompt, 0)
+    got = kv.forward(prompt, 0)
+    assert np.array_equal(bits(got), bits(want))
+    tok = mc.sample_greedy(want[-1])
+    for step in range(4):
+        w = ref.forward([tok], prompt.size + step)
+        g = kv.forward([tok], prompt.size + step)
+        assert np.array_equal(bits(g), bits(w)), f"step {step}"
+        tok = mc.sample_greedy(w[0])
+    ref.close()
+    kv.free()
+    model.free()
