@@ -162,6 +162,28 @@ def reference_decode(path: str, steps: int, warmup: int, threads: int):
     return total_steps / (total_ms / 1e3), first, f"{total_steps} decode forwards at positions 32..158, {threads} threads"
 
 
+def step_trace_summary(kv) -> dict:
+    """Per-kernel timeline of the last timed step (first CTA of each kernel):
+    dependency wait -> prologue done, prologue -> epilogue, hand-off from the
+    predecessor, and the attention phases."""
+    t = kv.step_trace().astype(np.int64)
+    names = ["qkv", "attn", "o", "gate_up", "down"]
+    kinds = [names[i % 5] for i in range(t.shape[0] - 1)] + ["lm_head"]
+    trace = {"step_us": float(t[-1, 3] - t[0, 0]) / 1e3, "per_kernel_us": {}}
+    for k in dict.fromkeys(kinds):
+        idx = [i for i, kk in enumerate(kinds) if kk == k]
+        dep = [t[i, 1] - t[i - 1, 3] for i in idx if i > 0]  # wait after the predecessor's epilogue started
+        trace["per_kernel_us"][k] = {
+            "dep_to_prologue": float(np.mean([t[i, 2] - t[i, 1] for i in idx])) / 1e3,
+            "prologue_to_epilogue": float(np.mean([t[i, 3] - t[i, 2] for i in idx])) / 1e3,
+            "handoff": float(np.mean(dep)) / 1e3 if dep else None}
+    ai = [i for i, kk in enumerate(kinds) if kk == "attn"]
+    trace["attention_phases_us"] = {
+        name: float(np.mean([t[i, b] - t[i, a] for i in ai])) / 1e3
+        for name, a, b in (("scores", 2, 4), ("max_exp", 4, 5), ("sum", 5, 6), ("kv", 6, 7))}
+    return trace
+
+
 def run_reference_arm(args, rank: int):
     if rank != 0:
         return
@@ -269,6 +291,136 @@ def run_attention(args):
         del ks, vs
 
 
+# Config 4: Qwen2.5-7B shape, tensor-parallel over the ranks (strong scaling:
+# one request, its weights split by rows across the GPUs).
+N_CTX_7B, N_PROMPT_7B = 4096, 64
+METRIC_7B = "decode tok/s (7B-shape Q8_0, ctx 4096, one request, row-sharded over the GPUs)"
+
+
+def run_tp7b(args):
+    import datetime
+    import torch
+    import mi_cuda
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as td
+        td.init_process_group("nccl", timeout=datetime.timedelta(seconds=900))
+        dist = td
+    mi_cuda.init(local)
+    path = os.path.join(MODEL_DIR, f"qwen2_7b_seed{SEED_MODEL}_fast.gguf")
+    t0 = time.time()
+    if rank == 0:
+        mi_gguf.ensure_qwen2_gguf(path, mi_gguf.QWEN2_7B, SEED_MODEL, fast=True)
+    gen_s = time.time() - t0
+    if dist:
+        dist.barrier()
+    t0 = time.time()
+    model = mi_cuda.Qwen2Model(path, device=local, rank=rank, world=world)
+    hp = model.hparams
+    kv = mi_cuda.KVCache(model, N_CTX_7B)
+    if dist:
+        mi_cuda.tp_connect(kv)
+    load_s = time.time() - t0
+    prompt = np.random.default_rng(SEED_PROMPT).integers(0, hp.n_vocab, N_PROMPT_7B).astype(np.int32)
+    kv.forward(prompt, 0, last_logits_only=True, want_logits=False)
+    first = kv.last_token()
+    seed_tokens = np.concatenate([prompt, [first]]).astype(np.int32)
+    stream = torch.cuda.ExternalStream(kv.stream_handle, device=f"cuda:{local}")
+    kv.set_position(seed_tokens, N_PROMPT_7B)
+    kv.decode_steps(args.warmup, N_PROMPT_7B, PERIOD)
+    torch.cuda.synchronize()
+    kv.set_position(seed_tokens, N_PROMPT_7B)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        kv.decode_steps(args.steps, N_PROMPT_7B, PERIOD)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    gen = kv.read_tokens(N_PROMPT_7B, N_PREDICT)
+    trace = step_trace_summary(kv) if args.trace else None
+
+    # e2e through the public per-token API: token H2D, the device's greedy
+    # token D2H (4 bytes; the logits stay sharded on the GPUs)
+    n_e2e = max(1, min(args.e2e_steps, PERIOD))
+    tok = first
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(n_e2e):
+        kv.forward([tok], N_PROMPT_7B + i, last_logits_only=True, want_logits=False)
+        tok = kv.last_token()
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+
+    cpu = parity = None
+    if rank == 0 and not args.no_cpu_baseline:
+        import mi_oracle
+        threads = os.cpu_count() or 1
+        n_dec = 8
+        m = mi_oracle.ReferenceModel(path, n_ctx=N_CTX_7B, n_threads=threads)
+        ref_tok, pre_ms, dec_ms = m.generate(prompt, n_dec + 1)
+        m.close()
+        cpu = {"value": n_dec / (dec_ms / 1e3), "unit": "tok/s", "cores": threads, "kind": "reference",
+               "sample": f"{n_dec} decode forwards at positions 64..{64 + n_dec - 1} after the 64-token prefill "
+                         f"({pre_ms / 1e3:.1f} s), {threads} threads"}
+        parity = {"greedy_tokens_identical": bool(np.array_equal(ref_tok, gen[:n_dec + 1])),
+                  "n_tokens": n_dec + 1, "vs": "reference AVX2 CPU path (oracle/_ref)"}
+
+    value = args.steps / (ms / 1e3)
+    n_kvs = [N_PROMPT_7B + (i % PERIOD) + 1 for i in range(args.steps)]
+    total_bytes = sum(step_bytes(hp, n) for n in n_kvs)
+    peak, peak_kind = load_peaks()
+    achieved = total_bytes / (ms / 1e3) / 1e9
+    if rank == 0:
+        line = {
+            "metric": METRIC_7B, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "i8*i8->f32",
+            "data": f"synthetic: random-init N(0,0.02) Q8_0 GGUF (mi_gguf_gen, seed {SEED_MODEL}), "
+                    f"64 uniform prompt ids (seed {SEED_PROMPT})",
+            "config": {"workload": "qwen2.5-7b-shape Q8_0 greedy decode, ctx 4096, prompt 64, positions "
+                                   "64..190 cycled on the device", "n_ctx": N_CTX_7B, "prompt": N_PROMPT_7B,
+                       "parallelism": f"tp{world} (row-sharded GEMVs, peer-store exchange)",
+                       "l2": "inputs larger than L2: 7.5 GB of weights streamed every step"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * world, "unit": "GB/s",
+                         "frac": achieved / (peak * world), "traffic": None, "peak_kind": f"{peak_kind} x {world}",
+                         "kernel": f"decode step graph ({kv.kernels_per_step} kernels per rank)",
+                         "bytes_per_step": total_bytes / args.steps},
+            "e2e": {"value": n_e2e / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 + 36,
+                    "d2h_bytes_per_step": 4, "api": "mi_cuda_qwen2_forward (no logits) + mi_cuda_qwen2_last_token"},
+            "gpu_launches": args.steps * kv.kernels_per_step * world,
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+            "parity": parity,
+            "setup_s": {"gguf_write": gen_s, "load_and_connect": load_s},
+        }
+        if trace is not None:
+            line["trace"] = trace
+        print(json.dumps(line), flush=True)
+    kv.free()
+    model.free()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -277,8 +429,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=PERIOD)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", choices=["decode", "gemv", "attention"], default="decode",
-                    help="decode: config 0 (default); gemv: config-1 GEMV sweep; attention: config 2")
+    ap.add_argument("--config", choices=["decode", "gemv", "attention", "tp7b"], default="decode",
+                    help="decode: config 0 (default); gemv: config-1 GEMV sweep; attention: config 2; "
+                         "tp7b: config 4, 7B shape tensor-parallel over the torchrun ranks")
     ap.add_argument("--shapes", default="896x896,128x896,4864x896,896x4864,151936x896",
                     help="gemv: NxK list")
     ap.add_argument("--nkv", default="128,1024,4096,32768", help="attention: n_kv list")
@@ -291,6 +444,8 @@ def main():
         return run_gemv_sweep(args)
     if args.config == "attention":
         return run_attention(args)
+    if args.config == "tp7b" and args.impl == "ours":
+        return run_tp7b(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -343,24 +498,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     gen = kv.read_tokens(N_PROMPT, N_PREDICT)
-    trace = None
-    if args.trace:
-        # per-kernel timeline of the last timed step (first CTA of each kernel)
-        t = kv.step_trace().astype(np.int64)
-        names = ["qkv", "attn", "o", "gate_up", "down"]
-        kinds = [names[i % 5] for i in range(t.shape[0] - 1)] + ["lm_head"]
-        trace = {"step_us": float(t[-1, 3] - t[0, 0]) / 1e3, "per_kernel_us": {}}
-        for k in dict.fromkeys(kinds):
-            idx = [i for i, kk in enumerate(kinds) if kk == k]
-            dep = [t[i, 1] - t[i - 1, 3] for i in idx if i > 0]  # wait after the predecessor's epilogue started
-            trace["per_kernel_us"][k] = {
-                "dep_to_prologue": float(np.mean([t[i, 2] - t[i, 1] for i in idx])) / 1e3,
-                "prologue_to_epilogue": float(np.mean([t[i, 3] - t[i, 2] for i in idx])) / 1e3,
-                "handoff": float(np.mean(dep)) / 1e3 if dep else None}
-        ai = [i for i, kk in enumerate(kinds) if kk == "attn"]
-        trace["attention_phases_us"] = {
-            name: float(np.mean([t[i, b] - t[i, a] for i in ai])) / 1e3
-            for name, a, b in (("scores", 2, 4), ("max_exp", 4, 5), ("sum", 5, 6), ("kv", 6, 7))}
+    trace = step_trace_summary(kv) if args.trace else None
 
     # roofline: algorithmic bytes of the timed steps over their device time
     n_kvs = [N_PROMPT + (i % PERIOD) + 1 for i in range(args.steps)]

@@ -21,13 +21,15 @@ constexpr int kSpecSumMin = 256;
 // Shared-memory map of the GEMV kernel, computed identically on host and
 // device: [0,64) mbarriers, [64,128) broadcast scalars, activation quants,
 // activation scales, per-row results, F32 input staging (norm prologues),
-// then n_stages weight stages of stage_rows rows each (quants, then scales).
+// then n_stages weight stages, each stage_rows rows by kc blocks of K (the
+// groups' quants, then their scales).
 struct GemvSmem {
   size_t act_qs, act_d, res, xs, sq, spec, stages, stage_bytes, total;
 };
 
 __host__ __device__ inline GemvSmem gemv_smem(int64_t K, int32_t rows_per_cta, int32_t stage_rows,
-                                              int32_t n_stages, int32_t pro, int32_t stage_x) {
+                                              int32_t n_stages, int32_t pro, int32_t stage_x,
+                                              int32_t kc) {
   GemvSmem L;
   size_t off = 128;
   L.act_qs = off;
@@ -44,7 +46,7 @@ __host__ __device__ inline GemvSmem gemv_smem(int64_t K, int32_t rows_per_cta, i
   if (pro >= PRO_NORM_QUANT) off += (size_t)((spec_sum_scratch_bytes(8, 4) + 15) / 16 * 16);
   off = (off + 127) / 128 * 128;
   L.stages = off;
-  L.stage_bytes = (size_t)(((int64_t)stage_rows * K + (int64_t)stage_rows * (K / 32) * 2 + 127) / 128 * 128);
+  L.stage_bytes = (size_t)(((int64_t)stage_rows * kc * 34 + 127) / 128 * 128);
   off += (size_t)n_stages * L.stage_bytes;
   L.total = off;
   return L;
@@ -69,6 +71,11 @@ __host__ __device__ inline GemvSmem gemv_smem(int64_t K, int32_t rows_per_cta, i
 // prologue builds the quantized activation in shared memory (optionally after
 // the embedding lookup and rms_norm), the warps consume the stages, and the
 // epilogue applies bias / residual / SiLU*up / argmax.
+//
+// Wide rows (n_chunks > 1): a stage holds a K-chunk of up to 8 row groups;
+// the tiles run chunk by chunk through one pass of rows, and each warp keeps
+// its group's lane accumulators across the chunks, so the per-lane block
+// order is unchanged.
 // ---------------------------------------------------------------------------
 template <int NT, int TPR, bool TP>
 __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
@@ -77,7 +84,8 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t K = p.K;
   const int nb = (int)(K >> 5);
-  const GemvSmem L = gemv_smem(K, p.rows_per_cta, p.stage_rows, p.n_stages, p.pro, p.stage_x);
+  const int kc = p.kc, n_chunks = p.n_chunks;
+  const GemvSmem L = gemv_smem(K, p.rows_per_cta, p.stage_rows, p.n_stages, p.pro, p.stage_x, kc);
   uint64_t* bars = (uint64_t*)smem;
   float* misc = (float*)(smem + 64);
   int8_t* aq = (int8_t*)(smem + L.act_qs);
@@ -89,19 +97,35 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
   const int64_t r0 = (int64_t)blockIdx.x * p.rows_per_cta;
   const int64_t r1 = min(r0 + (int64_t)p.rows_per_cta, p.n_pad);
   const int nrows = (int)(r1 - r0);
-  const int n_tiles = (nrows + p.stage_rows - 1) / p.stage_rows;
+  const int n_tiles = (nrows + p.stage_rows - 1) / p.stage_rows * n_chunks;
   const uint8_t* wq = p.w;
   const uint8_t* wd = p.w + p.n_pad * K;
 
   auto issue = [&](int t) {
     const int s = t % p.n_stages;
-    const int64_t tr0 = r0 + (int64_t)t * p.stage_rows;
+    const int pass = n_chunks == 1 ? t : t / n_chunks, ch = t - pass * n_chunks;
+    const int64_t tr0 = r0 + (int64_t)pass * p.stage_rows;
     const int rows = (int)min((int64_t)p.stage_rows, r1 - tr0);
-    const uint32_t qb = (uint32_t)(rows * K), db = (uint32_t)(rows * nb * 2);
     uint8_t* st = stages + (size_t)s * L.stage_bytes;
-    mbar_arrive_expect_tx(&bars[s], qb + db);
-    bulk_load(st, wq + tr0 * K, qb, &bars[s]);
-    bulk_load(st + (size_t)p.stage_rows * K, wd + tr0 * nb * 2, db, &bars[s]);
+    if (n_chunks == 1) {
+      const uint32_t qb = (uint32_t)(rows * K), db = (uint32_t)(rows * nb * 2);
+      mbar_arrive_expect_tx(&bars[s], qb + db);
+      bulk_load(st, wq + tr0 * K, qb, &bars[s]);
+      bulk_load(st + (size_t)p.stage_rows * K, wd + tr0 * nb * 2, db, &bars[s]);
+    } else {
+      // blocks [c0, c0 + kcb) of each 4-row group: 128 B of quants and 8 B of
+      // scales per block, contiguous in the packed layout (nb and kc even keep
+      // every copy 16-byte aligned)
+      const int c0 = ch * kc, kcb = min(kc, nb - c0), ng = rows >> 2;
+      const uint32_t qb = 128u * (uint32_t)kcb, db = 8u * (uint32_t)kcb;
+      mbar_arrive_expect_tx(&bars[s], (uint32_t)ng * (qb + db));
+      const int64_t g0 = tr0 >> 2;
+      uint8_t* sdst = st + (size_t)p.stage_rows * 32 * kc;
+      for (int g = 0; g < ng; g++) {
+        bulk_load(st + (size_t)g * 128 * kc, wq + (g0 + g) * 4 * K + (int64_t)c0 * 128, qb, &bars[s]);
+        bulk_load(sdst + (size_t)g * 8 * kc, wd + ((g0 + g) * nb + c0) * 8, db, &bars[s]);
+      }
+    }
   };
 
   trace_mark(p.trace, p.trace_slot, 0);
@@ -179,15 +203,31 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
       __syncthreads();
       scale = misc[0];
     }
-    for (int b = warp; b < nb; b += NW) {
-      const int64_t k = (int64_t)b * 32 + lane;
-      float v;
+    // One block per warp at a time would serialize the quantizer's two
+    // divisions; four independent blocks per iteration overlap them.
+    auto value = [&](int64_t k) {
       if (p.pro >= PRO_NORM_QUANT)
-        v = __fmul_rn(__fmul_rn(xs[k], scale), p.norm_w[k]);  // rms_norm, then MUL weight
-      else
-        v = p.stage_x ? xs[k] : p.x[k];
+        return __fmul_rn(__fmul_rn(xs[k], scale), p.norm_w[k]);  // rms_norm, then MUL weight
+      return p.stage_x ? xs[k] : p.x[k];
+    };
+    int b = warp;
+    for (; b + 3 * NW < nb; b += 4 * NW) {
+      float v[4], d[4];
+      int8_t q[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) v[u] = value((int64_t)(b + u * NW) * 32 + lane);
+#pragma unroll
+      for (int u = 0; u < 4; u++) q[u] = quantize_lane(v[u], &d[u]);
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        aq[(int64_t)(b + u * NW) * 32 + lane] = q[u];
+        if (lane == 0) ad[b + u * NW] = d[u];
+      }
+    }
+    for (; b < nb; b += NW) {
+      const int64_t k = (int64_t)b * 32 + lane;
       float d;
-      aq[k] = quantize_lane(v, &d);
+      aq[k] = quantize_lane(value(k), &d);
       if (lane == 0) ad[b] = d;
     }
   }
@@ -198,6 +238,7 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
   const int rr = lane >> 3, j = lane & 7;
   const int* aq4 = (const int*)aq;
   bool ok = true;
+  float acc_run = 0.0f;  // wide rows: the warp's lane accumulator between K-chunks
   for (int t = 0; t < n_tiles; t++) {
     const int s = t % p.n_stages;
     ok = mbar_wait_bounded(&bars[s], (uint32_t)((t / p.n_stages) & 1), p.err);
@@ -206,31 +247,41 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
       break;
     }
     const uint8_t* st = stages + (size_t)s * L.stage_bytes;
-    const int64_t tr0 = r0 + (int64_t)t * p.stage_rows;
-    const int ngroups = (int)(min((int64_t)p.stage_rows, r1 - tr0) >> 2);
     const uint32_t* sq = (const uint32_t*)st;
-    const __half* sd = (const __half*)(st + (size_t)p.stage_rows * K);
     if (TPR == 8) {
-      // 8 threads per row, one lane each; a warp covers one group of 4 rows.
+      const int pass = n_chunks == 1 ? t : t / n_chunks, ch = t - pass * n_chunks;
+      const int64_t tr0 = r0 + (int64_t)pass * p.stage_rows;
+      const int ngroups = (int)(min((int64_t)p.stage_rows, r1 - tr0) >> 2);
+      const int c0 = ch * kc, kcb = min(kc, nb - c0);
+      const __half* sd = (const __half*)(st + (size_t)p.stage_rows * 32 * kc);
+      // 8 threads per row, one lane each; a warp covers one group of 4 rows
+      // (with K-chunks at most one, whose accumulator carries to the next chunk).
       for (int g = warp; g < ngroups; g += NW) {
-        const uint32_t* gq = sq + (size_t)g * K;
-        const __half* gd = sd + (size_t)g * nb * 4;
-        float acc = 0.0f;
+        const uint32_t* gq = sq + (size_t)g * 32 * kc;
+        const __half* gd = sd + (size_t)g * 4 * kc;
+        float acc = ch == 0 ? 0.0f : acc_run;
 #pragma unroll 4
-        for (int i = 0; i < nb; i++) {
-          const int pi = __dp4a((int)gq[i * 32 + lane], aq4[i * 8 + j], 0);
-          const float dxdy = __fmul_rn(__half2float(gd[i * 4 + rr]), ad[i]);
+        for (int i = 0; i < kcb; i++) {
+          const int pi = __dp4a((int)gq[i * 32 + lane], aq4[(c0 + i) * 8 + j], 0);
+          const float dxdy = __fmul_rn(__half2float(gd[i * 4 + rr]), ad[c0 + i]);
           acc = __fmaf_rn(__int2float_rn(pi), dxdy, acc);
+        }
+        if (ch + 1 < n_chunks) {
+          acc_run = acc;
+          continue;
         }
         const float s4 = __fadd_rn(acc, __shfl_xor_sync(FULL, acc, 4));
         const float s1 = __fadd_rn(s4, __shfl_xor_sync(FULL, s4, 1));
         const float s2 = __fadd_rn(s1, __shfl_xor_sync(FULL, s1, 2));
-        if (j == 0) res[t * p.stage_rows + g * 4 + rr] = s2;
+        if (j == 0) res[pass * p.stage_rows + g * 4 + rr] = s2;
       }
     } else {
       // 2 threads per row, lanes 4h..4h+3 each from one 16-byte load; a warp
       // covers 4 groups (16 rows). Thread h=0 ends with l0..l3, its partner
-      // (lane ^ 1) with l4..l7.
+      // (lane ^ 1) with l4..l7. (Whole rows per stage: n_chunks == 1.)
+      const int64_t tr0 = r0 + (int64_t)t * p.stage_rows;
+      const int ngroups = (int)(min((int64_t)p.stage_rows, r1 - tr0) >> 2);
+      const __half* sd = (const __half*)(st + (size_t)p.stage_rows * K);
       const int gw = lane >> 3, r4 = (lane >> 1) & 3, h = lane & 1;
       const uint4* aq16 = (const uint4*)aq;
       for (int g0 = warp * 4; g0 < ngroups; g0 += NW * 4) {
@@ -276,10 +327,12 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
   // ---- epilogue ----
   trace_mark(p.trace, p.trace_slot, 3);
   if (p.epi == EPI_SILU_GATEUP_Q) {
-    // This CTA's 64 packed rows are gate/up rows of act elements [32b, 32b+32):
-    // act[a] = silu(gate) * up, then the down projection's quantize node.
-    if (warp == 0) {
-      const int64_t a = (r0 >> 3) * 4 + lane;       // act element of this lane
+    // Each 64 packed rows of the CTA are the gate/up rows of one 32-element
+    // block of act: act[a] = silu(gate) * up, then the down projection's
+    // quantize node. Warp w handles the CTA's block w.
+    if (warp < (nrows >> 6)) {
+      const int64_t rb = r0 + 64 * warp;               // the block's first packed row
+      const int64_t a = (rb >> 3) * 4 + lane;           // act element of this lane
       const int lr = (int)((a >> 2) * 8 + (a & 3) - r0);  // its gate row, local
       const float v = __fmul_rn(silu_exact(res[lr], p.et), res[lr + 4]);
       float d;
@@ -290,7 +343,7 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
         const uint32_t b1 = __shfl_down_sync(FULL, b0, 1), b2 = __shfl_down_sync(FULL, b0, 2),
                        b3 = __shfl_down_sync(FULL, b0, 3);
         const uint32_t word = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
-        const int64_t blk = (p.row0 + r0) >> 6;
+        const int64_t blk = (p.row0 + rb) >> 6;
         const uint32_t tag = *p.epoch;
         for (int rk = 0; rk < p.n_ranks; rk++) {
           uint64_t* dst = p.out_ll[rk] + blk * 9;
@@ -298,7 +351,7 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
           if ((lane & 3) == 0) ll_store(dst + 1 + (lane >> 2), word, tag);
         }
       } else {
-        uint8_t* blk = p.act_out + (size_t)(r0 >> 6) * 36;
+        uint8_t* blk = p.act_out + (size_t)(rb >> 6) * 36;
         ((int8_t*)blk)[4 + lane] = q;
         if (lane == 0) *(float*)blk = d;
       }
@@ -435,6 +488,57 @@ cudaError_t prepare_attn_kernels(int optin);
 GemvPlan plan_gemv(int64_t k, int64_t n, int num_sms, int pro, int32_t rows_per_cta) {
   GemvPlan pl{};
   const int64_t n_pad = (n + 7) / 8 * 8;
+  const int64_t nb = k / 32;
+  const size_t limit = 220 * 1024;
+  pl.threads = 256;
+  pl.kc = (int32_t)nb;
+  pl.n_chunks = 1;
+  if (nb >= 64 && nb % 2 == 0) {
+    // Wide rows (K >= 2048): one 4-row group per warp, stages of up to 32 rows
+    // by a K-chunk of ~64 KB; each warp's accumulator carries across the
+    // chunks of its group. Rows per CTA are a multiple of 4.
+    const int64_t groups = n_pad / 4;
+    const int64_t target = std::max<int64_t>(1, std::min<int64_t>(num_sms, groups));
+    pl.rows_per_cta = rows_per_cta > 0 ? rows_per_cta : (int32_t)((groups + target - 1) / target * 4);
+    pl.grid = (int)((n_pad + pl.rows_per_cta - 1) / pl.rows_per_cta);
+    pl.tpr = 8;
+    pl.stage_rows = std::min<int32_t>(32, pl.rows_per_cta);
+    int64_t stage_bytes = 64 * 1024;
+    int64_t max_stages = 4;
+    // MI_CUDA_GEMV_WIDE="rows,stage_kb,stages" overrides the wide-row stage
+    // shape (for tuning sweeps; values are clamped to valid ones).
+    if (const char* e = std::getenv("MI_CUDA_GEMV_WIDE")) {
+      int r = 0, kb = 0, st = 0;
+      if (std::sscanf(e, "%d,%d,%d", &r, &kb, &st) == 3 && r > 0 && kb > 0 && st > 0) {
+        pl.stage_rows = std::min<int32_t>(pl.rows_per_cta, std::max(4, std::min(32, r / 4 * 4)));
+        stage_bytes = (int64_t)kb * 1024;
+        max_stages = st;
+      }
+    }
+    int64_t kc = std::min<int64_t>(nb, (stage_bytes / (pl.stage_rows * 34)) & ~1);
+    if (kc < 2) kc = 2;
+    pl.stage_x = 1;
+    for (;;) {
+      pl.kc = (int32_t)kc;
+      pl.n_chunks = (int32_t)((nb + kc - 1) / kc);
+      const int64_t tiles = (int64_t)(pl.rows_per_cta + pl.stage_rows - 1) / pl.stage_rows * pl.n_chunks;
+      pl.n_stages = (int32_t)std::min<int64_t>(tiles, max_stages);
+      for (;;) {
+        pl.smem = gemv_smem(k, pl.rows_per_cta, pl.stage_rows, pl.n_stages, pro, pl.stage_x, pl.kc).total;
+        if (pl.smem <= limit || pl.n_stages <= 2) break;
+        pl.n_stages--;
+      }
+      if (pl.smem <= limit) break;
+      if (pl.stage_x && pro == PRO_QUANT) {
+        pl.stage_x = 0;  // very wide K: quantize from global
+      } else if (kc > 2) {
+        kc = std::max<int64_t>(2, (kc / 2) & ~1);
+      } else {
+        break;
+      }
+    }
+    return pl;
+  }
   const int64_t groups8 = n_pad / 8;
   const int64_t target = std::max<int64_t>(1, std::min<int64_t>(num_sms, groups8));
   pl.rows_per_cta = rows_per_cta > 0 ? rows_per_cta
@@ -450,23 +554,21 @@ GemvPlan plan_gemv(int64_t k, int64_t n, int num_sms, int pro, int32_t rows_per_
     tiles = (pl.rows_per_cta + sr - 1) / sr;
   }
   pl.stage_rows = (int32_t)sr;
-  pl.n_stages = (int32_t)std::min<int64_t>(tiles, 4);
-  const size_t limit = 220 * 1024;
-  pl.stage_x = 1;
-  for (;;) {
-    pl.smem = gemv_smem(k, pl.rows_per_cta, pl.stage_rows, pl.n_stages, pro, pl.stage_x).total;
-    if (pl.smem <= limit) break;
-    if (pl.n_stages > 1) pl.n_stages--;
-    else if (pl.stage_x && pro == PRO_QUANT) pl.stage_x = 0;  // very wide K: quantize from global
-    else break;
-  }
-  pl.threads = 256;
   // Wide stages (>= 64 rows keep >= 4 warps busy) use 2 threads per row and
   // 16-byte loads; narrow ones use 8 threads per row for more parallelism.
   pl.tpr = pl.stage_rows >= 64 ? 2 : 8;
   if (const char* e = std::getenv("MI_CUDA_GEMV_TPR")) {
     const int v = std::atoi(e);
     if (v == 2 || v == 8) pl.tpr = v;
+  }
+  pl.n_stages = (int32_t)std::min<int64_t>(tiles, 4);
+  pl.stage_x = 1;
+  for (;;) {
+    pl.smem = gemv_smem(k, pl.rows_per_cta, pl.stage_rows, pl.n_stages, pro, pl.stage_x, pl.kc).total;
+    if (pl.smem <= limit) break;
+    if (pl.n_stages > 1) pl.n_stages--;
+    else if (pl.stage_x && pro == PRO_QUANT) pl.stage_x = 0;  // very wide K: quantize from global
+    else break;
   }
   return pl;
 }
@@ -507,6 +609,8 @@ cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& plan, cudaStream_t 
   q.stage_rows = plan.stage_rows;
   q.n_stages = plan.n_stages;
   q.stage_x = plan.stage_x;
+  q.kc = plan.kc;
+  q.n_chunks = plan.n_chunks;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)plan.grid);
   cfg.blockDim = dim3(256);

@@ -47,6 +47,7 @@ struct GemvParams {
   const uint8_t* w;
   int64_t K, N, n_pad;
   int32_t rows_per_cta, stage_rows, n_stages, pro, epi;
+  int32_t kc, n_chunks;  // set by the launcher: blocks per K-chunk of a stage, chunks per row pass
   int32_t tokens_len;  // entries of `tokens` / `tokens_rw` (bounds for pos)
   int32_t stage_x;     // set by the launcher: F32 input staged in shared memory
   // prologue inputs
@@ -93,11 +94,13 @@ struct GemvParams {
 struct GemvPlan {
   int grid, threads, tpr;
   int32_t rows_per_cta, stage_rows, n_stages, stage_x;
+  int32_t kc, n_chunks;  // K-chunk of a stage in 32-element blocks (kc == K/32: whole rows)
   size_t smem;
 };
 
 // Work split for an n-row, k-column packed matrix over the device's SMs.
-// rows_per_cta > 0 fixes the rows per CTA (a multiple of 8).
+// rows_per_cta > 0 fixes the rows per CTA (a multiple of 8; of 64 for the
+// SiLU*up quantizing epilogue, at most 8 blocks).
 GemvPlan plan_gemv(int64_t k, int64_t n, int num_sms, int pro, int32_t rows_per_cta = 0);
 // Per-device kernel attributes (dynamic shared memory limit); called once per
 // device at context creation, outside any stream capture.

@@ -696,8 +696,11 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
   const Shard& sh = m->sh;
   kv->plan_qkv = plan_gemv(E, sh.nqkv, sms, PRO_EMBED_NORM);
   kv->plan_o = plan_gemv(E, sh.no, sms, kv->quant_attn ? PRO_ACT : PRO_QUANT);
-  // one 32-element block of the FFN activation (64 packed gate/up rows) per CTA
-  kv->plan_gu = plan_gemv(E, 64 * sh.nff, sms, PRO_NORM_QUANT, 64);
+  // whole 32-element blocks of the FFN activation (64 packed gate/up rows
+  // each) per CTA: one block at narrow K; at wide K (one CTA per SM) enough
+  // blocks that every SM has a CTA in a single wave
+  const int64_t bpc = E / 32 >= 64 ? std::min<int64_t>(8, (sh.nff + sms - 1) / sms) : 1;
+  kv->plan_gu = plan_gemv(E, 64 * sh.nff, sms, PRO_NORM_QUANT, (int32_t)(64 * bpc));
   kv->plan_down = plan_gemv(FF, sh.no, sms, PRO_ACT);
   kv->plan_head = plan_gemv(E, sh.nv, sms, PRO_NORM_QUANT);
 
