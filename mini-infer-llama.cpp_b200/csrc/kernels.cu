@@ -19,7 +19,7 @@ constexpr unsigned FULL = 0xffffffffu;
 constexpr int kSpecSumMin = 256;
 
 // Shared-memory map of the GEMV kernel, computed identically on host and
-// device: [0,64) mbarriers, [64,128) broadcast scalars, activation quants,
+// device: [0,256) mbarriers, [256,320) broadcast scalars, activation quants,
 // activation scales, per-row results, F32 input staging (norm prologues),
 // then n_stages weight stages, each stage_rows rows by kc blocks of K (the
 // groups' quants, then their scales).
@@ -31,7 +31,7 @@ __host__ __device__ inline GemvSmem gemv_smem(int64_t K, int32_t rows_per_cta, i
                                               int32_t n_stages, int32_t pro, int32_t stage_x,
                                               int32_t kc) {
   GemvSmem L;
-  size_t off = 128;
+  size_t off = 320;
   L.act_qs = off;
   off += (size_t)((K + 15) / 16 * 16);
   L.act_d = off;
@@ -87,7 +87,7 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
   const int kc = p.kc, n_chunks = p.n_chunks;
   const GemvSmem L = gemv_smem(K, p.rows_per_cta, p.stage_rows, p.n_stages, p.pro, p.stage_x, kc);
   uint64_t* bars = (uint64_t*)smem;
-  float* misc = (float*)(smem + 64);
+  float* misc = (float*)(smem + 256);
   int8_t* aq = (int8_t*)(smem + L.act_qs);
   float* ad = (float*)(smem + L.act_d);
   float* res = (float*)(smem + L.res);
@@ -128,14 +128,39 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
     }
   };
 
+  // Warp-stream mode (TPR == 0, wide rows): warp w streams the CTA's groups
+  // w, w + NW, ... K-chunk by K-chunk through its own ring of S stages (its
+  // lane 0 issues the copies), with 8 threads per row; no CTA-wide barrier
+  // until the epilogue.
+  const int ngroups_cta = nrows >> 2;
+  const int active_warps = TPR == 0 ? (int)min((int64_t)NW, ((int64_t)p.rows_per_cta + 3) >> 2) : 1;
+  const int S = TPR == 0 ? p.n_stages / active_warps : p.n_stages;
+  const int my_tiles = TPR == 0 && ngroups_cta > warp ? (ngroups_cta - warp + NW - 1) / NW * n_chunks : 0;
+  uint64_t* wbars = bars + (TPR == 0 ? warp * S : 0);
+  uint8_t* wring = stages + (TPR == 0 ? (size_t)warp * S * L.stage_bytes : 0);
+  auto wissue = [&](int tau) {
+    const int s = tau % S;
+    const int gk = n_chunks == 1 ? tau : tau / n_chunks, ch = tau - gk * n_chunks;
+    const int64_t G = (r0 >> 2) + warp + (int64_t)gk * NW;
+    const int c0 = ch * kc, kcb = min(kc, nb - c0);
+    uint8_t* st = wring + (size_t)s * L.stage_bytes;
+    mbar_arrive_expect_tx(&wbars[s], 136u * (uint32_t)kcb);
+    bulk_load(st, wq + G * 4 * K + (int64_t)c0 * 128, 128u * (uint32_t)kcb, &wbars[s]);
+    bulk_load(st + (size_t)128 * kc, wd + (G * nb + c0) * 8, 8u * (uint32_t)kcb, &wbars[s]);
+  };
+
   trace_mark(p.trace, p.trace_slot, 0);
   if (tid == 0) {
     for (int s = 0; s < p.n_stages; s++) mbar_init(&bars[s], 1);
     fence_mbar_init();
   }
   __syncthreads();
-  if (tid == 0)
+  if (TPR == 0) {
+    if (lane == 0)
+      for (int t = 0; t < min(my_tiles, S); t++) wissue(t);
+  } else if (tid == 0) {
     for (int t = 0; t < min(n_tiles, p.n_stages); t++) issue(t);
+  }
   pdl_trigger();
   pdl_wait_cta();
   trace_mark(p.trace, p.trace_slot, 1);
@@ -239,7 +264,47 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
   const int* aq4 = (const int*)aq;
   bool ok = true;
   float acc_run = 0.0f;  // wide rows: the warp's lane accumulator between K-chunks
-  for (int t = 0; t < n_tiles; t++) {
+  if (TPR == 0) {
+    int tau = 0;
+    float acc = 0.0f;
+    for (; tau < my_tiles; tau++) {
+      const int s = tau % S;
+      ok = mbar_wait_bounded(&wbars[s], (uint32_t)((tau / S) & 1), p.err);
+      if (!__all_sync(FULL, ok)) {
+        ok = false;
+        break;
+      }
+      const int gk = n_chunks == 1 ? tau : tau / n_chunks, ch = tau - gk * n_chunks;
+      const int c0 = ch * kc, kcb = min(kc, nb - c0);
+      const uint8_t* st = wring + (size_t)s * L.stage_bytes;
+      const uint32_t* gq = (const uint32_t*)st;
+      const __half* gd = (const __half*)(st + (size_t)128 * kc);
+      if (ch == 0) acc = 0.0f;
+#pragma unroll 4
+      for (int i = 0; i < kcb; i++) {
+        const int pi = __dp4a((int)gq[i * 32 + lane], aq4[(c0 + i) * 8 + j], 0);
+        const float dxdy = __fmul_rn(__half2float(gd[i * 4 + rr]), ad[c0 + i]);
+        acc = __fmaf_rn(__int2float_rn(pi), dxdy, acc);
+      }
+      __syncwarp();
+      if (lane == 0 && tau + S < my_tiles) wissue(tau + S);
+      if (ch + 1 == n_chunks) {
+        const float s4 = __fadd_rn(acc, __shfl_xor_sync(FULL, acc, 4));
+        const float s1 = __fadd_rn(s4, __shfl_xor_sync(FULL, s4, 1));
+        const float s2 = __fadd_rn(s1, __shfl_xor_sync(FULL, s1, 2));
+        if (j == 0) res[(warp + gk * NW) * 4 + rr] = s2;
+      }
+    }
+    if (__syncthreads_or(!ok)) {
+      // Copies this warp issued and did not consume get a bounded chance to
+      // land before the CTA's shared memory is released.
+      if (lane == 0)
+        for (int t = tau; t < min(my_tiles, tau + S); t++)
+          (void)mbar_wait_bounded(&wbars[t % S], (uint32_t)((t / S) & 1), nullptr);
+      return;
+    }
+  }
+  for (int t = 0; TPR != 0 && t < n_tiles; t++) {
     const int s = t % p.n_stages;
     ok = mbar_wait_bounded(&bars[s], (uint32_t)((t / p.n_stages) & 1), p.err);
     if (!__syncthreads_and(ok)) {
@@ -494,35 +559,58 @@ GemvPlan plan_gemv(int64_t k, int64_t n, int num_sms, int pro, int32_t rows_per_
   pl.kc = (int32_t)nb;
   pl.n_chunks = 1;
   if (nb >= 64 && nb % 2 == 0) {
-    // Wide rows (K >= 2048): one 4-row group per warp, stages of up to 32 rows
-    // by a K-chunk of ~64 KB; each warp's accumulator carries across the
-    // chunks of its group. Rows per CTA are a multiple of 4.
+    // Wide rows (K >= 2048). Rows per CTA are a multiple of 4 (one CTA per SM
+    // or the caller's count). Default: warp-stream mode (tpr 0), each active
+    // warp owning a ring of S stages of one group's K-chunk, S = 3, the chunk
+    // as large as shared memory allows. MI_CUDA_GEMV_WIDE="0,S,stage_kb" or
+    // "8,rows,stage_kb" picks the mode and shape (tuning sweeps; clamped).
     const int64_t groups = n_pad / 4;
     const int64_t target = std::max<int64_t>(1, std::min<int64_t>(num_sms, groups));
     pl.rows_per_cta = rows_per_cta > 0 ? rows_per_cta : (int32_t)((groups + target - 1) / target * 4);
     pl.grid = (int)((n_pad + pl.rows_per_cta - 1) / pl.rows_per_cta);
-    pl.tpr = 8;
-    pl.stage_rows = std::min<int32_t>(32, pl.rows_per_cta);
-    int64_t stage_bytes = 64 * 1024;
-    int64_t max_stages = 4;
-    // MI_CUDA_GEMV_WIDE="rows,stage_kb,stages" overrides the wide-row stage
-    // shape (for tuning sweeps; values are clamped to valid ones).
+    int mode = 0, ov_a = 0, ov_kb = 0;
     if (const char* e = std::getenv("MI_CUDA_GEMV_WIDE")) {
-      int r = 0, kb = 0, st = 0;
-      if (std::sscanf(e, "%d,%d,%d", &r, &kb, &st) == 3 && r > 0 && kb > 0 && st > 0) {
-        pl.stage_rows = std::min<int32_t>(pl.rows_per_cta, std::max(4, std::min(32, r / 4 * 4)));
-        stage_bytes = (int64_t)kb * 1024;
-        max_stages = st;
+      int m = 0, x = 0, kb = 0;
+      if (std::sscanf(e, "%d,%d,%d", &m, &x, &kb) == 3 && (m == 0 || m == 8) && x > 0 && kb >= 0) {
+        mode = m;
+        ov_a = x;
+        ov_kb = kb;
       }
     }
+    pl.stage_x = 1;
+    // Narrow CTAs of moderately wide rows (the 0.5B FFN down projection) keep
+    // the shared-stage kernel.
+    if (!std::getenv("MI_CUDA_GEMV_WIDE") && pl.rows_per_cta < 16 && nb < 256) mode = 8;
+    if (mode == 0) {
+      pl.tpr = 0;
+      pl.stage_rows = 4;
+      const int64_t active = std::min<int64_t>(8, (pl.rows_per_cta + 3) / 4);
+      const int64_t S = ov_a > 0 ? std::min(ov_a, 4) : 3;
+      for (;;) {
+        const int64_t fixed = (int64_t)gemv_smem(k, pl.rows_per_cta, 4, 0, pro, pl.stage_x, 2).total;
+        const int64_t per_warp = ((int64_t)limit - fixed) / active;
+        int64_t kc = (per_warp / (S * 136) - 1) & ~1;  // 136 B per block, 128-byte stage rounding
+        if (ov_kb > 0) kc = std::min<int64_t>(kc, ((int64_t)ov_kb * 1024 / 136) & ~1);
+        kc = std::max<int64_t>(2, std::min<int64_t>(nb, kc));
+        pl.kc = (int32_t)kc;
+        pl.n_chunks = (int32_t)((nb + kc - 1) / kc);
+        pl.n_stages = (int32_t)(active * S);
+        pl.smem = gemv_smem(k, pl.rows_per_cta, 4, pl.n_stages, pro, pl.stage_x, pl.kc).total;
+        if (pl.smem <= limit || !(pl.stage_x && pro == PRO_QUANT)) break;
+        pl.stage_x = 0;  // very wide K: quantize from global
+      }
+      return pl;
+    }
+    pl.tpr = 8;
+    pl.stage_rows = std::min<int32_t>(pl.rows_per_cta, std::max(4, std::min(32, (ov_a > 0 ? ov_a : 32) / 4 * 4)));
+    const int64_t stage_bytes = (ov_kb > 0 ? ov_kb : 64) * 1024;
     int64_t kc = std::min<int64_t>(nb, (stage_bytes / (pl.stage_rows * 34)) & ~1);
     if (kc < 2) kc = 2;
-    pl.stage_x = 1;
     for (;;) {
       pl.kc = (int32_t)kc;
       pl.n_chunks = (int32_t)((nb + kc - 1) / kc);
       const int64_t tiles = (int64_t)(pl.rows_per_cta + pl.stage_rows - 1) / pl.stage_rows * pl.n_chunks;
-      pl.n_stages = (int32_t)std::min<int64_t>(tiles, max_stages);
+      pl.n_stages = (int32_t)std::min<int64_t>(tiles, 4);
       for (;;) {
         pl.smem = gemv_smem(k, pl.rows_per_cta, pl.stage_rows, pl.n_stages, pro, pl.stage_x, pl.kc).total;
         if (pl.smem <= limit || pl.n_stages <= 2) break;
@@ -592,8 +680,10 @@ cudaError_t prepare_kernels() {
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   if (e == cudaSuccess) e = set_gemv_smem<8, false>(optin);
   if (e == cudaSuccess) e = set_gemv_smem<2, false>(optin);
+  if (e == cudaSuccess) e = set_gemv_smem<0, false>(optin);
   if (e == cudaSuccess) e = set_gemv_smem<8, true>(optin);
   if (e == cudaSuccess) e = set_gemv_smem<2, true>(optin);
+  if (e == cudaSuccess) e = set_gemv_smem<0, true>(optin);
   if (e == cudaSuccess) e = prepare_attn_kernels(optin);
   return e;
 }
@@ -621,9 +711,12 @@ cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& plan, cudaStream_t 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (tp)
+  if (tp) {
+    if (plan.tpr == 0) return cudaLaunchKernelEx(&cfg, gemv_q8_kernel<256, 0, true>, q);
     return plan.tpr == 2 ? cudaLaunchKernelEx(&cfg, gemv_q8_kernel<256, 2, true>, q)
                          : cudaLaunchKernelEx(&cfg, gemv_q8_kernel<256, 8, true>, q);
+  }
+  if (plan.tpr == 0) return cudaLaunchKernelEx(&cfg, gemv_q8_kernel<256, 0, false>, q);
   if (plan.tpr == 2) return cudaLaunchKernelEx(&cfg, gemv_q8_kernel<256, 2, false>, q);
   return cudaLaunchKernelEx(&cfg, gemv_q8_kernel<256, 8, false>, q);
 }
