@@ -685,6 +685,7 @@ cudaError_t prepare_kernels() {
   if (e == cudaSuccess) e = set_gemv_smem<2, true>(optin);
   if (e == cudaSuccess) e = set_gemv_smem<0, true>(optin);
   if (e == cudaSuccess) e = prepare_attn_kernels(optin);
+  if (e == cudaSuccess) e = prepare_gemm_kernel();
   return e;
 }
 
@@ -766,7 +767,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnParams p) {
     }
     n_kv = n_past + 1;
   } else {
-    n_kv = p.n_kv_fixed;
+    n_kv = p.n_kv_fixed + (int)blockIdx.y;  // batched queries: query t sees n_kv_fixed + t keys
     n_past = n_kv - 1;
   }
   // Rows [c0, c0 + rows) of the cache into the K / V chunk buffers; in executor
@@ -845,7 +846,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnParams p) {
         Vs[(size_t)n_past * D + i] = vr[i];
       }
   } else {
-    for (int i = tid; i < D; i += NT) qr[i] = p.q_rot[(size_t)h * D + i];
+    for (int i = tid; i < D; i += NT) qr[i] = p.q_rot[((size_t)blockIdx.y * p.n_head + h) * D + i];
     load_k(0, rows0);
     load_v(0, rows0);
   }
@@ -925,8 +926,16 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnParams p) {
   }
   trace_mark(p.trace, p.trace_slot, 7);
   trace_mark(p.trace, p.trace_slot, 3);
-  if (tid < D && p.out) p.out[(size_t)h * D + tid] = acc;
-  if (p.act_out && tid < D) {
+  if (tid < D && p.out) p.out[((size_t)blockIdx.y * p.n_head + h) * D + tid] = acc;
+  if (p.act_qs && tid < D) {
+    // Batched queries: this head's outputs quantized into row blockIdx.y of
+    // the split Q8_0_ACT layout (the O projection's input).
+    float d;
+    const int8_t q = quantize_lane(acc, &d);
+    const size_t row = (size_t)blockIdx.y * p.n_head * D;
+    p.act_qs[row + (size_t)h * D + tid] = q;
+    if (lane == 0) p.act_d[(row + (size_t)h * D + tid) >> 5] = d;
+  } else if (p.act_out && tid < D) {
     // The O projection's quantize node (src/ops_cpu.cpp:462-479) for this head's
     // outputs: warp w holds block h*D/32 + w of the concatenated heads.
     float d;
@@ -964,11 +973,13 @@ cudaError_t prepare_attn_kernels(int optin) {
 }
 
 cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t s, bool pdl,
-                               bool tp) {
+                               bool tp, int32_t n_queries) {
   AttnParams q = p;
-  // Positions the scores may need: n_ctx in executor mode, n_kv otherwise.
-  const int64_t max_kv = exec_mode ? p.n_ctx : p.n_kv_fixed;
+  // Positions the scores may need: n_ctx in executor mode, n_kv otherwise
+  // (of the last query when several are batched).
+  const int64_t max_kv = exec_mode ? p.n_ctx : p.n_kv_fixed + std::max(1, n_queries) - 1;
   q.scores_in_smem = max_kv <= kScoresSmemMax ? 1 : 0;
+  if (n_queries > 1 && (exec_mode || !q.scores_in_smem)) return cudaErrorInvalidValue;
   const int64_t sc_bytes = q.scores_in_smem ? ((max_kv * 4 + 15) / 16 * 16 + kChainSlackBytes) : 0;
   const int64_t row_bytes = (int64_t)(2 * p.head_dim + 1) * 4;
   int64_t kt = (kAttnSmemBudget - sc_bytes) / row_bytes;
@@ -976,7 +987,7 @@ cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t
   if (kt < 32) kt = 32;
   q.kv_tile = (int32_t)kt;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)p.n_head);
+  cfg.gridDim = dim3((unsigned)p.n_head, (unsigned)std::max(1, n_queries));
   cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = (size_t)(kt * row_bytes + sc_bytes);
   cfg.stream = s;
@@ -987,7 +998,7 @@ cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t
   cfg.numAttrs = pdl ? 1 : 0;
   if (exec_mode && tp) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<true, false, true>, q);
   if (exec_mode) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<true, false, false>, q);
-  if (q.scores_in_smem && p.n_kv_fixed >= kSpecSumMin)
+  if (q.scores_in_smem && max_kv >= kSpecSumMin)
     return cudaLaunchKernelEx(&cfg, attn_decode_kernel<false, true, false>, q);
   return cudaLaunchKernelEx(&cfg, attn_decode_kernel<false, false, false>, q);
 }

@@ -133,9 +133,60 @@ struct AttnParams {
   int32_t trace_slot;
   const uint64_t* qkv_ll;  // tensor parallelism: q | k | v as exchange words (instead of qkv)
   const uint32_t* epoch;
+  // Batched queries (op mode, gridDim.y = T): query t uses q_rot + t*n_head*hd,
+  // n_kv = n_kv_fixed + t, and writes its outputs at row t.
+  int8_t* act_qs;  // optional: output quantized to the split Q8_0_ACT layout (row n_head*hd bytes)
+  float* act_d;
 };
 cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t s, bool pdl,
-                               bool tp = false);
+                               bool tp = false, int32_t n_queries = 1);
+
+// ---------------------------------------------------------------------------
+// Batched prefill (prefill.cu)
+// ---------------------------------------------------------------------------
+// Exact Q8_0 GEMM over M tokens: out[t * out_stride + r] = dot(W row r, act t)
+// (+ bias[r] / + resid[t * out_stride + r]); EPI_SILU_GATEUP_Q writes the
+// quantized silu(gate) * up activation instead. Activations in the split
+// Q8_0_ACT layout: quants [M][act_stride] bytes, scales [M][act_stride / 32].
+struct GemmParams {
+  const uint8_t* w;
+  int64_t K, N, n_pad;
+  const int8_t* act_qs;
+  const float* act_d;
+  int64_t act_stride;
+  int64_t M;
+  int32_t epi;
+  const float* bias;
+  const float* resid;
+  float* out;
+  int64_t out_stride;
+  int8_t* q_out;  // EPI_SILU_GATEUP_Q: split Q8_0_ACT rows of q_stride bytes
+  float* d_out;
+  int64_t q_stride;
+  ExpTab et;
+};
+cudaError_t prepare_gemm_kernel();
+cudaError_t launch_gemm(const GemmParams& p, cudaStream_t s);
+
+// Per token: [embedding lookup (x_out),] [rms_norm * norm_w,] Q8_0_ACT quantize
+// into the split layout (q_out [t][K], d_out [t][K/32]).
+struct NormQuantParams {
+  int64_t K;
+  const float* x;             // [T][K] when embed == nullptr
+  const uint8_t* embed;       // packed Q8_0 embedding table
+  int64_t embed_npad, embed_rows;
+  const int32_t* tokens;      // [T]
+  float* x_out;               // embedding rows [T][K]
+  const float* norm_w;        // nullptr: quantize only
+  float eps;
+  int8_t* q_out;
+  float* d_out;
+  int32_t* err;
+};
+cudaError_t launch_norm_quant(const NormQuantParams& p, int64_t n_tokens, cudaStream_t s);
+cudaError_t launch_rope_kv(const float* qkv, int64_t row, int32_t head_dim, int32_t n_head,
+                           int32_t n_head_kv, int32_t n_past, int64_t n_tokens, const float2* rope_cs,
+                           float* q_rot, float* cache_k, float* cache_v, cudaStream_t s);
 
 // ---------------------------------------------------------------------------
 // Small ops

@@ -1,0 +1,330 @@
+// Batched prefill: a whole prompt (T tokens) through a layer at once, with the
+// reference's arithmetic per (row, token) unchanged.
+//
+// The reference's batched forward computes every mul_mat element with the same
+// vec_dot as decode (ref src/ops_cpu.cpp:177-268: rows split over threads, the
+// per-row dot per column), its rms_norm / quantize per token row, and causal
+// attention whose masked terms are exact zeros (src/ops_cpu.cpp:304-410); its
+// own test asserts that batched and token-by-token forwards agree bit for bit
+// (tests/test_model_qwen2.cpp:186-288). So the prefill kernels compute, for each
+// token, exactly what the decode kernels compute -- only many tokens per launch:
+//   * gemm_q8_kernel: a 64-row x 32-token tile per CTA; each thread owns 2 rows
+//     x 4 tokens x the 8 AVX2 lane accumulators, blocks in order, so each
+//     (row, token) keeps the decode GEMV's lane chains and hsum order;
+//   * prefill_norm_quant_kernel: per token, [embedding lookup,] rms_norm * w and
+//     the Q8_0_ACT quantizer, written in a split layout (quants, then scales);
+//   * prefill_rope_kv_kernel: per token, RoPE of q and k and the KV-cache rows;
+//   * attention: the decode attention kernel, one CTA per (head, query), with
+//     n_kv = n_past + t + 1 for query t.
+#include <algorithm>
+
+#include "mi_device.cuh"
+
+namespace mi {
+
+namespace {
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Exact Q8_0 GEMM: out[t][r] = dot(W row r, act row t) for a 64 x 32 tile.
+// ---------------------------------------------------------------------------
+constexpr int kGemmBN = 64;  // weight rows per CTA (16 groups of 4)
+constexpr int kGemmBM = 32;  // tokens per CTA
+constexpr int kGemmKB = 16;  // 32-element blocks per stage
+constexpr int kGemmStages = 3;
+constexpr int kGemmWStride = kGemmKB * 128 + 16;  // bytes per group in a stage (padded)
+
+struct GemmSmem {
+  static constexpr int wq = 0;
+  static constexpr int wd = wq + 16 * kGemmWStride;
+  static constexpr int aq = wd + 16 * kGemmKB * 8;
+  static constexpr int ad = aq + kGemmBM * kGemmKB * 32;
+  static constexpr int stage = ad + kGemmBM * kGemmKB * 4;
+  static constexpr int res = kGemmStages * stage;  // [64 rows][32 tokens] floats (gate/up epilogue)
+  static constexpr int total = res + kGemmBN * kGemmBM * 4;
+};
+
+__global__ void __launch_bounds__(256, 1) gemm_q8_kernel(const GemmParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t K = p.K;
+  const int nb = (int)(K >> 5);
+  const int64_t R0 = (int64_t)blockIdx.x * kGemmBN, T0 = (int64_t)blockIdx.y * kGemmBM;
+  const int64_t G0 = R0 >> 2;
+  const int64_t n_groups = p.n_pad >> 2;
+  const uint8_t* wq = p.w;
+  const uint8_t* wd = p.w + p.n_pad * K;
+  const int n_k = (nb + kGemmKB - 1) / kGemmKB;
+
+  auto load_stage = [&](int kt) {
+    uint8_t* st = smem + (kt % kGemmStages) * GemmSmem::stage;
+    const int c0 = kt * kGemmKB, kbb = min(kGemmKB, nb - c0);
+    // weight quants: 16 groups x kbb blocks x 128 B, 16-byte pieces
+    for (int c = tid; c < 16 * kbb * 8; c += 256) {
+      const int g = c / (kbb * 8), off = c - g * (kbb * 8);
+      if (G0 + g < n_groups)
+        cp_async16(st + GemmSmem::wq + g * kGemmWStride + off * 16,
+                   wq + (G0 + g) * 4 * K + (int64_t)c0 * 128 + off * 16);
+    }
+    // weight scales: 4 fp16 per group and block (8 B)
+    for (int c = tid; c < 16 * kbb; c += 256) {
+      const int g = c / kbb, i = c - g * kbb;
+      if (G0 + g < n_groups)
+        cp_async8(st + GemmSmem::wd + (g * kGemmKB + i) * 8, wd + ((G0 + g) * nb + c0 + i) * 8);
+    }
+    // activation quants: 32 tokens x kbb x 32 B
+    for (int c = tid; c < kGemmBM * kbb * 2; c += 256) {
+      const int t = c / (kbb * 2), off = c - t * (kbb * 2);
+      if (T0 + t < p.M)
+        cp_async16(st + GemmSmem::aq + t * kGemmKB * 32 + off * 16,
+                   p.act_qs + (T0 + t) * p.act_stride + (int64_t)c0 * 32 + off * 16);
+    }
+    // activation scales
+    for (int c = tid; c < kGemmBM * kbb; c += 256) {
+      const int t = c / kbb, i = c - t * kbb;
+      if (T0 + t < p.M)
+        cp_async4(st + GemmSmem::ad + (t * kGemmKB + i) * 4, p.act_d + (T0 + t) * (p.act_stride >> 5) + c0 + i);
+    }
+  };
+
+  // thread tile: rows 2l, 2l+1 (group l/2, rows 2(l&1), 2(l&1)+1 of it) x
+  // tokens 4w..4w+3, 8 lane accumulators each
+  float acc[2][4][8];
+#pragma unroll
+  for (int r = 0; r < 2; r++)
+#pragma unroll
+    for (int t = 0; t < 4; t++)
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc[r][t][j] = 0.0f;
+  const int g = lane >> 1, pr = (lane & 1) * 2;
+
+#pragma unroll
+  for (int s = 0; s < kGemmStages - 1; s++) {
+    if (s < n_k) load_stage(s);
+    cp_async_commit();
+  }
+  for (int kt = 0; kt < n_k; kt++) {
+    cp_async_wait<kGemmStages - 2>();
+    __syncthreads();
+    if (kt + kGemmStages - 1 < n_k) load_stage(kt + kGemmStages - 1);
+    cp_async_commit();
+    const uint8_t* st = smem + (kt % kGemmStages) * GemmSmem::stage;
+    const int kbb = min(kGemmKB, nb - kt * kGemmKB);
+    const uint8_t* wrow = st + GemmSmem::wq + g * kGemmWStride + pr * 32;
+    const __half* wsc = (const __half*)(st + GemmSmem::wd) + g * kGemmKB * 4 + pr;
+    const uint8_t* abase = st + GemmSmem::aq + (warp * 4) * kGemmKB * 32;
+    const float* adb = (const float*)(st + GemmSmem::ad) + (warp * 4) * kGemmKB;
+    for (int i = 0; i < kbb; i++) {
+      int w[2][8];
+      {
+        const uint4 a0 = *(const uint4*)(wrow + i * 128);
+        const uint4 a1 = *(const uint4*)(wrow + i * 128 + 16);
+        const uint4 b0 = *(const uint4*)(wrow + i * 128 + 32);
+        const uint4 b1 = *(const uint4*)(wrow + i * 128 + 48);
+        w[0][0] = (int)a0.x; w[0][1] = (int)a0.y; w[0][2] = (int)a0.z; w[0][3] = (int)a0.w;
+        w[0][4] = (int)a1.x; w[0][5] = (int)a1.y; w[0][6] = (int)a1.z; w[0][7] = (int)a1.w;
+        w[1][0] = (int)b0.x; w[1][1] = (int)b0.y; w[1][2] = (int)b0.z; w[1][3] = (int)b0.w;
+        w[1][4] = (int)b1.x; w[1][5] = (int)b1.y; w[1][6] = (int)b1.z; w[1][7] = (int)b1.w;
+      }
+      const float sw0 = __half2float(wsc[i * 4]), sw1 = __half2float(wsc[i * 4 + 1]);
+#pragma unroll
+      for (int t = 0; t < 4; t++) {
+        const uint4 q0 = *(const uint4*)(abase + t * kGemmKB * 32 + i * 32);
+        const uint4 q1 = *(const uint4*)(abase + t * kGemmKB * 32 + i * 32 + 16);
+        const int a[8] = {(int)q0.x, (int)q0.y, (int)q0.z, (int)q0.w,
+                          (int)q1.x, (int)q1.y, (int)q1.z, (int)q1.w};
+        const float da = adb[t * kGemmKB + i];
+        const float d0 = __fmul_rn(sw0, da), d1 = __fmul_rn(sw1, da);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          acc[0][t][j] = __fmaf_rn(__int2float_rn(__dp4a(w[0][j], a[j], 0)), d0, acc[0][t][j]);
+          acc[1][t][j] = __fmaf_rn(__int2float_rn(__dp4a(w[1][j], a[j], 0)), d1, acc[1][t][j]);
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+
+  // hsum_ps order per (row, token): ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7))
+  float dot[2][4];
+#pragma unroll
+  for (int r = 0; r < 2; r++)
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+      const float* a = acc[r][t];
+      dot[r][t] = __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[4]), __fadd_rn(a[1], a[5])),
+                            __fadd_rn(__fadd_rn(a[2], a[6]), __fadd_rn(a[3], a[7])));
+    }
+
+  if (p.epi == EPI_SILU_GATEUP_Q) {
+    // The tile's 64 packed rows are the gate/up rows of one 32-element block
+    // of the FFN activation: silu(gate) * up per element, then the down
+    // projection's quantize node, per token.
+    float* res = (float*)(smem + GemmSmem::res);
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < 2; r++)
+#pragma unroll
+      for (int t = 0; t < 4; t++) res[(2 * lane + r) * kGemmBM + warp * 4 + t] = dot[r][t];
+    __syncthreads();
+    const int64_t blk = R0 >> 6;
+    const int e = lane;  // activation element within the block
+    const int lr = (e >> 2) * 8 + (e & 3);
+    for (int t = warp; t < kGemmBM; t += 8) {
+      const int64_t tok = T0 + t;
+      if (tok >= p.M) break;
+      const float v = __fmul_rn(silu_exact(res[lr * kGemmBM + t], p.et), res[(lr + 4) * kGemmBM + t]);
+      float d;
+      const int8_t q = quantize_lane(v, &d);
+      p.q_out[tok * p.q_stride + blk * 32 + e] = q;
+      if (e == 0) p.d_out[tok * (p.q_stride >> 5) + blk] = d;
+    }
+    return;
+  }
+#pragma unroll
+  for (int t = 0; t < 4; t++) {
+    const int64_t tok = T0 + warp * 4 + t;
+    if (tok >= p.M) continue;
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+      const int64_t row = R0 + 2 * lane + r;
+      if (row >= p.N) continue;
+      float v = dot[r][t];
+      if (p.epi == EPI_BIAS) v = __fadd_rn(v, p.bias[row]);
+      else if (p.epi == EPI_RESID) v = __fadd_rn(p.resid[tok * p.out_stride + row], v);
+      p.out[tok * p.out_stride + row] = v;
+    }
+  }
+}
+
+cudaError_t prepare_gemm_kernel() {
+  return cudaFuncSetAttribute(gemm_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              GemmSmem::total);
+}
+
+cudaError_t launch_gemm(const GemmParams& p, cudaStream_t s) {
+  if (p.M <= 0) return cudaSuccess;
+  if (p.K % 32 != 0 || (p.epi == EPI_SILU_GATEUP_Q && p.n_pad % kGemmBN != 0)) return cudaErrorInvalidValue;
+  dim3 grid((unsigned)((p.n_pad + kGemmBN - 1) / kGemmBN), (unsigned)((p.M + kGemmBM - 1) / kGemmBM));
+  gemm_q8_kernel<<<grid, 256, GemmSmem::total, s>>>(p);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Per-token [embedding,] rms_norm * w and Q8_0_ACT quantize (split layout).
+// One CTA per token: the same steps as the GEMV prologue of the decode path.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) prefill_norm_quant_kernel(const NormQuantParams p) {
+  extern __shared__ __align__(16) float xs[];  // [K] values, then [K + slack] squares
+  __shared__ __align__(16) uint8_t spec[spec_sum_scratch_bytes(8, 4)];
+  __shared__ float scale_sh;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t t = blockIdx.x, K = p.K;
+  const int nb = (int)(K >> 5);
+  float* sq = xs + K;
+  if (p.embed) {
+    int tok = p.tokens[t];
+    if (tok < 0 || tok >= p.embed_rows) {
+      if (tid == 0) atomicExch(p.err, 1 /* MI_CUDA_ERR_ARG */);
+      tok = 0;
+    }
+    for (int64_t k = tid; k < K; k += 256) {
+      const int64_t b = k >> 5;
+      const float v = __fmul_rn((float)packed_qs(p.embed, K, tok, b)[k & 31],
+                                packed_scale(p.embed, K, p.embed_npad, tok, b));
+      xs[k] = v;
+      p.x_out[t * K + k] = v;
+    }
+  } else {
+    for (int64_t k = tid; k < K; k += 256) xs[k] = p.x[t * K + k];
+  }
+  __syncthreads();
+  float scale = 1.0f;
+  if (p.norm_w) {
+    for (int64_t k = tid; k < K; k += 256) sq[k] = __fmul_rn(xs[k], xs[k]);
+    __syncthreads();
+    const float ss = K <= 1024 ? spec_ordered_sum<256, 2>(sq, (int)K, spec)
+                               : spec_ordered_sum<256, 4>(sq, (int)K, spec);
+    if (tid == 0) scale_sh = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), p.eps)));
+    __syncthreads();
+    scale = scale_sh;
+  }
+  for (int b = warp; b < nb; b += 8) {
+    const int64_t k = (int64_t)b * 32 + lane;
+    const float v = p.norm_w ? __fmul_rn(__fmul_rn(xs[k], scale), p.norm_w[k]) : xs[k];
+    float d;
+    p.q_out[t * K + k] = quantize_lane(v, &d);
+    if (lane == 0) p.d_out[t * nb + b] = d;
+  }
+}
+
+cudaError_t launch_norm_quant(const NormQuantParams& p, int64_t n_tokens, cudaStream_t s) {
+  if (n_tokens <= 0) return cudaSuccess;
+  const size_t smem = (size_t)(2 * p.K) * 4 + kChainSlackBytes;
+  if (smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute(prefill_norm_quant_kernel,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  prefill_norm_quant_kernel<<<(unsigned)n_tokens, 256, smem, s>>>(p);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Per-token NEOX RoPE of q and k (src/ops_cpu.cpp:270-302) and the KV-cache
+// append (MI_OP_CPY, src/ops_cpu.cpp:446-460) at positions n_past + t.
+// qkv rows are [q (n_head*hd) | k (n_head_kv*hd) | v (n_head_kv*hd)].
+// ---------------------------------------------------------------------------
+__global__ void prefill_rope_kv_kernel(const float* qkv, int64_t row, int32_t head_dim, int32_t n_head,
+                                       int32_t n_head_kv, int32_t n_past, const float2* rope_cs,
+                                       float* q_rot, float* cache_k, float* cache_v) {
+  const int64_t t = blockIdx.x;
+  const int half = head_dim >> 1;
+  const float* src = qkv + t * row;
+  const float2* cs = rope_cs + (int64_t)(n_past + t) * half;
+  const int nq = n_head * half, nk = n_head_kv * half;
+  for (int e = threadIdx.x; e < nq + nk; e += blockDim.x) {
+    const bool isq = e < nq;
+    const int ee = isq ? e : e - nq;
+    const int h = ee / half, i = ee - h * half;
+    const float* x = src + (isq ? 0 : (int64_t)n_head * head_dim) + (int64_t)h * head_dim;
+    const float2 c = cs[i];
+    const float x0 = x[i], x1 = x[i + half];
+    const float y0 = __fsub_rn(__fmul_rn(x0, c.x), __fmul_rn(x1, c.y));
+    const float y1 = __fadd_rn(__fmul_rn(x0, c.y), __fmul_rn(x1, c.x));
+    float* d = isq ? q_rot + (t * n_head + h) * head_dim
+                   : cache_k + ((int64_t)(n_past + t) * n_head_kv + h) * head_dim;
+    d[i] = y0;
+    d[i + half] = y1;
+  }
+  const int kvd = n_head_kv * head_dim;
+  const float* v = src + (int64_t)(n_head + n_head_kv) * head_dim;
+  for (int e = threadIdx.x; e < kvd; e += blockDim.x) cache_v[(int64_t)(n_past + t) * kvd + e] = v[e];
+}
+
+cudaError_t launch_rope_kv(const float* qkv, int64_t row, int32_t head_dim, int32_t n_head,
+                           int32_t n_head_kv, int32_t n_past, int64_t n_tokens, const float2* rope_cs,
+                           float* q_rot, float* cache_k, float* cache_v, cudaStream_t s) {
+  if (n_tokens <= 0) return cudaSuccess;
+  prefill_rope_kv_kernel<<<(unsigned)n_tokens, 256, 0, s>>>(qkv, row, head_dim, n_head, n_head_kv, n_past,
+                                                            rope_cs, q_rot, cache_k, cache_v);
+  return cudaGetLastError();
+}
+
+}  // namespace mi

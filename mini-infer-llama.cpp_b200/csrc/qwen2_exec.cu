@@ -132,6 +132,15 @@ struct mi_cuda_kv_cache {
   uint32_t* epoch = nullptr;
   GemvPlan plan_qkv{}, plan_o{}, plan_gu{}, plan_down{}, plan_head{};
   cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+  // Batched-prefill workspace, allocated on first use and grown to the largest
+  // batch: residual streams X / X2 [T][E], q|k|v [T][E + 2kvd], rotated q
+  // [T][E], the split Q8_0_ACT inputs of the E-wide and FF-wide GEMMs, and
+  // (only when every row's logits are requested) logits [T][n_vocab].
+  uint8_t* pbuf = nullptr;
+  int64_t pcap = 0, plog_cap = 0;
+  float *pX = nullptr, *pX2 = nullptr, *pQKV = nullptr, *pQR = nullptr, *pLogits = nullptr;
+  int8_t *pAqE = nullptr, *pAqF = nullptr;
+  float *pAdE = nullptr, *pAdF = nullptr;
 };
 
 namespace {
@@ -655,6 +664,240 @@ int capture(mi_cuda_kv_cache* kv, bool with_head, cudaGraphExec_t* out, int32_t*
   return MI_CUDA_OK;
 }
 
+// Workspace for a batch of n tokens (every row's logits when all_logits).
+int ensure_prefill_ws(mi_cuda_kv_cache* kv, int64_t n, bool all_logits) {
+  const mi_cuda_qwen2_hparams& hp = kv->model->hp;
+  const int64_t E = hp.n_embd, FF = hp.n_ff, kvd = (int64_t)hp.n_head_kv * hp.head_dim;
+  if (n > kv->pcap) {
+    CK(cudaStreamSynchronize(kv->stream));
+    if (kv->pbuf) CK(cudaFree(kv->pbuf));
+    kv->pbuf = nullptr;
+    kv->pcap = 0;
+    size_t off = 0;
+    auto slot = [&](size_t b) {
+      const size_t o = off;
+      off += a256(b);
+      return o;
+    };
+    const size_t oX = slot(n * E * 4), oX2 = slot(n * E * 4), oQKV = slot(n * (E + 2 * kvd) * 4),
+                 oQR = slot(n * E * 4), oAqE = slot(n * E), oAdE = slot(n * (E / 32) * 4), oAqF = slot(n * FF),
+                 oAdF = slot(n * (FF / 32) * 4);
+    CK(cudaMalloc(&kv->pbuf, off));
+    kv->pX = (float*)(kv->pbuf + oX);
+    kv->pX2 = (float*)(kv->pbuf + oX2);
+    kv->pQKV = (float*)(kv->pbuf + oQKV);
+    kv->pQR = (float*)(kv->pbuf + oQR);
+    kv->pAqE = (int8_t*)(kv->pbuf + oAqE);
+    kv->pAdE = (float*)(kv->pbuf + oAdE);
+    kv->pAqF = (int8_t*)(kv->pbuf + oAqF);
+    kv->pAdF = (float*)(kv->pbuf + oAdF);
+    kv->pcap = n;
+  }
+  if (all_logits && n > kv->plog_cap) {
+    CK(cudaStreamSynchronize(kv->stream));
+    if (kv->pLogits) CK(cudaFree(kv->pLogits));
+    kv->pLogits = nullptr;
+    kv->plog_cap = 0;
+    CK(cudaMalloc(&kv->pLogits, (size_t)n * hp.n_vocab * 4));
+    kv->plog_cap = n;
+  }
+  return MI_CUDA_OK;
+}
+
+// Enqueues a batched prefill of tokens[n_past .. n_past + n) (already in the
+// device token buffer): every layer for all n tokens at once, then the LM head
+// and greedy argmax for the last token (the StepState must hold pos =
+// n_past + n - 1; the head advances it). With all_logits the logits of every
+// row land in kv->pLogits (rows 0 .. n-2; the last row is kv->logits).
+int enqueue_prefill(mi_cuda_kv_cache* kv, int32_t n, int32_t n_past, bool all_logits) {
+  mi_cuda_model* m = kv->model;
+  const mi_cuda_qwen2_hparams& hp = m->hp;
+  const int64_t E = hp.n_embd, D = hp.head_dim, kvd = (int64_t)hp.n_head_kv * D, FF = hp.n_ff;
+  const int64_t row_qkv = E + 2 * kvd;
+  const ExpTab et = m->ctx->et;
+  int32_t* err = &kv->state->err;
+  const size_t layer_floats = (size_t)2 * kv->n_ctx * kvd;
+  cudaStream_t s = kv->stream;
+  if (int rc = ensure_prefill_ws(kv, n, all_logits)) return rc;
+  for (int l = 0; l < hp.n_layer; l++) {
+    const Layer& L = m->layers[(size_t)l];
+    NormQuantParams nq{};
+    nq.K = E;
+    nq.x = kv->pX;
+    if (l == 0) {
+      nq.embed = m->embed.w;
+      nq.embed_npad = m->embed.npad;
+      nq.embed_rows = hp.n_vocab;
+      nq.tokens = kv->tokens + n_past;
+      nq.x_out = kv->pX;
+    }
+    nq.norm_w = L.attn_norm;
+    nq.eps = hp.rms_eps;
+    nq.q_out = kv->pAqE;
+    nq.d_out = kv->pAdE;
+    nq.err = err;
+    CK(launch_norm_quant(nq, n, s));
+
+    GemmParams g{};
+    g.w = L.qkv.w;
+    g.K = E;
+    g.N = L.qkv.N;
+    g.n_pad = L.qkv.npad;
+    g.act_qs = kv->pAqE;
+    g.act_d = kv->pAdE;
+    g.act_stride = E;
+    g.M = n;
+    g.epi = EPI_BIAS;
+    g.bias = L.bqkv;
+    g.out = kv->pQKV;
+    g.out_stride = row_qkv;
+    g.et = et;
+    CK(launch_gemm(g, s));
+
+    float* ck = kv->cache + (size_t)l * layer_floats;
+    float* cv = ck + (size_t)kv->n_ctx * kvd;
+    CK(launch_rope_kv(kv->pQKV, row_qkv, (int32_t)D, hp.n_head, hp.n_head_kv, n_past, n, kv->rope, kv->pQR,
+                      ck, cv, s));
+
+    AttnParams a{};
+    a.q_rot = kv->pQR;
+    a.cache_k = ck;
+    a.cache_v = cv;
+    a.head_dim = (int32_t)D;
+    a.n_head = hp.n_head;
+    a.n_head_kv = hp.n_head_kv;
+    a.n_kv_fixed = n_past + 1;
+    a.scale = 1.0f / std::sqrt((float)hp.head_dim);
+    a.n_ctx = kv->n_ctx;
+    a.scores = kv->scores;
+    a.scores_stride = kv->n_ctx;
+    if (kv->quant_attn) {
+      a.act_qs = kv->pAqE;  // whole 32-element blocks per head: quantized in the epilogue
+      a.act_d = kv->pAdE;
+    } else {
+      a.out = kv->pX2;  // F32 rows, quantized below (X2 is free until the O projection)
+    }
+    a.et = et;
+    a.err = err;
+    CK(launch_attn_decode(a, false, s, false, false, n));
+    if (!kv->quant_attn) {
+      NormQuantParams aq{};
+      aq.K = E;
+      aq.x = kv->pX2;
+      aq.q_out = kv->pAqE;
+      aq.d_out = kv->pAdE;
+      aq.err = err;
+      CK(launch_norm_quant(aq, n, s));
+    }
+
+    GemmParams o = g;
+    o.w = L.o.w;
+    o.N = L.o.N;
+    o.n_pad = L.o.npad;
+    o.epi = EPI_RESID;
+    o.bias = nullptr;
+    o.resid = kv->pX;
+    o.out = kv->pX2;
+    o.out_stride = E;
+    CK(launch_gemm(o, s));
+
+    nq = NormQuantParams{};
+    nq.K = E;
+    nq.x = kv->pX2;
+    nq.norm_w = L.ffn_norm;
+    nq.eps = hp.rms_eps;
+    nq.q_out = kv->pAqE;
+    nq.d_out = kv->pAdE;
+    nq.err = err;
+    CK(launch_norm_quant(nq, n, s));
+
+    GemmParams gu = g;
+    gu.w = L.gateup.w;
+    gu.N = L.gateup.N;
+    gu.n_pad = L.gateup.npad;
+    gu.epi = EPI_SILU_GATEUP_Q;
+    gu.bias = nullptr;
+    gu.out = nullptr;
+    gu.q_out = kv->pAqF;
+    gu.d_out = kv->pAdF;
+    gu.q_stride = FF;
+    CK(launch_gemm(gu, s));
+
+    GemmParams dn{};
+    dn.w = L.down.w;
+    dn.K = FF;
+    dn.N = L.down.N;
+    dn.n_pad = L.down.npad;
+    dn.act_qs = kv->pAqF;
+    dn.act_d = kv->pAdF;
+    dn.act_stride = FF;
+    dn.M = n;
+    dn.epi = EPI_RESID;
+    dn.resid = kv->pX2;
+    dn.out = kv->pX;
+    dn.out_stride = E;
+    dn.et = et;
+    CK(launch_gemm(dn, s));
+  }
+  if (all_logits && n > 1) {
+    NormQuantParams nq{};
+    nq.K = E;
+    nq.x = kv->pX;
+    nq.norm_w = m->output_norm;
+    nq.eps = hp.rms_eps;
+    nq.q_out = kv->pAqE;
+    nq.d_out = kv->pAdE;
+    nq.err = err;
+    CK(launch_norm_quant(nq, n - 1, s));
+    GemmParams h{};
+    h.w = m->lm_head.w;
+    h.K = E;
+    h.N = m->lm_head.N;
+    h.n_pad = m->lm_head.npad;
+    h.act_qs = kv->pAqE;
+    h.act_d = kv->pAdE;
+    h.act_stride = E;
+    h.M = n - 1;
+    h.epi = EPI_STORE;
+    h.out = kv->pLogits;
+    h.out_stride = hp.n_vocab;
+    h.et = et;
+    CK(launch_gemm(h, s));
+  }
+  // LM head + greedy argmax of the last token (the decode kernel, on row n-1).
+  GemvParams h{};
+  h.w = m->lm_head.w;
+  h.K = E;
+  h.N = m->lm_head.N;
+  h.n_pad = m->lm_head.npad;
+  h.pro = PRO_NORM_QUANT;
+  h.x = kv->pX + (size_t)(n - 1) * E;
+  h.norm_w = m->output_norm;
+  h.eps = hp.rms_eps;
+  h.epi = EPI_ARGMAX;
+  h.out = kv->logits;
+  h.part_val = kv->part_val;
+  h.part_idx = kv->part_idx;
+  h.counter = &kv->state->counter;
+  h.next_token = &kv->state->next_token;
+  h.tokens_rw = kv->tokens;
+  h.tokens_len = kv->n_ctx + 1;
+  h.pos_rw = &kv->state->pos;
+  h.feedback = &kv->state->feedback;
+  h.et = et;
+  h.err = err;
+  CK(launch_gemv(h, kv->plan_head, s, false));
+  return MI_CUDA_OK;
+}
+
+// Batched prefill applies to unsharded models; MI_CUDA_PREFILL=stepwise keeps
+// prompts on the per-position decode graph (for A/B comparisons).
+bool use_batched_prefill(mi_cuda_kv_cache* kv, int32_t n) {
+  if (n < 2 || kv->model->world > 1) return false;
+  const char* e = std::getenv("MI_CUDA_PREFILL");
+  return !(e && std::strcmp(e, "stepwise") == 0);
+}
+
 // The step graphs exist (a sharded model's KV cache gets them at connect).
 int graphs_ready(mi_cuda_kv_cache* kv) {
   if (!kv->g_head || !kv->g_nohead)
@@ -828,6 +1071,8 @@ void mi_cuda_kv_cache_free(mi_cuda_kv_cache* kv) {
   for (int r = 0; r < kMaxRanks; r++)
     if (kv->peer[r] && kv->peer[r] != kv->xbuf) cudaIpcCloseMemHandle(kv->peer[r]);
   if (kv->xbuf) cudaFree(kv->xbuf);
+  if (kv->pbuf) cudaFree(kv->pbuf);
+  if (kv->pLogits) cudaFree(kv->pLogits);
   if (kv->g_head) cudaGraphExecDestroy(kv->g_head);
   if (kv->g_nohead) cudaGraphExecDestroy(kv->g_nohead);
   for (auto& e : kv->ev)
@@ -916,8 +1161,22 @@ int mi_cuda_qwen2_forward(mi_cuda_model* m, mi_cuda_kv_cache* kv, const int32_t*
   *kv->h_state = StepState{};
   kv->h_state->pos = n_past;
   kv->h_state->feedback = 0;
-  CK(cudaMemcpyAsync(kv->state, kv->h_state, sizeof(StepState), cudaMemcpyHostToDevice, kv->stream));
   const size_t V = (size_t)m->hp.n_vocab;
+  if (use_batched_prefill(kv, n_tokens)) {
+    kv->h_state->pos = n_past + n_tokens - 1;
+    CK(cudaMemcpyAsync(kv->state, kv->h_state, sizeof(StepState), cudaMemcpyHostToDevice, kv->stream));
+    const bool all = !last_logits_only && h_logits_out;
+    if (int rc = enqueue_prefill(kv, n_tokens, n_past, all)) return rc;
+    if (h_logits_out) {
+      if (all)
+        CK(cudaMemcpyAsync(h_logits_out, kv->pLogits, (size_t)(n_tokens - 1) * V * 4, cudaMemcpyDeviceToHost,
+                           kv->stream));
+      float* last = h_logits_out + (last_logits_only ? 0 : (size_t)(n_tokens - 1) * V);
+      CK(cudaMemcpyAsync(last, kv->logits, V * 4, cudaMemcpyDeviceToHost, kv->stream));
+    }
+    return check_state_error(kv);
+  }
+  CK(cudaMemcpyAsync(kv->state, kv->h_state, sizeof(StepState), cudaMemcpyHostToDevice, kv->stream));
   for (int32_t t = 0; t < n_tokens; t++) {
     const bool head = !last_logits_only || t == n_tokens - 1;
     CK(cudaGraphLaunch(head ? kv->g_head : kv->g_nohead, kv->stream));
@@ -966,8 +1225,15 @@ int mi_cuda_qwen2_generate(mi_cuda_model* m, mi_cuda_kv_cache* kv, const int32_t
   // The reference loop stops once n_past reaches n_ctx (src/main.cpp:409-423).
   const int32_t n_decode = std::min<int32_t>(n_predict - 1, kv->n_ctx - n_prompt);
   CK(cudaEventRecord(kv->ev[0], kv->stream));
-  for (int32_t t = 0; t + 1 < n_prompt; t++) CK(cudaGraphLaunch(kv->g_nohead, kv->stream));
-  CK(cudaGraphLaunch(kv->g_head, kv->stream));
+  if (use_batched_prefill(kv, n_prompt)) {
+    // the prompt in one batch; its LM head feeds the first token back
+    kv->h_state->pos = n_prompt - 1;
+    CK(cudaMemcpyAsync(kv->state, kv->h_state, sizeof(StepState), cudaMemcpyHostToDevice, kv->stream));
+    if (int rc2 = enqueue_prefill(kv, n_prompt, 0, false)) return rc2;
+  } else {
+    for (int32_t t = 0; t + 1 < n_prompt; t++) CK(cudaGraphLaunch(kv->g_nohead, kv->stream));
+    CK(cudaGraphLaunch(kv->g_head, kv->stream));
+  }
   CK(cudaEventRecord(kv->ev[1], kv->stream));
   for (int32_t i = 0; i < n_decode; i++) CK(cudaGraphLaunch(kv->g_head, kv->stream));
   CK(cudaEventRecord(kv->ev[2], kv->stream));

@@ -168,3 +168,48 @@ def test_7b_widths_bitexact(mc, model_path):
     ref.close()
     kv.free()
     model.free()
+
+
+@pytest.mark.parametrize("shape,seed,fast,n_ctx,n_prompt", [("TINY", 1, False, 64, 40), ("SMALL", 4, False, 256, 97),
+                                                            ("MID7B", 21, True, 128, 33)])
+def test_batched_prefill_bitexact(mc, model_path, shape, seed, fast, n_ctx, n_prompt):
+    """The batched prefill (exact GEMM tiles, per-token norms, one attention
+    CTA per head and query) gives the reference's logits for every prompt row,
+    bit for bit, also when the prompt arrives in two batches, and the KV cache
+    it leaves continues decoding identically."""
+    path = model_path(shape, seed, fast=fast)
+    ref = mi_oracle.ReferenceModel(path, n_ctx=n_ctx, n_threads=os.cpu_count() or 1)
+    model = mc.Qwen2Model(path)
+    kv = mc.KVCache(model, n_ctx)
+    prompt = np.random.default_rng(seed + 100).integers(0, ref.n_vocab, n_prompt).astype(np.int32)
+    want = ref.forward(prompt, 0)
+    got = kv.forward(prompt, 0)
+    assert np.array_equal(bits(got), bits(want))
+    assert kv.last_token() == mc.sample_greedy(want[-1])
+    # two batches (n_past > 0 for the second), last row only
+    cut = n_prompt // 3
+    kv.forward(prompt[:cut], 0, last_logits_only=True)
+    got2 = kv.forward(prompt[cut:], cut, last_logits_only=True)
+    assert np.array_equal(bits(got2[0]), bits(want[-1]))
+    tok = mc.sample_greedy(want[-1])
+    for step in range(3):
+        w = ref.forward([tok], n_prompt + step)
+        g = kv.forward([tok], n_prompt + step)
+        assert np.array_equal(bits(g), bits(w)), f"decode step {step}"
+        tok = mc.sample_greedy(w[0])
+    ref.close()
+    kv.free()
+    model.free()
+
+
+def test_batched_and_stepwise_prefill_agree(mc, model_path, monkeypatch):
+    path = model_path("SMALL", 4)
+    model = mc.Qwen2Model(path)
+    kv = mc.KVCache(model, 256)
+    prompt = np.random.default_rng(5).integers(0, model.n_vocab, 64).astype(np.int32)
+    batched, _, _ = kv.generate(prompt, 40)
+    monkeypatch.setenv("MI_CUDA_PREFILL", "stepwise")
+    stepwise, _, _ = kv.generate(prompt, 40)
+    assert np.array_equal(batched, stepwise)
+    kv.free()
+    model.free()
