@@ -982,9 +982,13 @@ cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t
   if (n_queries > 1 && (exec_mode || !q.scores_in_smem)) return cudaErrorInvalidValue;
   const int64_t sc_bytes = q.scores_in_smem ? ((max_kv * 4 + 15) / 16 * 16 + kChainSlackBytes) : 0;
   const int64_t row_bytes = (int64_t)(2 * p.head_dim + 1) * 4;
-  int64_t kt = (kAttnSmemBudget - sc_bytes) / row_bytes;
+  // Batched queries launch thousands of CTAs: small K/V tiles keep several
+  // of them resident per SM.
+  const int64_t budget = n_queries > 1 ? 40 * 1024 + sc_bytes : kAttnSmemBudget;
+  int64_t kt = (budget - sc_bytes) / row_bytes;
   kt = std::min<int64_t>(256, kt) / 32 * 32;
   if (kt < 32) kt = 32;
+  if (n_queries > 1) kt = std::min<int64_t>(kt, 64);
   q.kv_tile = (int32_t)kt;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.n_head, (unsigned)std::max(1, n_queries));

@@ -184,6 +184,24 @@ struct NormQuantParams {
   int32_t* err;
 };
 cudaError_t launch_norm_quant(const NormQuantParams& p, int64_t n_tokens, cudaStream_t s);
+// Causal attention for T queries at positions n_past + t: one CTA per (KV
+// head, query), n_rep query heads each; output quantized to the split
+// Q8_0_ACT layout (act_qs / act_d, rows of `row` elements) or F32 rows (out).
+struct PrefillAttnParams {
+  const float* q_rot;    // [T][n_head][head_dim]
+  const float* cache_k;  // [n_ctx][n_head_kv][head_dim]
+  const float* cache_v;
+  int32_t head_dim, n_head, n_head_kv, n_rep, n_past;
+  float scale;
+  int64_t row;  // output row length (n_head * head_dim)
+  int8_t* act_qs;
+  float* act_d;
+  float* out;
+  ExpTab et;
+  int32_t sc_stride;  // set by the launcher
+};
+bool prefill_attn_fits(int32_t head_dim, int32_t n_rep, int64_t max_kv);
+cudaError_t launch_attn_prefill(const PrefillAttnParams& p, int64_t n_tokens, cudaStream_t s);
 cudaError_t launch_rope_kv(const float* qkv, int64_t row, int32_t head_dim, int32_t n_head,
                            int32_t n_head_kv, int32_t n_past, int64_t n_tokens, const float2* rope_cs,
                            float* q_rot, float* cache_k, float* cache_v, cudaStream_t s);

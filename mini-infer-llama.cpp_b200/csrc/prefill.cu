@@ -49,6 +49,14 @@ constexpr int kGemmBM = 32;  // tokens per CTA
 constexpr int kGemmKB = 16;  // 32-element blocks per stage
 constexpr int kGemmStages = 3;
 constexpr int kGemmWStride = kGemmKB * 128 + 16;  // bytes per group in a stage (padded)
+// A lane partial p = dp4a(w, a) satisfies |p| <= 4 * 127 * 127 < 2^22. With
+// the accumulator input bits(1.5 * 2^23) the dp4a result is the bit pattern of
+// the float 1.5 * 2^23 + p (exactly: the sum stays in [2^23, 2^24), where
+// floats are the integers), and subtracting 1.5 * 2^23 gives (float)p exactly.
+// This keeps the conversion off the int-to-float unit, whose rate (a quarter
+// of the FMA rate) bounds the GEMM otherwise.
+constexpr int kBiasI = 0x4B400000;
+constexpr float kBiasF = 12582912.0f;
 
 struct GemmSmem {
   static constexpr int wq = 0;
@@ -153,8 +161,10 @@ __global__ void __launch_bounds__(256, 1) gemm_q8_kernel(const GemmParams p) {
         const float d0 = __fmul_rn(sw0, da), d1 = __fmul_rn(sw1, da);
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-          acc[0][t][j] = __fmaf_rn(__int2float_rn(__dp4a(w[0][j], a[j], 0)), d0, acc[0][t][j]);
-          acc[1][t][j] = __fmaf_rn(__int2float_rn(__dp4a(w[1][j], a[j], 0)), d1, acc[1][t][j]);
+          acc[0][t][j] = __fmaf_rn(__fsub_rn(__int_as_float(__dp4a(w[0][j], a[j], kBiasI)), kBiasF), d0,
+                                   acc[0][t][j]);
+          acc[1][t][j] = __fmaf_rn(__fsub_rn(__int_as_float(__dp4a(w[1][j], a[j], kBiasI)), kBiasF), d1,
+                                   acc[1][t][j]);
         }
       }
     }
@@ -324,6 +334,134 @@ cudaError_t launch_rope_kv(const float* qkv, int64_t row, int32_t head_dim, int3
   if (n_tokens <= 0) return cudaSuccess;
   prefill_rope_kv_kernel<<<(unsigned)n_tokens, 256, 0, s>>>(qkv, row, head_dim, n_head, n_head_kv, n_past,
                                                             rope_cs, q_rot, cache_k, cache_v);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Prefill attention: one CTA per (KV head, query t) runs the reference's
+// attention for the n_rep query heads that share the KV head (GQA mapping
+// h = kvh * n_rep + r, src/ops_cpu.cpp:356-410), at n_kv = n_past + t + 1:
+//   scores  s[r][k] = (sum over d, in order, of K[k][d] * q[r][d]) * scale,
+//   softmax max, e = expf(s - max), the denominator as one ordered chain,
+//           p = e * (1 / sum),
+//   out[r][o] = sum over k, in order, of V[k][o] * p[r][k].
+// The K / V tiles are shared by the n_rep heads; each chain is one thread's.
+// ---------------------------------------------------------------------------
+constexpr int kPfKT = 64;  // keys per K / V tile
+
+__global__ void __launch_bounds__(256) attn_prefill_kernel(const PrefillAttnParams p) {
+  extern __shared__ __align__(16) float sm[];
+  __shared__ float mx[8], inv[8];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int kvh = blockIdx.x, t = blockIdx.y;
+  const int D = p.head_dim, R = p.n_rep, HKV = p.n_head_kv, KP = D + 1;
+  const int n_kv = p.n_past + t + 1;
+  const int cap = p.sc_stride;  // score row stride (>= n_kv, a multiple of 4)
+  float* qs = sm;                          // [R][D]
+  float* Ks = qs + R * D;                  // [kPfKT][D + 1]
+  float* Vs = Ks + kPfKT * KP;             // [kPfKT][D]
+  float* sc = Vs + kPfKT * D;              // [R][cap] (+ slack)
+  const size_t rs = (size_t)HKV * D;
+  const float* kb = p.cache_k + (size_t)kvh * D;
+  const float* vb = p.cache_v + (size_t)kvh * D;
+  const int h0 = kvh * R;
+  for (int e = tid; e < R * D; e += 256) qs[e] = p.q_rot[((size_t)t * p.n_head + h0) * D + e];
+  const int n_chunks = (n_kv + kPfKT - 1) / kPfKT;
+  for (int c = 0; c < n_chunks; c++) {
+    const int c0 = c * kPfKT, rows = min(kPfKT, n_kv - c0);
+    __syncthreads();
+    for (int e = tid; e < rows * (D >> 2); e += 256) {
+      const int r = e / (D >> 2), q4 = e - r * (D >> 2);
+      const float4 v = *(const float4*)(kb + (size_t)(c0 + r) * rs + q4 * 4);
+      float* d = Ks + r * KP + q4 * 4;  // padded rows: the per-key dot reads conflict-free
+      d[0] = v.x;
+      d[1] = v.y;
+      d[2] = v.z;
+      d[3] = v.w;
+    }
+    __syncthreads();
+    for (int e = tid; e < R * rows; e += 256) {
+      const int r = e / rows, k = e - r * rows;
+      const float acc = ordered_dot(0.0f, Ks + k * KP, 1, qs + r * D, D);
+      sc[r * cap + c0 + k] = __fmul_rn(acc, p.scale);
+    }
+  }
+  __syncthreads();
+  // softmax: the maximum per head (order-free), expf, the ordered denominator
+  if (warp < R) {
+    float m = -INFINITY;
+    for (int k = lane; k < n_kv; k += 32) m = fmaxf(m, sc[warp * cap + k]);
+    m = warp_max(m);
+    if (lane == 0) mx[warp] = m;
+  }
+  __syncthreads();
+  for (int e = tid; e < R * n_kv; e += 256) {
+    const int r = e / n_kv, k = e - r * n_kv;
+    sc[r * cap + k] = expf_exact(__fsub_rn(sc[r * cap + k], mx[r]), p.et);
+  }
+  __syncthreads();
+  if (warp < R && lane == 0) inv[warp] = __fdiv_rn(1.0f, ordered_sum_smem(sc + warp * cap, n_kv));
+  __syncthreads();
+  for (int e = tid; e < R * n_kv; e += 256) {
+    const int r = e / n_kv, k = e - r * n_kv;
+    sc[r * cap + k] = __fmul_rn(sc[r * cap + k], inv[r]);
+  }
+  // out[r][o]: thread chains (r, o) = (e / D, e % D) for e = tid + 256 c
+  constexpr int kMaxChains = 4;  // R * D <= 1024
+  float acc[kMaxChains] = {0.0f, 0.0f, 0.0f, 0.0f};
+  for (int c = 0; c < n_chunks; c++) {
+    const int c0 = c * kPfKT, rows = min(kPfKT, n_kv - c0);
+    __syncthreads();
+    for (int e = tid; e < rows * (D >> 2); e += 256) {
+      const int r = e / (D >> 2), q4 = e - r * (D >> 2);
+      *(float4*)(Vs + r * D + q4 * 4) = *(const float4*)(vb + (size_t)(c0 + r) * rs + q4 * 4);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kMaxChains; j++) {
+      const int e = tid + 256 * j;
+      if (e < R * D) {
+        const int r = e / D, o = e - r * D;
+        acc[j] = ordered_dot(acc[j], Vs + o, D, sc + r * cap + c0, rows);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kMaxChains; j++) {
+    const int e = tid + 256 * j;
+    if (e >= R * D) break;  // warp-uniform: R * D is a multiple of 32
+    const size_t col = (size_t)h0 * D + e;  // element of the concatenated heads
+    if (p.act_qs) {
+      // the O projection's quantize node, one 32-element block per warp
+      float d;
+      const int8_t q = quantize_lane(acc[j], &d);
+      p.act_qs[(size_t)t * p.row + col] = q;
+      if (lane == 0) p.act_d[((size_t)t * p.row + col) >> 5] = d;
+    } else {
+      p.out[(size_t)t * p.row + col] = acc[j];
+    }
+  }
+}
+
+bool prefill_attn_fits(int32_t head_dim, int32_t n_rep, int64_t max_kv) {
+  const int64_t cap = (max_kv + 3) / 4 * 4;
+  const int64_t smem = ((int64_t)n_rep * head_dim + kPfKT * (head_dim + 1) + kPfKT * head_dim + n_rep * cap) * 4 +
+                       kChainSlackBytes;
+  return n_rep <= 8 && n_rep * head_dim <= 1024 && head_dim % 4 == 0 && smem <= 200 * 1024;
+}
+
+cudaError_t launch_attn_prefill(const PrefillAttnParams& p, int64_t n_tokens, cudaStream_t s) {
+  if (n_tokens <= 0) return cudaSuccess;
+  PrefillAttnParams q = p;
+  const int64_t max_kv = p.n_past + n_tokens;
+  if (!prefill_attn_fits(p.head_dim, p.n_rep, max_kv)) return cudaErrorInvalidValue;
+  if (p.act_qs && (p.n_rep * p.head_dim) % 32 != 0) return cudaErrorInvalidValue;
+  q.sc_stride = (int32_t)((max_kv + 3) / 4 * 4);
+  const size_t smem = (size_t)((int64_t)p.n_rep * p.head_dim + kPfKT * (p.head_dim + 1) + kPfKT * p.head_dim +
+                               (int64_t)p.n_rep * q.sc_stride) * 4 + kChainSlackBytes;
+  cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  attn_prefill_kernel<<<dim3((unsigned)p.n_head_kv, (unsigned)n_tokens), 256, smem, s>>>(q);
   return cudaGetLastError();
 }
 

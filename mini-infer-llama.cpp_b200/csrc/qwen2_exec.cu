@@ -759,28 +759,54 @@ int enqueue_prefill(mi_cuda_kv_cache* kv, int32_t n, int32_t n_past, bool all_lo
     CK(launch_rope_kv(kv->pQKV, row_qkv, (int32_t)D, hp.n_head, hp.n_head_kv, n_past, n, kv->rope, kv->pQR,
                       ck, cv, s));
 
-    AttnParams a{};
-    a.q_rot = kv->pQR;
-    a.cache_k = ck;
-    a.cache_v = cv;
-    a.head_dim = (int32_t)D;
-    a.n_head = hp.n_head;
-    a.n_head_kv = hp.n_head_kv;
-    a.n_kv_fixed = n_past + 1;
-    a.scale = 1.0f / std::sqrt((float)hp.head_dim);
-    a.n_ctx = kv->n_ctx;
-    a.scores = kv->scores;
-    a.scores_stride = kv->n_ctx;
-    if (kv->quant_attn) {
-      a.act_qs = kv->pAqE;  // whole 32-element blocks per head: quantized in the epilogue
-      a.act_d = kv->pAdE;
+    const int32_t n_rep = hp.n_head / hp.n_head_kv;
+    const bool quant_in_attn = (n_rep * D) % 32 == 0;
+    if (prefill_attn_fits((int32_t)D, n_rep, (int64_t)n_past + n)) {
+      PrefillAttnParams pa{};
+      pa.q_rot = kv->pQR;
+      pa.cache_k = ck;
+      pa.cache_v = cv;
+      pa.head_dim = (int32_t)D;
+      pa.n_head = hp.n_head;
+      pa.n_head_kv = hp.n_head_kv;
+      pa.n_rep = n_rep;
+      pa.n_past = n_past;
+      pa.scale = 1.0f / std::sqrt((float)hp.head_dim);
+      pa.row = E;
+      if (quant_in_attn) {
+        pa.act_qs = kv->pAqE;
+        pa.act_d = kv->pAdE;
+      } else {
+        pa.out = kv->pX2;
+      }
+      pa.et = et;
+      CK(launch_attn_prefill(pa, n, s));
     } else {
-      a.out = kv->pX2;  // F32 rows, quantized below (X2 is free until the O projection)
+      AttnParams a{};
+      a.q_rot = kv->pQR;
+      a.cache_k = ck;
+      a.cache_v = cv;
+      a.head_dim = (int32_t)D;
+      a.n_head = hp.n_head;
+      a.n_head_kv = hp.n_head_kv;
+      a.n_kv_fixed = n_past + 1;
+      a.scale = 1.0f / std::sqrt((float)hp.head_dim);
+      a.n_ctx = kv->n_ctx;
+      a.scores = kv->scores;
+      a.scores_stride = kv->n_ctx;
+      if (kv->quant_attn) {
+        a.act_qs = kv->pAqE;  // whole 32-element blocks per head: quantized in the epilogue
+        a.act_d = kv->pAdE;
+      } else {
+        a.out = kv->pX2;  // F32 rows, quantized below (X2 is free until the O projection)
+      }
+      a.et = et;
+      a.err = err;
+      CK(launch_attn_decode(a, false, s, false, false, n));
     }
-    a.et = et;
-    a.err = err;
-    CK(launch_attn_decode(a, false, s, false, false, n));
-    if (!kv->quant_attn) {
+    const bool f32_attn = prefill_attn_fits((int32_t)D, n_rep, (int64_t)n_past + n) ? !quant_in_attn
+                                                                                     : !kv->quant_attn;
+    if (f32_attn) {
       NormQuantParams aq{};
       aq.K = E;
       aq.x = kv->pX2;
