@@ -113,7 +113,9 @@ __device__ __forceinline__ void ll_store(uint64_t* p, uint32_t bits, uint32_t ta
 
 // The value bits of *p once it carries `tag`. Bounded: after kSpinLimit polls
 // it records MI_CUDA_ERR_TIMEOUT in *err, sets `dead` (later waits of the
-// thread then return at once) and returns 0.
+// thread then return at once) and returns 0. It also gives up as soon as it
+// sees *err set by another wait, so a stopped peer costs one time-out per
+// step, not one per kernel.
 __device__ __forceinline__ uint32_t ll_wait(const uint64_t* p, uint32_t tag, int32_t* err, bool& dead) {
   uint64_t v = ll_load(p);
   if ((uint32_t)(v >> 32) == tag) return (uint32_t)v;
@@ -121,6 +123,10 @@ __device__ __forceinline__ uint32_t ll_wait(const uint64_t* p, uint32_t tag, int
   for (uint32_t it = 0; it < kSpinLimit; it++) {
     v = ll_load(p);
     if ((uint32_t)(v >> 32) == tag) return (uint32_t)v;
+    if ((it & 1023u) == 1023u && err && *(volatile int32_t*)err != 0) {
+      dead = true;
+      return 0u;
+    }
   }
   dead = true;
   if (err) atomicExch(err, 5 /* MI_CUDA_ERR_TIMEOUT */);

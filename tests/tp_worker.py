@@ -40,8 +40,31 @@ def gather_logits(kv, model, rows):
     return full
 
 
+def stall_check(kv, rank, out_path):
+    """Rank 1 stops stepping (it launches nothing); rank 0 runs one decode step,
+    whose exchange waits must expire with MI_CUDA_ERR_TIMEOUT in bounded time
+    and leave the process able to report and clean up."""
+    import time
+    dist.barrier()
+    res = None
+    if rank == 0:
+        kv.set_position(np.array([1, 2, 3], dtype=np.int32), 2)
+        t0 = time.time()
+        code = 0
+        try:
+            kv.decode_steps(1)
+            kv.read_tokens(0, 3)
+        except mi_cuda.MiCudaError as e:
+            code = e.code
+        res = {"ok": code == mi_cuda.ERR_TIMEOUT, "code": code, "seconds": time.time() - t0}
+        with open(out_path, "w") as f:
+            json.dump(res, f)
+    dist.barrier()
+
+
 def main():
     shape_name, seed, out_path = sys.argv[1], int(sys.argv[2]), sys.argv[3]
+    mode = sys.argv[4] if len(sys.argv) > 4 else "parity"
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
@@ -57,6 +80,12 @@ def main():
     model = mi_cuda.Qwen2Model(path, device=local, rank=rank, world=world)
     kv = mi_cuda.KVCache(model, n_ctx)
     mi_cuda.tp_connect(kv)
+    if mode == "stall":
+        stall_check(kv, rank, out_path)
+        kv.free()
+        model.free()
+        dist.destroy_process_group()
+        return
     prompt = np.random.default_rng(seed).integers(0, model.n_vocab, 10).astype(np.int32)
 
     # 1. forward with logits (prefill rows, then decode steps)
