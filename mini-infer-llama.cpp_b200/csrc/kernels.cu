@@ -772,23 +772,45 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnParams p) {
   }
   // Rows [c0, c0 + rows) of the cache into the K / V chunk buffers; in executor
   // mode row n_past is this step's and comes from kr / vr instead.
+  // Four 16-byte loads in flight per thread before their shared-memory stores.
   auto load_k = [&](int c0, int rows) {
-    for (int e = tid; e < rows * D4; e += NT) {
-      const int r = e / D4, c = e - r * D4;
-      if (EXEC && c0 + r == n_past) continue;
-      const float4 v = *(const float4*)(kbase + (size_t)(c0 + r) * rs + c * 4);
-      float* d = Ks + (size_t)r * KP + c * 4;
-      d[0] = v.x;
-      d[1] = v.y;
-      d[2] = v.z;
-      d[3] = v.w;
+    const int total = rows * D4;
+    for (int e0 = tid; e0 < total; e0 += 4 * NT) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int e = e0 + u * NT, r = e / D4, c = e - r * D4;
+        if (e < total && !(EXEC && c0 + r == n_past))
+          v[u] = *(const float4*)(kbase + (size_t)(c0 + r) * rs + c * 4);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int e = e0 + u * NT, r = e / D4, c = e - r * D4;
+        if (e < total && !(EXEC && c0 + r == n_past)) {
+          float* d = Ks + (size_t)r * KP + c * 4;
+          d[0] = v[u].x;
+          d[1] = v[u].y;
+          d[2] = v[u].z;
+          d[3] = v[u].w;
+        }
+      }
     }
   };
   auto load_v = [&](int c0, int rows) {
-    for (int e = tid; e < rows * D4; e += NT) {
-      const int r = e / D4, c = e - r * D4;
-      if (EXEC && c0 + r == n_past) continue;
-      *(float4*)(Vs + (size_t)r * D + c * 4) = *(const float4*)(vbase + (size_t)(c0 + r) * rs + c * 4);
+    const int total = rows * D4;
+    for (int e0 = tid; e0 < total; e0 += 4 * NT) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int e = e0 + u * NT, r = e / D4, c = e - r * D4;
+        if (e < total && !(EXEC && c0 + r == n_past))
+          v[u] = *(const float4*)(vbase + (size_t)(c0 + r) * rs + c * 4);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int e = e0 + u * NT, r = e / D4, c = e - r * D4;
+        if (e < total && !(EXEC && c0 + r == n_past)) *(float4*)(Vs + (size_t)r * D + c * 4) = v[u];
+      }
     }
   };
   const int rows0 = min(KT, n_kv);
@@ -947,7 +969,11 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnParams p) {
 }
 
 namespace {
-constexpr int kAttnSmemBudget = 140 * 1024;  // dynamic shared memory per CTA
+constexpr int kAttnSmemBudget = 140 * 1024;  // dynamic shared memory per CTA (op mode)
+// Executor mode: one CTA per head (14 or 28 CTAs), so a larger K/V tile costs
+// no concurrency and keeps every position of a decode step in the tile that is
+// loaded before the dependency wait (192 positions at head_dim 128).
+constexpr int kExecAttnSmemBudget = 210 * 1024;
 constexpr int kScoresSmemMax = 8192;         // scores kept on chip up to this many positions
 }  // namespace
 
@@ -984,7 +1010,7 @@ cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t
   const int64_t row_bytes = (int64_t)(2 * p.head_dim + 1) * 4;
   // Batched queries launch thousands of CTAs: small K/V tiles keep several
   // of them resident per SM.
-  const int64_t budget = n_queries > 1 ? 40 * 1024 + sc_bytes : kAttnSmemBudget;
+  const int64_t budget = n_queries > 1 ? 40 * 1024 + sc_bytes : exec_mode ? kExecAttnSmemBudget : kAttnSmemBudget;
   int64_t kt = (budget - sc_bytes) / row_bytes;
   kt = std::min<int64_t>(256, kt) / 32 * 32;
   if (kt < 32) kt = 32;
