@@ -899,13 +899,8 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnParams p) {
   lmax = warp_max(lmax);
   if (lane == 0) red[warp] = lmax;
   __syncthreads();
-  if (tid == 0) {
-    float m = red[0];
-    for (int w = 1; w < (NT >> 5); w++) m = fmaxf(m, red[w]);
-    sh[0] = m;
-  }
-  __syncthreads();
-  const float mx = sh[0];
+  float mx = red[0];  // every thread reduces the warps' maxima (order-free)
+  for (int w = 1; w < (NT >> 5); w++) mx = fmaxf(mx, red[w]);
   for (int i = tid; i < n_kv; i += NT) sc[i] = expf_exact(__fsub_rn(sc[i], mx), p.et);
   __syncthreads();
   trace_mark(p.trace, p.trace_slot, 5);
@@ -930,8 +925,6 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnParams p) {
   __syncthreads();
   const float inv = sh[1];
   trace_mark(p.trace, p.trace_slot, 6);
-  for (int i = tid; i < n_kv; i += NT) sc[i] = __fmul_rn(sc[i], inv);
-  __syncthreads();
 
   // out[o] = sum_t V[o, kvh, t] * P[t], t ascending (src/ops_cpu.cpp:402-406).
   float acc = 0.0f;
@@ -944,7 +937,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnParams p) {
         for (int i = tid; i < D; i += NT) Vs[(size_t)(n_past - c0) * D + i] = vr[i];
       __syncthreads();
     }
-    if (tid < D) acc = ordered_dot(acc, Vs + tid, D, sc + c0, rows);
+    if (tid < D) acc = ordered_dot_scaled(acc, Vs + tid, D, sc + c0, inv, rows);
   }
   trace_mark(p.trace, p.trace_slot, 7);
   trace_mark(p.trace, p.trace_slot, 3);

@@ -228,6 +228,27 @@ __device__ __forceinline__ float ordered_dot(float acc, const float* v, int vs, 
   return acc;
 }
 
+// ordered_dot with the softmax normalization applied as the terms are used:
+// acc + v[0]*(p[0]*s) + v[vs]*(p[1]*s) + ..., each product rounded separately
+// (the same values as normalizing p first, src/ops_cpu.cpp:338-341, then
+// accumulating, src/ops_cpu.cpp:402-406).
+__device__ __forceinline__ float ordered_dot_scaled(float acc, const float* v, int vs, const float* p, float s,
+                                                   int n) {
+  int t = 0;
+  for (; t + 16 <= n; t += 16) {
+    float a[16], b[16];
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+      a[u] = v[(size_t)(t + u) * vs];
+      b[u] = __fmul_rn(p[t + u], s);
+    }
+#pragma unroll
+    for (int u = 0; u < 16; u++) acc = __fadd_rn(acc, __fmul_rn(a[u], b[u]));
+  }
+  for (; t < n; t++) acc = __fadd_rn(acc, __fmul_rn(v[(size_t)t * vs], __fmul_rn(p[t], s)));
+  return acc;
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -401,11 +401,7 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const PrefillAttnPara
   }
   __syncthreads();
   if (warp < R && lane == 0) inv[warp] = __fdiv_rn(1.0f, ordered_sum_smem(sc + warp * cap, n_kv));
-  __syncthreads();
-  for (int e = tid; e < R * n_kv; e += 256) {
-    const int r = e / n_kv, k = e - r * n_kv;
-    sc[r * cap + k] = __fmul_rn(sc[r * cap + k], inv[r]);
-  }
+  // (the normalization p = e * inv is applied inside the value chains)
   // out[r][o]: thread chains (r, o) = (e / D, e % D) for e = tid + 256 c
   constexpr int kMaxChains = 4;  // R * D <= 1024
   float acc[kMaxChains] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -422,7 +418,7 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const PrefillAttnPara
       const int e = tid + 256 * j;
       if (e < R * D) {
         const int r = e / D, o = e - r * D;
-        acc[j] = ordered_dot(acc[j], Vs + o, D, sc + r * cap + c0, rows);
+        acc[j] = ordered_dot_scaled(acc[j], Vs + o, D, sc + r * cap + c0, inv[r], rows);
       }
     }
   }
