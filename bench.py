@@ -12,9 +12,10 @@ K steps cycles through that position range on the device.
 Printed JSON (rank 0, one line):
   value     device-timed decode tok/s (CUDA events on the executor stream,
             weights resident in HBM; 527 MB of weights per step > 126 MB L2)
-  e2e       the same metric through the public per-token API
-            (mi_cuda_qwen2_forward + host greedy sampling, as the reference's
-            own loop does): token H2D from pinned memory, logits D2H per step
+  e2e       the same metric through the public per-token API: every step the
+            token H2D from pinned memory, mi_cuda_qwen2_forward, and the greedy
+            token D2H (mi_cuda_qwen2_last_token); e2e_logits reads the logits
+            row instead and samples on the host, as the reference's loop does
   roofline  algorithmic bytes per decode step / step time vs the measured
             HBM copy bandwidth (MEASURED_PEAKS.json)
   cpu_baseline  the reference's own CPU decode (compiled from its sources,
@@ -606,26 +607,33 @@ def main():
     peak, peak_kind = load_peaks()
     achieved = total_bytes / (ms / 1e3) / 1e9
 
-    # e2e through the public per-token API (host greedy sampling, like the
-    # reference's loop): H2D token + state from pinned memory, D2H logits
-    pinned = torch.empty((1, hp.n_vocab), dtype=torch.float32, pin_memory=True)
-    out = pinned.numpy()
-    tok = first
+    # e2e through the public per-token API, every step: the token H2D (with the
+    # step state) from pinned memory, mi_cuda_qwen2_forward, and the step's
+    # result D2H -- the greedy token from the device argmax (e2e), or the
+    # logits row sampled on the host as the reference's loop does (e2e_logits).
     lib = mi_cuda.lib()
     n_e2e = max(1, min(args.e2e_steps, PERIOD))
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for i in range(n_e2e):
-        tb = np.array([tok], dtype=np.int32)
-        mi_cuda.check(lib.mi_cuda_qwen2_forward(model.h, kv.h, tb.ctypes.data, 1, N_PROMPT + i, 1,
-                                                out.ctypes.data))
-        tok = mi_cuda.sample_greedy(out[0])
-    e2e_s = time.perf_counter() - t0
-    e2e_tps = n_e2e / e2e_s
-    if dist:
-        t = torch.tensor([e2e_s], device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_tps = n_e2e * world / float(t.item())
+
+    def e2e_run(with_logits: bool) -> float:
+        pinned = torch.empty((1, hp.n_vocab), dtype=torch.float32, pin_memory=True)
+        out = pinned.numpy()
+        tok = first
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for i in range(n_e2e):
+            tb = np.array([tok], dtype=np.int32)
+            mi_cuda.check(lib.mi_cuda_qwen2_forward(model.h, kv.h, tb.ctypes.data, 1, N_PROMPT + i, 1,
+                                                    out.ctypes.data if with_logits else None))
+            tok = mi_cuda.sample_greedy(out[0]) if with_logits else kv.last_token()
+        e2e_s = time.perf_counter() - t0
+        if dist:
+            t = torch.tensor([e2e_s], device=f"cuda:{local}")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_s = float(t.item())
+        return n_e2e * world / e2e_s
+
+    e2e_tps = e2e_run(False)
+    e2e_logits_tps = e2e_run(True)
 
     cpu = None
     parity = None
@@ -653,8 +661,11 @@ def main():
                          "peak_kind": peak_kind,
                          "kernel": f"decode step graph ({kv.kernels_per_step} kernels)",
                          "bytes_per_step": total_bytes / args.steps},
-            "e2e": {"value": e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": 4 + 32,
-                    "d2h_bytes_per_step": hp.n_vocab * 4 + 4, "api": "mi_cuda_qwen2_forward + host greedy"},
+            "e2e": {"value": e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": 4 + 32, "d2h_bytes_per_step": 4 + 4,
+                    "api": "mi_cuda_qwen2_forward (token in) + mi_cuda_qwen2_last_token (greedy token out)"},
+            "e2e_logits": {"value": e2e_logits_tps, "unit": "tok/s", "h2d_bytes_per_step": 4 + 32,
+                           "d2h_bytes_per_step": hp.n_vocab * 4 + 4,
+                           "api": "mi_cuda_qwen2_forward (logits row out) + host greedy, as the reference loop"},
             "gpu_launches": args.steps * kv.kernels_per_step + (args.steps - 1) // PERIOD,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
