@@ -185,9 +185,66 @@ def step_trace_summary(kv) -> dict:
     return trace
 
 
+def run_reference_arm_prefill(args):
+    """Config 3 on the reference: its mi_qwen2_forward of the 1024-token prompt
+    (last logits) on all host cores; at most 3 timed forwards (bounded)."""
+    import mi_oracle
+    path = ensure_model(0, None)
+    threads = os.cpu_count() or 1
+    m = mi_oracle.ReferenceModel(path, n_ctx=N_CTX, n_threads=threads)
+    prompt = np.random.default_rng(SEED_PROMPT).integers(0, m.n_vocab, N_PREFILL).astype(np.int32)
+    steps = max(1, min(args.steps, 3))
+    m.forward(prompt, 0, last_logits_only=True)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        m.forward(prompt, 0, last_logits_only=True)
+    s = (time.perf_counter() - t0) / steps
+    m.close()
+    tps = N_PREFILL / s
+    print(json.dumps({
+        "metric": METRIC_PREFILL, "value": tps, "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
+        "steps": steps, "warmup": 1, "ms_per_step": s * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": tps / PUBLISHED_PREFILL, "dtype": "i8*i8->f32", "data": "synthetic",
+        "config": {"workload": "qwen2.5-0.5b-shape Q8_0 prefill, 1024-token prompt, ctx 2048, last logits",
+                   "parallelism": "cpu threads"},
+        "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": "reference",
+                         "sample": f"{steps} forwards of the 1024-token prompt, {threads} threads"},
+        "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_reference_arm_7b(args):
+    """Config 4 on the reference: its decode loop over the 7B-shape model on all
+    host cores (one process; no GPUs), bounded to 16 decode forwards."""
+    import mi_oracle
+    path = os.path.join(MODEL_DIR, f"qwen2_7b_seed{SEED_MODEL}_fast.gguf")
+    mi_gguf.ensure_qwen2_gguf(path, mi_gguf.QWEN2_7B, SEED_MODEL, fast=True)
+    threads = os.cpu_count() or 1
+    m = mi_oracle.ReferenceModel(path, n_ctx=N_CTX_7B, n_threads=threads)
+    prompt = np.random.default_rng(SEED_PROMPT).integers(0, m.n_vocab, N_PROMPT_7B).astype(np.int32)
+    n_dec = max(1, min(args.steps, 16))
+    _, pre_ms, dec_ms = m.generate(prompt, n_dec + 1)
+    m.close()
+    tps = n_dec / (dec_ms / 1e3)
+    print(json.dumps({
+        "metric": METRIC_7B, "value": tps, "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
+        "steps": n_dec, "warmup": 0, "ms_per_step": dec_ms / n_dec, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "i8*i8->f32", "data": "synthetic",
+        "config": {"workload": "qwen2.5-7b-shape Q8_0 greedy decode, ctx 4096, prompt 64", "parallelism": "cpu threads"},
+        "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": "reference",
+                         "sample": f"{n_dec} decode forwards after the 64-token prefill ({pre_ms / 1e3:.1f} s), "
+                                   f"{threads} threads"},
+        "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 def run_reference_arm(args, rank: int):
     if rank != 0:
         return
+    if args.config == "prefill":
+        return run_reference_arm_prefill(args)
+    if args.config == "tp7b":
+        return run_reference_arm_7b(args)
     path = ensure_model(0, None)
     threads = os.cpu_count() or 1
     tps, _, sample = reference_decode(path, args.steps, args.warmup, threads)
