@@ -46,8 +46,8 @@ __device__ __forceinline__ void cp_async_wait() {
 // ---------------------------------------------------------------------------
 constexpr int kGemmBN = 64;  // weight rows per CTA (16 groups of 4)
 constexpr int kGemmBM = 32;  // tokens per CTA
-constexpr int kGemmKB = 16;  // 32-element blocks per stage
-constexpr int kGemmStages = 3;
+constexpr int kGemmKB = 12;  // 32-element blocks per stage
+constexpr int kGemmStages = 2;  // ~88 KB of shared memory: two CTAs per SM
 constexpr int kGemmWStride = kGemmKB * 128 + 16;  // bytes per group in a stage (padded)
 // A lane partial p = dp4a(w, a) satisfies |p| <= 4 * 127 * 127 < 2^22. With
 // the accumulator input bits(1.5 * 2^23) the dp4a result is the bit pattern of
@@ -68,7 +68,7 @@ struct GemmSmem {
   static constexpr int total = res + kGemmBN * kGemmBM * 4;
 };
 
-__global__ void __launch_bounds__(256, 1) gemm_q8_kernel(const GemmParams p) {
+__global__ void __launch_bounds__(256, 2) gemm_q8_kernel(const GemmParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t K = p.K;
