@@ -1,0 +1,43 @@
+"""The bench's algorithmic byte and MAC counts against the figures derived from
+the model shapes: a decode step reads every weight once (Q8_0 at 34/32 B per
+weight, F32 norms and biases), one embedding row, and the K/V rows; a prefill
+multiplies every projection by every token and the LM head by the last."""
+import importlib.util
+import os
+
+import mi_gguf
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _bench():
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+class _HP:
+    def __init__(self, s):
+        self.n_embd, self.head_dim, self.n_ff = s.n_embd, s.head_dim, s.n_ff
+        self.n_layer, self.n_vocab, self.n_head_kv = s.n_layer, s.n_vocab, s.n_head_kv
+
+
+def test_decode_step_bytes():
+    b = _bench()
+    hp05 = _HP(mi_gguf.QWEN2_05B)
+    # weights + norms/biases + embedding row: 525,120,952 B; KV: 24,576 B per position
+    assert b.step_bytes(hp05, 0) - 24576 == 525_120_952
+    assert b.step_bytes(hp05, 96) - b.step_bytes(hp05, 95) == 24576
+    hp7 = _HP(mi_gguf.QWEN2_7B)
+    assert b.step_bytes(hp7, 0) - 114688 == 7_513_515_744
+    assert b.step_bytes(hp7, 1) - b.step_bytes(hp7, 0) == 114688
+
+
+def test_prefill_macs():
+    b = _bench()
+    hp05 = _HP(mi_gguf.QWEN2_05B)
+    per_token = 357_826_560  # 24 layers x (QKV + O + gate/up + down) int8 MACs
+    head = 151936 * 896
+    assert b.prefill_macs(hp05, 1) == per_token + head
+    assert b.prefill_macs(hp05, 1024) == 1024 * per_token + head
