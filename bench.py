@@ -168,8 +168,10 @@ def step_trace_summary(kv) -> dict:
     dependency wait -> prologue done, prologue -> epilogue, hand-off from the
     predecessor, and the attention phases."""
     t = kv.step_trace().astype(np.int64)
-    names = ["qkv", "attn", "o", "gate_up", "down"]
-    kinds = [names[i % 5] for i in range(t.shape[0] - 1)] + ["lm_head"]
+    per = (t.shape[0] - 1) // kv.model.hparams.n_layer
+    # 4 kernels a layer when QKV and attention run as one cluster kernel
+    names = ["qkv_attn", "o", "gate_up", "down"] if per == 4 else ["qkv", "attn", "o", "gate_up", "down"]
+    kinds = [names[i % per] for i in range(t.shape[0] - 1)] + ["lm_head"]
     trace = {"step_us": float(t[-1, 3] - t[0, 0]) / 1e3, "per_kernel_us": {}}
     for k in dict.fromkeys(kinds):
         idx = [i for i, kk in enumerate(kinds) if kk == k]
@@ -178,10 +180,16 @@ def step_trace_summary(kv) -> dict:
             "dep_to_prologue": float(np.mean([t[i, 2] - t[i, 1] for i in idx])) / 1e3,
             "prologue_to_epilogue": float(np.mean([t[i, 3] - t[i, 2] for i in idx])) / 1e3,
             "handoff": float(np.mean(dep)) / 1e3 if dep else None}
-    ai = [i for i, kk in enumerate(kinds) if kk == "attn"]
+    if per == 4:
+        # fused kernel marks: 2 prologue, 4 k/v handed over, 5 scores, 6 exp, 7 sum, 3 KV done
+        ai = [i for i, kk in enumerate(kinds) if kk == "qkv_attn"]
+        phases = (("qkv_rows_and_handover", 2, 4), ("scores", 4, 5), ("max_exp", 5, 6), ("sum", 6, 7),
+                  ("kv", 7, 3))
+    else:
+        ai = [i for i, kk in enumerate(kinds) if kk == "attn"]
+        phases = (("scores", 2, 4), ("max_exp", 4, 5), ("sum", 5, 6), ("kv", 6, 7))
     trace["attention_phases_us"] = {
-        name: float(np.mean([t[i, b] - t[i, a] for i in ai])) / 1e3
-        for name, a, b in (("scores", 2, 4), ("max_exp", 4, 5), ("sum", 5, 6), ("kv", 6, 7))}
+        name: float(np.mean([t[i, b] - t[i, a] for i in ai])) / 1e3 for name, a, b in phases}
     return trace
 
 

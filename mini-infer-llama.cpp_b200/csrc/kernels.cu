@@ -78,7 +78,7 @@ __host__ __device__ inline GemvSmem gemv_smem(int64_t K, int32_t rows_per_cta, i
 // order is unchanged.
 // ---------------------------------------------------------------------------
 template <int NT, int TPR, bool TP>
-__global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(NT, 2) gemv_q8_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int NW = NT / 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -161,9 +161,21 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
   } else if (tid == 0) {
     for (int t = 0; t < min(n_tiles, p.n_stages); t++) issue(t);
   }
+  // Operands that do not depend on the predecessor -- the bias of the CTA's
+  // first NT rows, the rms_norm weights of this lane's first four blocks --
+  // are loaded before the dependency wait, the residual right after it, so
+  // their latency overlaps the wait, the prologue and the chains.
+  float pre = 0.0f;
+  if (!TP && p.epi == EPI_BIAS && tid < nrows && r0 + tid < p.N) pre = p.bias[r0 + tid];
+  float nw[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  if (p.pro >= PRO_NORM_QUANT)
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+      if (warp + u * NW < nb) nw[u] = p.norm_w[(int64_t)(warp + u * NW) * 32 + lane];
   pdl_trigger();
   pdl_wait_cta();
   trace_mark(p.trace, p.trace_slot, 1);
+  if (!TP && p.epi == EPI_RESID && tid < nrows && r0 + tid < p.N) pre = p.resid[r0 + tid];
 
   // ---- prologue: the quantized activation in shared memory ----
   if (TP && p.pro == PRO_ACT && p.act_ll) {
@@ -229,18 +241,23 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
       scale = misc[0];
     }
     // One block per warp at a time would serialize the quantizer's two
-    // divisions; four independent blocks per iteration overlap them.
-    auto value = [&](int64_t k) {
-      if (p.pro >= PRO_NORM_QUANT)
-        return __fmul_rn(__fmul_rn(xs[k], scale), p.norm_w[k]);  // rms_norm, then MUL weight
+    // divisions; four independent blocks per iteration overlap them. The
+    // warp's blocks are warp + u*NW; the first four use the preloaded norm
+    // weights nw[u].
+    auto value = [&](int64_t k, float nwk) {
+      if (p.pro >= PRO_NORM_QUANT) return __fmul_rn(__fmul_rn(xs[k], scale), nwk);  // rms_norm, then MUL weight
       return p.stage_x ? xs[k] : p.x[k];
     };
+    auto nw_at = [&](int64_t k) { return p.pro >= PRO_NORM_QUANT ? p.norm_w[k] : 0.0f; };
     int b = warp;
     for (; b + 3 * NW < nb; b += 4 * NW) {
       float v[4], d[4];
       int8_t q[4];
 #pragma unroll
-      for (int u = 0; u < 4; u++) v[u] = value((int64_t)(b + u * NW) * 32 + lane);
+      for (int u = 0; u < 4; u++) {
+        const int64_t k = (int64_t)(b + u * NW) * 32 + lane;
+        v[u] = value(k, b == warp ? nw[u] : nw_at(k));
+      }
 #pragma unroll
       for (int u = 0; u < 4; u++) q[u] = quantize_lane(v[u], &d[u]);
 #pragma unroll
@@ -249,11 +266,22 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
         if (lane == 0) ad[b + u * NW] = d[u];
       }
     }
-    for (; b < nb; b += NW) {
-      const int64_t k = (int64_t)b * 32 + lane;
-      float d;
-      aq[k] = quantize_lane(value(k), &d);
-      if (lane == 0) ad[b] = d;
+    if (b == warp) {  // fewer than four blocks for this warp: all preloaded
+#pragma unroll
+      for (int u = 0; u < 3; u++) {
+        if (b + u * NW >= nb) break;
+        const int64_t k = (int64_t)(b + u * NW) * 32 + lane;
+        float d;
+        aq[k] = quantize_lane(value(k, nw[u]), &d);
+        if (lane == 0) ad[b + u * NW] = d;
+      }
+    } else {
+      for (; b < nb; b += NW) {
+        const int64_t k = (int64_t)b * 32 + lane;
+        float d;
+        aq[k] = quantize_lane(value(k, nw_at(k)), &d);
+        if (lane == 0) ad[b] = d;
+      }
     }
   }
   __syncthreads();
@@ -324,13 +352,7 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
       for (int g = warp; g < ngroups; g += NW) {
         const uint32_t* gq = sq + (size_t)g * 32 * kc;
         const __half* gd = sd + (size_t)g * 4 * kc;
-        float acc = ch == 0 ? 0.0f : acc_run;
-#pragma unroll 4
-        for (int i = 0; i < kcb; i++) {
-          const int pi = __dp4a((int)gq[i * 32 + lane], aq4[(c0 + i) * 8 + j], 0);
-          const float dxdy = __fmul_rn(__half2float(gd[i * 4 + rr]), ad[c0 + i]);
-          acc = __fmaf_rn(__int2float_rn(pi), dxdy, acc);
-        }
+        const float acc = lane_chain(ch == 0 ? 0.0f : acc_run, gq, gd, aq4 + c0 * 8, ad + c0, kcb, lane, j, rr);
         if (ch + 1 < n_chunks) {
           acc_run = acc;
           continue;
@@ -456,8 +478,8 @@ __global__ void __launch_bounds__(NT) gemv_q8_kernel(const GemvParams p) {
       const int64_t r = r0 + lr;
       if (r >= p.N) continue;
       float v = res[lr];
-      if (p.epi == EPI_BIAS) v = __fadd_rn(v, p.bias[r]);
-      else if (p.epi == EPI_RESID) v = __fadd_rn(p.resid[r], v);
+      if (p.epi == EPI_BIAS) v = __fadd_rn(v, lr == tid ? pre : p.bias[r]);
+      else if (p.epi == EPI_RESID) v = __fadd_rn(lr == tid ? pre : p.resid[r], v);
       p.out[r] = v;
     }
     return;
@@ -562,8 +584,9 @@ GemvPlan plan_gemv(int64_t k, int64_t n, int num_sms, int pro, int32_t rows_per_
     // Wide rows (K >= 2048). Rows per CTA are a multiple of 4 (one CTA per SM
     // or the caller's count). Default: warp-stream mode (tpr 0), each active
     // warp owning a ring of S stages of one group's K-chunk, S = 3, the chunk
-    // as large as shared memory allows. MI_CUDA_GEMV_WIDE="0,S,stage_kb" or
-    // "8,rows,stage_kb" picks the mode and shape (tuning sweeps; clamped).
+    // as large as shared memory allows. MI_CUDA_GEMV_WIDE="0,S,stage_kb",
+    // "8,rows,stage_kb" or "2,rows,stage_kb" picks the mode and shape (tuning
+    // sweeps; clamped; mode 2 needs whole rows per stage, else it runs as 8).
     const int64_t groups = n_pad / 4;
     const int64_t target = std::max<int64_t>(1, std::min<int64_t>(num_sms, groups));
     pl.rows_per_cta = rows_per_cta > 0 ? rows_per_cta : (int32_t)((groups + target - 1) / target * 4);
@@ -571,7 +594,7 @@ GemvPlan plan_gemv(int64_t k, int64_t n, int num_sms, int pro, int32_t rows_per_
     int mode = 0, ov_a = 0, ov_kb = 0;
     if (const char* e = std::getenv("MI_CUDA_GEMV_WIDE")) {
       int m = 0, x = 0, kb = 0;
-      if (std::sscanf(e, "%d,%d,%d", &m, &x, &kb) == 3 && (m == 0 || m == 8) && x > 0 && kb >= 0) {
+      if (std::sscanf(e, "%d,%d,%d", &m, &x, &kb) == 3 && (m == 0 || m == 8 || m == 2) && x > 0 && kb >= 0) {
         mode = m;
         ov_a = x;
         ov_kb = kb;
@@ -625,6 +648,7 @@ GemvPlan plan_gemv(int64_t k, int64_t n, int num_sms, int pro, int32_t rows_per_
         break;
       }
     }
+    if (mode == 2 && pl.n_chunks == 1) pl.tpr = 2;
     return pl;
   }
   const int64_t groups8 = n_pad / 8;
@@ -670,6 +694,7 @@ cudaError_t set_gemv_smem(int optin) {
     e = cudaFuncSetAttribute(gemv_q8_kernel<256, TPR, TP>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              optin - (int)f.sharedSizeBytes);
+  if (e == cudaSuccess) e = set_carveout(gemv_q8_kernel<256, TPR, TP>);
   return e;
 }
 }  // namespace
@@ -686,6 +711,7 @@ cudaError_t prepare_kernels() {
   if (e == cudaSuccess) e = set_gemv_smem<0, true>(optin);
   if (e == cudaSuccess) e = prepare_attn_kernels(optin);
   if (e == cudaSuccess) e = prepare_gemm_kernel();
+  if (e == cudaSuccess) e = prepare_qkv_attn_kernel(optin);
   return e;
 }
 
@@ -979,6 +1005,7 @@ cudaError_t set_attn_smem(int optin) {
     e = cudaFuncSetAttribute(attn_decode_kernel<EXEC, SPEC, TP>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              optin - (int)f.sharedSizeBytes);
+  if (e == cudaSuccess) e = set_carveout(attn_decode_kernel<EXEC, SPEC, TP>);
   return e;
 }
 }  // namespace

@@ -13,6 +13,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
+
 #include "mi_expf_core.h"
 #include "mi_internal.h"
 
@@ -92,6 +94,55 @@ __device__ __forceinline__ void pdl_wait_cta() {
 }
 __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// MI_CUDA_CARVEOUT=<percent> sets every decode kernel's preferred shared-memory
+// carveout (cudaFuncAttributePreferredSharedMemoryCarveout); unset leaves the
+// driver's choice. An SM changes its carveout only when idle, so a kernel whose
+// CTAs need a large share can start beside its predecessor's CTAs only on SMs
+// already configured that large.
+template <typename F>
+inline cudaError_t set_carveout(F* func) {
+  const char* c = std::getenv("MI_CUDA_CARVEOUT");
+  if (!c) return cudaSuccess;
+  const int pct = std::atoi(c);
+  if (pct < 0 || pct > 100) return cudaSuccess;
+  return cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout, pct);
+}
+
+// ---------------------------------------------------------------------------
+// Thread-block clusters: the hardware cluster barrier (every thread of every
+// CTA arrives, then waits; exited threads do not count) and stores into
+// another CTA's shared memory (distributed shared memory).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The shared::cluster address of `p` (a variable of this CTA's shared memory)
+// in the CTA of cluster rank `rank`.
+__device__ __forceinline__ uint32_t dsmem_addr(const void* p, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_addr(p)), "r"(rank));
+  return a;
+}
+__device__ __forceinline__ void dsmem_store(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ float dsmem_load(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
 }
 
 // ---------------------------------------------------------------------------
@@ -246,6 +297,47 @@ __device__ __forceinline__ float ordered_dot_scaled(float acc, const float* v, i
     for (int u = 0; u < 16; u++) acc = __fadd_rn(acc, __fmul_rn(a[u], b[u]));
   }
   for (; t < n; t++) acc = __fadd_rn(acc, __fmul_rn(v[(size_t)t * vs], __fmul_rn(p[t], s)));
+  return acc;
+}
+
+// One lane's accumulator chain of the Q8_0 dot over n blocks of a 4-row group
+// held in shared memory in the packed layout (block i: quants gq[i*32 + lane],
+// scales gd[i*4 + rr]) against the quantized activation (aq4 words, ad scales,
+// both already offset to the chain's first block):
+//   acc = fma((float)dp4a(w_i, a_i), fp16(w.d_i) * a.d_i, acc), i ascending.
+// The operands of eight blocks are loaded before their dependent FMAs, so the
+// chain runs at FMA latency rather than at shared-memory load latency.
+__device__ __forceinline__ float lane_chain(float acc, const uint32_t* gq, const __half* gd, const int* aq4,
+                                            const float* ad, int n, int lane, int j, int rr) {
+  int i = 0;
+  for (; i + 8 <= n; i += 8) {
+    int w[8], a[8];
+    float dx[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      w[u] = (int)gq[(i + u) * 32 + lane];
+      a[u] = aq4[(i + u) * 8 + j];
+      dx[u] = __fmul_rn(__half2float(gd[(i + u) * 4 + rr]), ad[i + u]);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++) acc = __fmaf_rn(__int2float_rn(__dp4a(w[u], a[u], 0)), dx[u], acc);
+  }
+  if (i + 4 <= n) {
+    int w[4], a[4];
+    float dx[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      w[u] = (int)gq[(i + u) * 32 + lane];
+      a[u] = aq4[(i + u) * 8 + j];
+      dx[u] = __fmul_rn(__half2float(gd[(i + u) * 4 + rr]), ad[i + u]);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) acc = __fmaf_rn(__int2float_rn(__dp4a(w[u], a[u], 0)), dx[u], acc);
+    i += 4;
+  }
+  for (; i < n; i++)
+    acc = __fmaf_rn(__int2float_rn(__dp4a((int)gq[i * 32 + lane], aq4[i * 8 + j], 0)),
+                    __fmul_rn(__half2float(gd[i * 4 + rr]), ad[i]), acc);
   return acc;
 }
 

@@ -142,6 +142,64 @@ cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t
                                bool tp = false, int32_t n_queries = 1);
 
 // ---------------------------------------------------------------------------
+// Fused QKV projection + decode attention (executor, one GPU)
+// ---------------------------------------------------------------------------
+// One thread-block cluster of n_rep + 1 CTAs per KV head: CTA c < n_rep
+// computes the q rows of query head kvh * n_rep + c, CTA n_rep the k and v
+// rows of the KV head. Every CTA runs the rms_norm + quantize prologue; the
+// k/v CTA applies RoPE, appends k and v to the cache and stores them into the
+// query CTAs' shared memory; after the cluster barrier each query CTA runs the
+// decode attention of its head. Removes the QKV -> attention kernel boundary.
+struct QkvAttnParams {
+  const uint8_t* w;  // packed Q | K | V rows
+  int64_t K, n_pad;
+  const float* bias;  // [n_head * hd + 2 * n_head_kv * hd]
+  int32_t pro;        // PRO_NORM_QUANT, or PRO_EMBED_NORM (layer 0)
+  int32_t tokens_len;
+  const float* x;
+  const float* norm_w;
+  float eps;
+  int32_t pad0;
+  const uint8_t* embed;
+  int64_t embed_npad, embed_rows;
+  const int32_t* tokens;
+  float* x_out;  // PRO_EMBED_NORM: CTA 0 stores the embedding row here
+  float* cache_k;
+  float* cache_v;
+  int32_t head_dim, n_head, n_head_kv, n_ctx;
+  const int32_t* pos;
+  const float2* rope_cs;
+  float scale;
+  int32_t kv_tile, scores_in_smem;  // set from the plan
+  int32_t pad1;
+  float* scores;  // [n_head][scores_stride] when the scores do not fit on chip
+  int64_t scores_stride;
+  float* out;         // [n_head][hd]; null when act_out is set
+  uint8_t* act_out;   // the O projection's Q8_0_ACT input (head_dim % 32 == 0)
+  ExpTab et;
+  int32_t* err;
+  uint64_t* trace;
+  int32_t trace_slot;
+  // Detail slots: CTA 0 (query CTA of head 0) and CTA n_rep (the first k/v
+  // CTA) store 0 entry, 1 dependency satisfied, 2 x loaded, 3 rms_norm sum
+  // done, 4 prologue done, 5 rows done, 6 bias + RoPE done, 7 hand-over done
+  // (query CTA: k / v read; k/v CTA: every query CTA arrived).
+  int32_t trace_slot_q, trace_slot_kv;
+};
+struct QkvAttnPlan {
+  bool ok;
+  int32_t cluster, kv_tile, scores_in_smem;
+  size_t smem;
+};
+// The fused kernel's plan for a model shape, or ok == false when the shape
+// does not fit it (head_dim, cluster size, shared memory within smem_budget
+// bytes) or the device cannot run one of its clusters.
+QkvAttnPlan plan_qkv_attn(int64_t K, int32_t head_dim, int32_t n_head, int32_t n_head_kv, int32_t n_ctx,
+                          size_t smem_budget);
+cudaError_t launch_qkv_attn(const QkvAttnParams& p, const QkvAttnPlan& plan, cudaStream_t s, bool pdl);
+cudaError_t prepare_qkv_attn_kernel(int optin);
+
+// ---------------------------------------------------------------------------
 // Batched prefill (prefill.cu)
 // ---------------------------------------------------------------------------
 // Exact Q8_0 GEMM over M tokens: out[t * out_stride + r] = dot(W row r, act t)

@@ -67,6 +67,10 @@ int fail(int code, const std::string& msg) {
   } while (0)
 
 constexpr int kTraceStamps = 8;  // globaltimer stamps per kernel slot (mi_device.cuh)
+// Shared memory of one fused QKV + attention CTA: with the ~48 KB of a 0.5B
+// FFN-down GEMV CTA it still fits one SM, so the kernel's clusters can start
+// (and stream their weights) while the previous layer's down projection runs.
+constexpr size_t kFusedSmemBudget = 168 * 1024;
 
 int64_t npad8(int64_t n) { return (n + 7) / 8 * 8; }
 size_t packed_bytes(int64_t k, int64_t n) { return (size_t)(npad8(n) * k + npad8(n) * (k / 32) * 2); }
@@ -131,6 +135,10 @@ struct mi_cuda_kv_cache {
   bool connected = false;
   uint32_t* epoch = nullptr;
   GemvPlan plan_qkv{}, plan_o{}, plan_gu{}, plan_down{}, plan_head{};
+  // One GPU, shapes that fit: the QKV GEMV and the attention run as one
+  // cluster kernel per layer (qkv_attn.cu).
+  QkvAttnPlan plan_fused{};
+  bool fused = false;
   cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
   // Batched-prefill workspace, allocated on first use and grown to the largest
   // batch: residual streams X / X2 [T][E], q|k|v [T][E + 2kvd], rotated q
@@ -482,63 +490,105 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     const size_t o_qkv = kv->x_qkv + (size_t)l * nqkv_full, o_h1 = kv->x_h1 + (size_t)l * E,
                  o_act = kv->x_act + (size_t)l * act_words, o_h2 = kv->x_h2 + (size_t)l * E,
                  o_prev = l > 0 ? kv->x_h2 + (size_t)(l - 1) * E : 0;
-    GemvParams p{};
-    p.w = L.qkv.w;
-    p.K = E;
-    p.N = L.qkv.N;
-    p.n_pad = L.qkv.npad;
-    p.pro = l == 0 ? PRO_EMBED_NORM : PRO_NORM_QUANT;
-    p.x = kv->x;
-    p.norm_w = L.attn_norm;
-    p.eps = hp.rms_eps;
-    p.embed = m->embed.w;
-    p.embed_npad = m->embed.npad;
-    p.embed_rows = hp.n_vocab;
-    p.tokens = kv->tokens;
-    p.tokens_len = kv->n_ctx + 1;
-    p.pos = &kv->state->pos;
-    p.x_out = kv->x;
-    p.epi = EPI_BIAS;
-    p.bias = L.bqkv;
-    p.out = kv->qkv;
-    p.et = et;
-    p.err = err;
-    p.trace = kv->trace;
-    p.trace_slot = count;
-    if (tp) {
-      p.row0 = sh.qkv0;
-      if (l > 0) p.x_ll = local(o_prev);
-      outs(p, o_qkv);
-    }
-    CK(launch_gemv(p, kv->plan_qkv, kv->stream, pdl, tp));
-    pdl = kv->pdl;
-    count++;
+    float* const cache_k = kv->cache + (size_t)l * layer_floats;
+    float* const cache_v = cache_k + (size_t)kv->n_ctx * kvd;
+    if (kv->fused) {
+      QkvAttnParams f{};
+      f.w = L.qkv.w;
+      f.K = E;
+      f.n_pad = L.qkv.npad;
+      f.bias = L.bqkv;
+      f.pro = l == 0 ? PRO_EMBED_NORM : PRO_NORM_QUANT;
+      f.tokens_len = kv->n_ctx + 1;
+      f.x = kv->x;
+      f.norm_w = L.attn_norm;
+      f.eps = hp.rms_eps;
+      f.embed = m->embed.w;
+      f.embed_npad = m->embed.npad;
+      f.embed_rows = hp.n_vocab;
+      f.tokens = kv->tokens;
+      f.x_out = kv->x;
+      f.cache_k = cache_k;
+      f.cache_v = cache_v;
+      f.head_dim = (int32_t)D;
+      f.n_head = hp.n_head;
+      f.n_head_kv = hp.n_head_kv;
+      f.n_ctx = kv->n_ctx;
+      f.pos = &kv->state->pos;
+      f.rope_cs = kv->rope;
+      f.scale = 1.0f / std::sqrt((float)hp.head_dim);
+      f.scores = kv->scores;
+      f.scores_stride = kv->n_ctx;
+      f.out = kv->quant_attn ? nullptr : kv->attn;
+      f.act_out = kv->quant_attn ? kv->attn_q : nullptr;
+      f.et = et;
+      f.err = err;
+      f.trace = kv->trace;
+      f.trace_slot = count;
+      f.trace_slot_q = 4 * hp.n_layer + 1 + 2 * l;
+      f.trace_slot_kv = f.trace_slot_q + 1;
+      CK(launch_qkv_attn(f, kv->plan_fused, kv->stream, pdl));
+      pdl = kv->pdl;
+      count++;
+    } else {
+      GemvParams p{};
+      p.w = L.qkv.w;
+      p.K = E;
+      p.N = L.qkv.N;
+      p.n_pad = L.qkv.npad;
+      p.pro = l == 0 ? PRO_EMBED_NORM : PRO_NORM_QUANT;
+      p.x = kv->x;
+      p.norm_w = L.attn_norm;
+      p.eps = hp.rms_eps;
+      p.embed = m->embed.w;
+      p.embed_npad = m->embed.npad;
+      p.embed_rows = hp.n_vocab;
+      p.tokens = kv->tokens;
+      p.tokens_len = kv->n_ctx + 1;
+      p.pos = &kv->state->pos;
+      p.x_out = kv->x;
+      p.epi = EPI_BIAS;
+      p.bias = L.bqkv;
+      p.out = kv->qkv;
+      p.et = et;
+      p.err = err;
+      p.trace = kv->trace;
+      p.trace_slot = count;
+      if (tp) {
+        p.row0 = sh.qkv0;
+        if (l > 0) p.x_ll = local(o_prev);
+        outs(p, o_qkv);
+      }
+      CK(launch_gemv(p, kv->plan_qkv, kv->stream, pdl, tp));
+      pdl = kv->pdl;
+      count++;
 
-    AttnParams a{};
-    a.qkv = kv->qkv;
-    a.cache_k = kv->cache + (size_t)l * layer_floats;
-    a.cache_v = a.cache_k + (size_t)kv->n_ctx * kvd;
-    a.head_dim = (int32_t)D;
-    a.n_head = hp.n_head;
-    a.n_head_kv = hp.n_head_kv;
-    a.pos = &kv->state->pos;
-    a.rope_cs = kv->rope;
-    a.scale = 1.0f / std::sqrt((float)hp.head_dim);
-    a.n_ctx = kv->n_ctx;
-    a.scores = kv->scores;
-    a.scores_stride = kv->n_ctx;
-    a.out = kv->quant_attn ? nullptr : kv->attn;
-    a.act_out = kv->quant_attn ? kv->attn_q : nullptr;
-    a.et = et;
-    a.err = err;
-    a.trace = kv->trace;
-    a.trace_slot = count;
-    if (tp) {
-      a.qkv_ll = local(o_qkv);
-      a.epoch = kv->epoch;
+      AttnParams a{};
+      a.qkv = kv->qkv;
+      a.cache_k = cache_k;
+      a.cache_v = cache_v;
+      a.head_dim = (int32_t)D;
+      a.n_head = hp.n_head;
+      a.n_head_kv = hp.n_head_kv;
+      a.pos = &kv->state->pos;
+      a.rope_cs = kv->rope;
+      a.scale = 1.0f / std::sqrt((float)hp.head_dim);
+      a.n_ctx = kv->n_ctx;
+      a.scores = kv->scores;
+      a.scores_stride = kv->n_ctx;
+      a.out = kv->quant_attn ? nullptr : kv->attn;
+      a.act_out = kv->quant_attn ? kv->attn_q : nullptr;
+      a.et = et;
+      a.err = err;
+      a.trace = kv->trace;
+      a.trace_slot = count;
+      if (tp) {
+        a.qkv_ll = local(o_qkv);
+        a.epoch = kv->epoch;
+      }
+      CK(launch_attn_decode(a, true, kv->stream, pdl, tp));
+      count++;
     }
-    CK(launch_attn_decode(a, true, kv->stream, pdl, tp));
-    count++;
 
     GemvParams o{};
     o.w = L.o.w;
@@ -972,6 +1022,19 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
   kv->plan_gu = plan_gemv(E, 64 * sh.nff, sms, PRO_NORM_QUANT, (int32_t)(64 * bpc));
   kv->plan_down = plan_gemv(FF, sh.no, sms, PRO_ACT);
   kv->plan_head = plan_gemv(E, sh.nv, sms, PRO_NORM_QUANT);
+  // The fused QKV + attention kernel where the shape fits it (one GPU);
+  // MI_CUDA_FUSED_ATTN=0 keeps the GEMV + attention kernel pair, and
+  // MI_CUDA_FUSED_SMEM_KB sets its shared-memory budget (for comparisons).
+  if (m->world == 1) {
+    const char* fe = std::getenv("MI_CUDA_FUSED_ATTN");
+    size_t budget = kFusedSmemBudget;
+    if (const char* b = std::getenv("MI_CUDA_FUSED_SMEM_KB"))
+      if (std::atoi(b) > 0) budget = (size_t)std::atoi(b) * 1024;
+    if (!(fe && std::atoi(fe) == 0)) {
+      kv->plan_fused = plan_qkv_attn(E, (int32_t)D, hp.n_head, hp.n_head_kv, n_ctx, budget);
+      kv->fused = kv->plan_fused.ok;
+    }
+  }
 
   const size_t cache_bytes = (size_t)hp.n_layer * 2 * n_ctx * kvd * 4;
   const size_t rope_bytes = (size_t)n_ctx * (D / 2) * 8;
@@ -988,7 +1051,7 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
                o_pi = slot(1024 * 4), o_tok = slot((size_t)(n_ctx + 1) * 4),
                o_state = slot(sizeof(StepState)), o_attnq = slot(E / 32 * 36),
                o_actq = slot(FF / 32 * 36),
-               o_trace = slot((size_t)(5 * hp.n_layer + 1) * kTraceStamps * 8), o_epoch = slot(4);
+               o_trace = slot((size_t)(6 * hp.n_layer + 1) * kTraceStamps * 8), o_epoch = slot(4);
   CK(cudaMalloc(&kv->buf, off));
   CK(cudaMemset(kv->buf, 0, off));
   kv->cache = (float*)(kv->buf + o_cache);
@@ -1007,7 +1070,9 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
   kv->attn_q = kv->buf + o_attnq;
   kv->act_q = kv->buf + o_actq;
   kv->trace = (uint64_t*)(kv->buf + o_trace);
-  kv->trace_slots = 5 * hp.n_layer + 1;
+  // one slot per kernel of a step; the fused QKV + attention kernel adds two
+  // detail slots per layer after the step's slots
+  kv->trace_slots = 6 * hp.n_layer + 1;
   kv->epoch = (uint32_t*)(kv->buf + o_epoch);
   const uint32_t one = 1u;  // exchange words start zeroed: tag 0 is never current
   CK(cudaMemcpy(kv->epoch, &one, 4, cudaMemcpyHostToDevice));
@@ -1038,6 +1103,15 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
   }
   int rc = capture(kv.get(), true, &kv->g_head, &kv->kernels_per_step);
   if (!rc) rc = capture(kv.get(), false, &kv->g_nohead, nullptr);
+  if (rc && kv->fused) {
+    // Retry with the two-kernel QKV + attention path if the cluster launch was refused.
+    kv->fused = false;
+    if (kv->g_head) cudaGraphExecDestroy(kv->g_head);
+    kv->g_head = nullptr;
+    cudaGetLastError();
+    rc = capture(kv.get(), true, &kv->g_head, &kv->kernels_per_step);
+    if (!rc) rc = capture(kv.get(), false, &kv->g_nohead, nullptr);
+  }
   if (rc) {
     // Retry without programmatic dependent launch if the graph refused it.
     kv->pdl = false;

@@ -28,12 +28,29 @@ def logits_close(a, b):
     return float(np.max(np.abs(a - b))), cos
 
 
+def kernels_per_layer(kv, model):
+    return (kv.kernels_per_step - 1) // model.hparams.n_layer
+
+
+@pytest.fixture(params=["fused", "fused_small_tile", "pair"])
+def qkv_attn_path(request, monkeypatch):
+    """Runs a test with the fused QKV + attention cluster kernel (4 kernels a
+    layer; fused_small_tile: a 44 KB shared-memory budget, which leaves the
+    SMALL shape a 32-position K/V tile, so attention walks several tiles) and
+    with the QKV GEMV + attention kernel pair (5 a layer)."""
+    monkeypatch.setenv("MI_CUDA_FUSED_ATTN", "0" if request.param == "pair" else "1")
+    if request.param == "fused_small_tile":
+        monkeypatch.setenv("MI_CUDA_FUSED_SMEM_KB", "44")
+    return 5 if request.param == "pair" else 4
+
+
 @pytest.mark.parametrize("shape,seed,n_ctx", [("TINY", 1, 64), ("SMALL", 4, 256)])
-def test_forward_prefill_and_decode_bitexact(mc, model_path, shape, seed, n_ctx):
+def test_forward_prefill_and_decode_bitexact(mc, model_path, qkv_attn_path, shape, seed, n_ctx):
     path = model_path(shape, seed)
     ref = mi_oracle.ReferenceModel(path, n_ctx=n_ctx)
     model = mc.Qwen2Model(path)
     kv = mc.KVCache(model, n_ctx)
+    assert kernels_per_layer(kv, model) == qkv_attn_path
     rng = np.random.default_rng(seed)
     prompt = rng.integers(0, ref.n_vocab, 9).astype(np.int32)
     want = ref.forward(prompt, 0)
@@ -56,11 +73,12 @@ def test_forward_prefill_and_decode_bitexact(mc, model_path, shape, seed, n_ctx)
 
 
 @pytest.mark.parametrize("shape,seed,n_ctx,n_prompt,n_predict", [("TINY", 3, 128, 16, 100), ("SMALL", 5, 512, 32, 128)])
-def test_generate_token_identical(mc, model_path, shape, seed, n_ctx, n_prompt, n_predict):
+def test_generate_token_identical(mc, model_path, qkv_attn_path, shape, seed, n_ctx, n_prompt, n_predict):
     path = model_path(shape, seed)
     ref = mi_oracle.ReferenceModel(path, n_ctx=n_ctx, n_threads=os.cpu_count() or 1)
     model = mc.Qwen2Model(path)
     kv = mc.KVCache(model, n_ctx)
+    assert kernels_per_layer(kv, model) == qkv_attn_path
     prompt = np.random.default_rng(seed).integers(0, ref.n_vocab, n_prompt).astype(np.int32)
     want, _, _ = ref.generate(prompt, n_predict)
     got, pre_ms, dec_ms = kv.generate(prompt, n_predict)
@@ -75,18 +93,23 @@ def test_generate_token_identical(mc, model_path, shape, seed, n_ctx, n_prompt, 
     model.free()
 
 
-def test_step_trace(mc, model_path):
+def test_step_trace(mc, model_path, qkv_attn_path):
     path = model_path("SMALL", 4)
     model = mc.Qwen2Model(path)
     kv = mc.KVCache(model, 64)
     kv.set_position(np.array([1, 2, 3], dtype=np.int32), 2)
     kv.decode_steps(3)
     t = kv.step_trace().astype(np.int64)
-    assert t.shape == (kv.kernels_per_step, 8) == (5 * 4 + 1, 8)
+    per = qkv_attn_path
+    assert t.shape == (kv.kernels_per_step, 8) == (per * 4 + 1, 8)
     assert np.all(t[:, :4] > 0)
     assert np.all(np.diff(t[:, :4], axis=1) >= 0)    # entry <= dep done <= prologue <= epilogue
-    attn = t[1::5][:4]                               # attention phases: scores, exp, sum, KV
-    assert np.all(np.diff(attn[:, [2, 4, 5, 6, 7]], axis=1) >= 0)
+    if per == 5:
+        attn = t[1::5][:4]                           # attention phases: scores, exp, sum, KV
+        assert np.all(np.diff(attn[:, [2, 4, 5, 6, 7]], axis=1) >= 0)
+    else:
+        fused = t[0::4][:4]                          # prologue, k/v handed over, scores, exp, sum, KV
+        assert np.all(np.diff(fused[:, [2, 4, 5, 6, 7, 3]], axis=1) >= 0)
     assert np.all(t[1:, 1] >= t[:-1, 1])             # kernels' dependent sections run in order
     assert t[-1, 3] - t[0, 0] < 10_000_000           # the step took less than 10 ms
     kv.free()
@@ -114,6 +137,32 @@ def test_context_limit_matches_reference(mc, model_path):
     kv.free()
     model.free()
     ref.close()
+
+
+def test_decode_past_context_reports_state_error(mc, model_path, qkv_attn_path):
+    """A device-resident step at position n_ctx (no cache row left) records
+    MI_CUDA_ERR_STATE instead of writing; the cache stays usable."""
+    path = model_path("SMALL", 4)
+    n_ctx = 24
+    ref = mi_oracle.ReferenceModel(path, n_ctx=n_ctx)
+    model = mc.Qwen2Model(path)
+    kv = mc.KVCache(model, n_ctx)
+    prompt = np.arange(1, 21, dtype=np.int32)
+    want, _, _ = ref.generate(prompt, 4)
+    kv.forward(prompt, 0, last_logits_only=True)  # the prompt's cache rows
+    assert kv.last_token() == want[0]
+    seed = np.concatenate([prompt, want[:1]]).astype(np.int32)
+    kv.set_position(seed, prompt.size)
+    kv.decode_steps(n_ctx - prompt.size + 1)     # the last step is at pos == n_ctx
+    with pytest.raises(mc.MiCudaError) as e:
+        kv.read_tokens(prompt.size, 2)
+    assert e.value.code == mc.ERR_STATE
+    kv.set_position(seed, prompt.size)
+    kv.decode_steps(3)
+    assert np.array_equal(kv.read_tokens(prompt.size, 4), want)
+    ref.close()
+    kv.free()
+    model.free()
 
 
 @pytest.mark.slow
