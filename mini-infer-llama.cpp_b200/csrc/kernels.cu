@@ -666,9 +666,11 @@ GemvPlan plan_gemv(int64_t k, int64_t n, int num_sms, int pro, int32_t rows_per_
     tiles = (pl.rows_per_cta + sr - 1) / sr;
   }
   pl.stage_rows = (int32_t)sr;
-  // Wide stages (>= 64 rows keep >= 4 warps busy) use 2 threads per row and
-  // 16-byte loads; narrow ones use 8 threads per row for more parallelism.
-  pl.tpr = pl.stage_rows >= 64 ? 2 : 8;
+  // 2 threads per row with 16-byte loads: a quarter of the shared-memory loads
+  // of 8 threads per row, and the same code as the other narrow GEMVs of the
+  // step (measured faster on B200 even for 8-row CTAs, where only 16 threads
+  // of the CTA compute).
+  pl.tpr = 2;
   if (const char* e = std::getenv("MI_CUDA_GEMV_TPR")) {
     const int v = std::atoi(e);
     if (v == 2 || v == 8) pl.tpr = v;

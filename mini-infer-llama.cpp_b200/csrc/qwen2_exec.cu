@@ -982,9 +982,12 @@ int graphs_ready(mi_cuda_kv_cache* kv) {
 }
 
 int check_state_error(mi_cuda_kv_cache* kv) {
+  // The error word into pinned memory behind the stream's work: one host
+  // round trip per call.
+  CK(cudaMemcpyAsync(&kv->h_state->err, &kv->state->err, sizeof(int32_t), cudaMemcpyDeviceToHost,
+                     kv->stream));
   CK(cudaStreamSynchronize(kv->stream));
-  int32_t err = 0;
-  CK(cudaMemcpy(&err, &kv->state->err, 4, cudaMemcpyDeviceToHost));
+  const int32_t err = kv->h_state->err;
   if (err) {
     CK(cudaMemset(&kv->state->err, 0, 4));
     if (err == MI_CUDA_ERR_TIMEOUT) return fail(MI_CUDA_ERR_TIMEOUT, "a device-side wait timed out");
