@@ -139,6 +139,14 @@ __device__ __forceinline__ uint32_t dsmem_addr(const void* p, uint32_t rank) {
 __device__ __forceinline__ void dsmem_store(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
+// Four floats into another CTA's shared memory at `addr`, counted (16 bytes)
+// on that CTA's mbarrier `bar` (both shared::cluster addresses from
+// dsmem_addr); the receiver waits on its barrier like on a bulk copy.
+__device__ __forceinline__ void dsmem_store_async(uint32_t addr, float4 v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
+               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(bar)
+               : "memory");
+}
 __device__ __forceinline__ float dsmem_load(uint32_t addr) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");

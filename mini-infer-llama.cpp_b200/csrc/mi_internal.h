@@ -183,7 +183,7 @@ struct QkvAttnParams {
   // Detail slots: CTA 0 (query CTA of head 0) and CTA n_rep (the first k/v
   // CTA) store 0 entry, 1 dependency satisfied, 2 x loaded, 3 rms_norm sum
   // done, 4 prologue done, 5 rows done, 6 bias + RoPE done, 7 hand-over done
-  // (query CTA: k / v read; k/v CTA: every query CTA arrived).
+  // (query CTA: k / v received; k/v CTA: k / v sent).
   int32_t trace_slot_q, trace_slot_kv;
 };
 struct QkvAttnPlan {

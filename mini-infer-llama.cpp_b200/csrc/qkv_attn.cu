@@ -82,7 +82,7 @@ __host__ __device__ inline FusedSmem fused_smem(int64_t K, int32_t D, int32_t kt
 
 __global__ void __launch_bounds__(kNT, 1) qkv_attn_kernel(const QkvAttnParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ float qr[256], kr[256], vr[256];
+  __shared__ __align__(16) float qr[256], kr[256], vr[256];
   __shared__ float red[kNW];
   __shared__ float sh[2];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -96,7 +96,8 @@ __global__ void __launch_bounds__(kNT, 1) qkv_attn_kernel(const QkvAttnParams p)
   const int h = kvh * n_rep + crank;  // query head (query CTAs)
   const int KT = p.kv_tile, KP = D + 1;
   const FusedSmem L = fused_smem(K, D, KT, 0);
-  uint64_t* bar = (uint64_t*)smem;
+  uint64_t* bar = (uint64_t*)smem;         // the CTA's weight copies
+  uint64_t* bar_kv = (uint64_t*)(smem + 8);  // query CTAs: k and v from the k/v CTA
   float* misc = (float*)(smem + 16);
   int8_t* aq = (int8_t*)(smem + L.aq);
   float* ad = (float*)(smem + L.ad);
@@ -130,10 +131,15 @@ __global__ void __launch_bounds__(kNT, 1) qkv_attn_kernel(const QkvAttnParams p)
   // ---- before the dependency wait: weights and cached K / V into shared memory ----
   if (tid == 0) {
     mbar_init(bar, 1);
+    mbar_init(bar_kv, 1);
     fence_mbar_init();
   }
   __syncthreads();
+  // Cluster phase 0: every CTA's barriers are initialized (the k/v CTA stores
+  // into the query CTAs' shared memory only after it).
+  cluster_arrive_relaxed();
   if (tid == 0) {
+    if (!kv_cta) mbar_arrive_expect_tx(bar_kv, (uint32_t)(2 * D * 4));
     // D rows from packed row r (a multiple of 8): quants at r * K, scales at
     // r * nb * 2 bytes into the scale plane
     const uint32_t qb = (uint32_t)((int64_t)D * K), db = (uint32_t)(D * nb * 2);
@@ -345,35 +351,36 @@ __global__ void __launch_bounds__(kNT, 1) qkv_attn_kernel(const QkvAttnParams p)
   __syncthreads();
   mark(6);
 
-  // ---- k / v hand-over: the query CTAs read them from the k/v CTA ----
-  // Phase A: k / v are in the k/v CTA's kr / vr. Phase B: every query CTA has
-  // read them (the k/v CTA's shared memory stays allocated until then).
+  // ---- k / v hand-over ----
+  // The k/v CTA stores k and v into every query CTA's kr / vr with st.async,
+  // counted on that CTA's bar_kv; a query CTA waits on its own barrier.
+  // Cluster phase 1: every query CTA has received them (the k/v CTA exits
+  // only then).
   if (kv_cta) {
-    cluster_arrive_release();
-    if (ok && tid < D) {  // the KV-cache append, off the query CTAs' path
+    cluster_wait_acquire();  // phase 0
+    const int per = D >> 1;  // float4s per query CTA: k then v
+    for (int e = tid; e < n_rep * per; e += kNT) {
+      const int c = e / per, i4 = e - c * per;
+      const float* src = i4 < D4 ? kr + 4 * i4 : vr + 4 * (i4 - D4);
+      dsmem_store_async(dsmem_addr(src, (uint32_t)c), *(const float4*)src, dsmem_addr(bar_kv, (uint32_t)c));
+    }
+    if (ok && tid < D) {  // the KV-cache append
       p.cache_k[((size_t)n_past * HKV + kvh) * D + tid] = kr[tid];
       p.cache_v[((size_t)n_past * HKV + kvh) * D + tid] = vr[tid];
     }
-    cluster_wait_acquire();
     mark(7);
     cluster_arrive_relaxed();
-    cluster_wait_acquire();
+    cluster_wait_acquire();  // phase 1
     if (!ok && tid == 0) (void)mbar_wait_bounded(bar, 0u, nullptr);
     return;
   }
-  cluster_arrive_relaxed();
-  cluster_wait_acquire();
-  if (tid < D) {
-    const float kv0 = dsmem_load(dsmem_addr(&kr[tid], (uint32_t)n_rep));
-    const float kv1 = dsmem_load(dsmem_addr(&vr[tid], (uint32_t)n_rep));
-    kr[tid] = kv0;
-    vr[tid] = kv1;
-    if (n_past < KT) {
-      Ks[(size_t)n_past * KP + tid] = kv0;
-      Vs[(size_t)n_past * D + tid] = kv1;
-    }
+  (void)mbar_wait_bounded(bar_kv, 0u, p.err);
+  if (n_past < KT && tid < D) {
+    Ks[(size_t)n_past * KP + tid] = kr[tid];
+    Vs[(size_t)n_past * D + tid] = vr[tid];
   }
-  cluster_arrive_release();
+  cluster_wait_acquire();  // phase 0
+  cluster_arrive_relaxed();
   __syncthreads();
   trace_mark(p.trace, p.trace_slot, 4);
   mark(7);
@@ -457,7 +464,7 @@ __global__ void __launch_bounds__(kNT, 1) qkv_attn_kernel(const QkvAttnParams p)
   } else if (tid < D) {
     p.out[(size_t)h * D + tid] = acc;
   }
-  cluster_wait_acquire();  // phase B (passed long ago: the k/v CTA arrives right after phase A)
+  cluster_wait_acquire();  // phase 1
 }
 
 int g_optin = 0;  // the device's opt-in shared memory per block (prepare_qkv_attn_kernel)

@@ -84,6 +84,27 @@ def test_gemv_config1_bitexact(mc, S, torch_cuda, n, k):
     assert np.array_equal(isums, (wq * aq[None]).sum(-1))
 
 
+@pytest.mark.parametrize("n,k,var,val", [(896, 4864, "MI_CUDA_GEMV_WIDE", "8,8,8"),
+                                         (896, 4864, "MI_CUDA_GEMV_WIDE", "8,8,4"),
+                                         (200, 2080, "MI_CUDA_GEMV_TPR", "8"),
+                                         (896, 4864, "MI_CUDA_GEMV_WIDE", "2,8,64")])
+def test_gemv_stage_layouts_bitexact(mc, S, torch_cuda, monkeypatch, n, k, var, val):
+    """The 8-thread mapping's quad loads under every stage shape: K-chunks of
+    30 and 14 blocks (chunks starting off a multiple of 4 blocks), an odd
+    number of blocks per row (K = 2080: no quad loads), and the 2-thread
+    mapping on wide rows."""
+    monkeypatch.setenv(var, val)
+    torch = torch_cuda
+    rng = np.random.default_rng(n + 7 * k)
+    w = mi_gguf.quantize_q8_0(rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)).view(np.uint8)
+    x = rng.standard_normal((1, k), dtype=np.float32)
+    act = S.quantize_act(x)
+    want = S.mul_mat(w, k, n, act, 1)
+    wp = mc.q8_0_pack(dev(torch, w.reshape(-1)), k, n)
+    assert np.array_equal(bits(mc.mul_mat(wp, k, n, x=dev(torch, x)).cpu().numpy()), bits(want))
+    assert np.array_equal(bits(mc.mul_mat(wp, k, n, act=dev(torch, act.reshape(-1))).cpu().numpy()), bits(want))
+
+
 def test_gemv_multi_column_and_relative_tolerance(mc, R, torch_cuda):
     torch = torch_cuda
     rng = np.random.default_rng(77)
