@@ -112,8 +112,8 @@ inline cudaError_t set_carveout(F* func) {
 
 // ---------------------------------------------------------------------------
 // Thread-block clusters: the hardware cluster barrier (every thread of every
-// CTA arrives, then waits; exited threads do not count) and stores into
-// another CTA's shared memory (distributed shared memory).
+// CTA arrives, then waits; exited threads do not count) and asynchronous
+// stores into another CTA's shared memory (distributed shared memory).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -122,9 +122,6 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 }
 __device__ __forceinline__ void cluster_arrive_relaxed() {
   asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_arrive_release() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait_acquire() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -136,9 +133,6 @@ __device__ __forceinline__ uint32_t dsmem_addr(const void* p, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_addr(p)), "r"(rank));
   return a;
 }
-__device__ __forceinline__ void dsmem_store(uint32_t addr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
 // Four floats into another CTA's shared memory at `addr`, counted (16 bytes)
 // on that CTA's mbarrier `bar` (both shared::cluster addresses from
 // dsmem_addr); the receiver waits on its barrier like on a bulk copy.
@@ -146,11 +140,6 @@ __device__ __forceinline__ void dsmem_store_async(uint32_t addr, float4 v, uint3
   asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
                "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(bar)
                : "memory");
-}
-__device__ __forceinline__ float dsmem_load(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
 }
 
 // ---------------------------------------------------------------------------
