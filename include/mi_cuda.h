@@ -92,6 +92,13 @@ int mi_cuda_mul_mat_q8_0(const void* d_w_packed, int64_t k, int64_t n, const voi
 int mi_cuda_mul_mat_q8_0_f32(const void* d_w_packed, int64_t k, int64_t n, const float* d_x,
                              int64_t m, float* d_dst, mi_cuda_stream s);
 
+/* mi_compute_mul_mat with the reference's scalar dot (MI_QUANT_FORCE_SCALAR,
+ * ref src/quant.cpp:221-239): d_dst[j*n + i] = fma chain over the blocks of
+ * (float)isum * (fp16(w.d) * a.d), one accumulator per row. For parity with a
+ * reference run on the scalar path; the decode path uses the AVX2 order. */
+int mi_cuda_mul_mat_q8_0_scalar(const void* d_w_packed, int64_t k, int64_t n, const void* d_act,
+                                int64_t m, float* d_dst, mi_cuda_stream s);
+
 /* Per-block int32 sums of W row i x act row 0 (sum of the 8 lane partials,
  * ref mi_q8_0_block_isum_avx2, src/quant_avx2.cpp:121-124), computed by the
  * GEMV's own dp4a path: d_isums[i*(k/32) + b]. */

@@ -1136,6 +1136,50 @@ cudaError_t launch_block_isums(const uint8_t* w, int64_t k, int64_t n, int64_t n
   return cudaGetLastError();
 }
 
+// The reference's scalar dispatch of the Q8_0 x Q8_0_ACT dot, selected there
+// by MI_QUANT_FORCE_SCALAR (ref src/quant.cpp:221-230, 232-239): one
+// accumulator per row, acc = fma((float)isum_i, fp16(w.d_i) * a.d_i, acc) over
+// blocks i in order, isum_i the block's exact int32 sum. One warp per (row,
+// column): the lanes form 32 blocks' sums and scale products at a time, then
+// every lane runs the chain over them in block order (shuffled from lane t).
+__global__ void gemv_q8_scalar_order_kernel(const uint8_t* w, int64_t K, int64_t n, int64_t npad,
+                                            const uint8_t* act, float* dst) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t j = blockIdx.y;
+  if (r >= n) return;  // whole warps
+  const int64_t nb = K / 32;
+  const uint8_t* a = act + j * nb * 36;
+  float acc = 0.0f;
+  for (int64_t b0 = 0; b0 < nb; b0 += 32) {
+    int isum = 0;
+    float dxdy = 0.0f;
+    const int64_t b = b0 + lane;
+    if (b < nb) {
+      const int* wq = (const int*)packed_qs(w, K, r, b);
+      const int* aq = (const int*)(a + b * 36 + 4);
+#pragma unroll
+      for (int k = 0; k < 8; k++) isum = __dp4a(wq[k], aq[k], isum);
+      dxdy = __fmul_rn(packed_scale(w, K, npad, r, b), *(const float*)(a + b * 36));
+    }
+    const int cnt = (int)min((int64_t)32, nb - b0);
+    for (int t = 0; t < cnt; t++) {
+      const int is = __shfl_sync(FULL, isum, t);
+      const float dx = __shfl_sync(FULL, dxdy, t);
+      acc = __fmaf_rn(__int2float_rn(is), dx, acc);
+    }
+  }
+  if (lane == 0) dst[j * n + r] = acc;
+}
+
+cudaError_t launch_gemv_scalar_order(const uint8_t* w, int64_t k, int64_t n, int64_t n_pad,
+                                     const uint8_t* act, int64_t m, float* dst, cudaStream_t s) {
+  if (n == 0 || m == 0) return cudaSuccess;
+  const dim3 grid((unsigned)((n + 7) / 8), (unsigned)m);
+  gemv_q8_scalar_order_kernel<<<grid, 256, 0, s>>>(w, k, n, n_pad, act, dst);
+  return cudaGetLastError();
+}
+
 // mi_compute_get_rows on a Q8_0 table (src/ops_cpu.cpp:128-139).
 __global__ void get_rows_kernel(const uint8_t* table, int64_t ne0, int64_t npad,
                                 const int32_t* ids, int64_t n_ids, float* dst) {

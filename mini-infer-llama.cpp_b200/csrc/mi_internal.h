@@ -280,6 +280,10 @@ cudaError_t launch_quantize_act(const float* x, int64_t k, int64_t m, uint8_t* a
                                 cudaStream_t s);
 cudaError_t launch_block_isums(const uint8_t* w, int64_t k, int64_t n, int64_t n_pad,
                                const uint8_t* act, int32_t* isums, cudaStream_t s);
+// dst[j*n + i] = dot(W row i, act row j) in the reference's scalar order (one
+// fma chain over the blocks' int32 sums).
+cudaError_t launch_gemv_scalar_order(const uint8_t* w, int64_t k, int64_t n, int64_t n_pad,
+                                     const uint8_t* act, int64_t m, float* dst, cudaStream_t s);
 cudaError_t launch_get_rows(const uint8_t* table, int64_t ne0, int64_t n_pad,
                             const int32_t* ids, int64_t n_ids, float* dst, cudaStream_t s);
 cudaError_t launch_rms_norm(const float* x, int64_t ne0, int64_t n_rows, float eps, float* dst,

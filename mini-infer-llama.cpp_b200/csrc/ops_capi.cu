@@ -246,6 +246,16 @@ int mi_cuda_mul_mat_q8_0_f32(const void* d_w_packed, int64_t k, int64_t n, const
   return mul_mat_common(d_w_packed, k, n, d_x, m, d_dst, s, PRO_QUANT);
 }
 
+int mi_cuda_mul_mat_q8_0_scalar(const void* d_w_packed, int64_t k, int64_t n, const void* d_act,
+                                int64_t m, float* d_dst, mi_cuda_stream s) {
+  MI_CTX(c);
+  MI_REQUIRE(d_w_packed && d_act && d_dst && k > 0 && n > 0 && m >= 0 && m <= 65535 && k % 32 == 0,
+             "mi_cuda_mul_mat_q8_0_scalar: bad arguments");
+  return cuda_status(launch_gemv_scalar_order((const uint8_t*)d_w_packed, k, n, npad8(n),
+                                              (const uint8_t*)d_act, m, d_dst, S(s)),
+                     "mul_mat_q8_0_scalar");
+}
+
 int mi_cuda_q8_0_block_isums(const void* d_w_packed, int64_t k, int64_t n, const void* d_act,
                              int32_t* d_isums, mi_cuda_stream s) {
   MI_CTX(c);

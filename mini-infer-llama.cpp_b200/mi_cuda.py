@@ -53,6 +53,7 @@ _SIGS = {
     "mi_cuda_quantize_q8_0_act": (I32, [P, I64, I64, P, P]),
     "mi_cuda_mul_mat_q8_0": (I32, [P, I64, I64, P, I64, P, P]),
     "mi_cuda_mul_mat_q8_0_f32": (I32, [P, I64, I64, P, I64, P, P]),
+    "mi_cuda_mul_mat_q8_0_scalar": (I32, [P, I64, I64, P, I64, P, P]),
     "mi_cuda_q8_0_block_isums": (I32, [P, I64, I64, P, P, P]),
     "mi_cuda_get_rows_q8_0": (I32, [P, I64, I64, P, I64, P, P]),
     "mi_cuda_rms_norm": (I32, [P, I64, I64, F32, P, P]),
@@ -178,6 +179,14 @@ def mul_mat(w_packed, k: int, n: int, act=None, x=None, m: int = 1):
         check(lib().mi_cuda_mul_mat_q8_0(_p(w_packed), k, n, _p(act), m, _p(out), _stream()))
     else:
         check(lib().mi_cuda_mul_mat_q8_0_f32(_p(w_packed), k, n, _p(x), m, _p(out), _stream()))
+    return out
+
+
+def mul_mat_scalar(w_packed, k: int, n: int, act, m: int = 1):
+    """mi_compute_mul_mat on the reference's scalar dot path (MI_QUANT_FORCE_SCALAR)."""
+    torch = _torch()
+    out = torch.empty((m, n), dtype=torch.float32, device=w_packed.device)
+    check(lib().mi_cuda_mul_mat_q8_0_scalar(_p(w_packed), k, n, _p(act), m, _p(out), _stream()))
     return out
 
 

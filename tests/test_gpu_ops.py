@@ -105,6 +105,26 @@ def test_gemv_stage_layouts_bitexact(mc, S, torch_cuda, monkeypatch, n, k, var, 
     assert np.array_equal(bits(mc.mul_mat(wp, k, n, act=dev(torch, act.reshape(-1))).cpu().numpy()), bits(want))
 
 
+@pytest.mark.parametrize("n,k,m", [(896, 896, 1), (128, 896, 2), (896, 4864, 1), (12, 1056, 3)])
+def test_gemv_scalar_order_bitexact(mc, S, R, torch_cuda, n, k, m):
+    """The reference's scalar dot (MI_QUANT_FORCE_SCALAR path): bit-exact
+    against the oracle's restatement and the reference's own scalar dot."""
+    torch = torch_cuda
+    rng = np.random.default_rng(n * 5 + k + m)
+    w = mi_gguf.quantize_q8_0(rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)).view(np.uint8)
+    act = S.quantize_act(rng.standard_normal((m, k), dtype=np.float32))
+    wr = w.reshape(n, k // 32 * 34)
+    want = np.empty((m, n), dtype=np.float32)
+    for j in range(m):
+        for i in range(n):
+            want[j, i] = S.lib.mio_vec_dot_q8_0_wact_scalar(wr[i].ctypes.data, act[j].ctypes.data, k)
+    i = n // 2
+    assert np.float32(R.lib.mi_ref_vec_dot_q8_0_wact_scalar(wr[i].ctypes.data, act[0].ctypes.data, k)) == want[0, i]
+    wp = mc.q8_0_pack(dev(torch, w.reshape(-1)), k, n)
+    got = mc.mul_mat_scalar(wp, k, n, dev(torch, act.reshape(-1)), m).cpu().numpy()
+    assert np.array_equal(bits(got), bits(want))
+
+
 def test_gemv_multi_column_and_relative_tolerance(mc, R, torch_cuda):
     torch = torch_cuda
     rng = np.random.default_rng(77)
