@@ -343,17 +343,28 @@ def run_attention(args):
         scratch = torch.empty(L.mi_cuda_attention_decode_scratch_bytes(H, n_kv), dtype=torch.uint8, device="cuda")
         st = torch.cuda.current_stream().cuda_stream
 
+        split_scratch = torch.empty(L.mi_cuda_attention_decode_split_scratch_bytes(H, HKV, n_kv, D),
+                                    dtype=torch.uint8, device="cuda")
+
         def fn(i):
             mi_cuda.check(L.mi_cuda_attention_decode(q.data_ptr(), ks[i].data_ptr(), vs[i].data_ptr(), D, H, HKV,
                                                      n_kv, 0.125, scratch.data_ptr(), out.data_ptr(), st))
 
-        ms = _time_rotating(torch, fn, n_copies, args.steps, args.warmup)
+        def fn_split(i):
+            mi_cuda.check(L.mi_cuda_attention_decode_split(q.data_ptr(), ks[i].data_ptr(), vs[i].data_ptr(), D, H,
+                                                           HKV, n_kv, 0.125, split_scratch.data_ptr(),
+                                                           out.data_ptr(), st))
+
         algo = kvb + 2 * H * D * 4
-        gbs = algo / (ms / 1e3) / 1e9
-        print(json.dumps({"config": "attention", "n_kv": n_kv, "us_per_launch": ms * 1e3,
-                          "bytes_per_launch": algo, "achieved_gbs": gbs, "peak_gbs": peak,
-                          "frac": gbs / peak, "peak_kind": peak_kind, "kv_copies": n_copies,
-                          "launches": args.steps}), flush=True)
+        # exact: the reference's summation order (bit-identical); split: positions
+        # split over CTAs, sums regrouped (labelled fast mode, not bit-identical)
+        for mode, f in (("exact", fn), ("split", fn_split)):
+            ms = _time_rotating(torch, f, n_copies, args.steps, args.warmup)
+            gbs = algo / (ms / 1e3) / 1e9
+            print(json.dumps({"config": "attention", "mode": mode, "n_kv": n_kv, "us_per_launch": ms * 1e3,
+                              "bytes_per_launch": algo, "achieved_gbs": gbs, "peak_gbs": peak,
+                              "frac": gbs / peak, "peak_kind": peak_kind, "kv_copies": n_copies,
+                              "launches": args.steps}), flush=True)
         del ks, vs
 
 

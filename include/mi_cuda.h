@@ -159,6 +159,19 @@ int mi_cuda_attention_decode(const float* d_q, const float* d_cache_k, const flo
                              int64_t head_dim, int64_t n_head, int64_t n_head_kv, int64_t n_kv,
                              float scale, void* d_scratch, float* d_dst, mi_cuda_stream s);
 
+/* No counterpart in the reference: a fast mode of mi_cuda_attention_decode
+ * (same inputs and output layout) that splits the positions over many CTAs and
+ * combines their partial softmax sums. Each score and exponential is the
+ * reference's, but the denominator and value sums are regrouped, so results
+ * differ from the reference's in the last bits (|error| ~1e-7 relative on
+ * N(0,1) data). head_dim <= 128 and a multiple of 4, n_head / n_head_kv <= 16.
+ * d_scratch holds mi_cuda_attention_decode_split_scratch_bytes() bytes. */
+size_t mi_cuda_attention_decode_split_scratch_bytes(int64_t n_head, int64_t n_head_kv, int64_t n_kv,
+                                                    int64_t head_dim);
+int mi_cuda_attention_decode_split(const float* d_q, const float* d_cache_k, const float* d_cache_v,
+                                   int64_t head_dim, int64_t n_head, int64_t n_head_kv, int64_t n_kv,
+                                   float scale, void* d_scratch, float* d_dst, mi_cuda_stream s);
+
 /* No counterpart in the reference. mi_cuda_attention_decode for callers that
  * cannot allocate device memory on their call path (a zero-allocation runtime
  * after start-up, code running while the caller records a CUDA graph, a plugin

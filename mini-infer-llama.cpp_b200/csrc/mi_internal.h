@@ -141,6 +141,16 @@ struct AttnParams {
 cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t s, bool pdl,
                                bool tp = false, int32_t n_queries = 1);
 
+// Decode attention split over positions (attn_split.cu): a fast mode that
+// regroups the softmax and value sums (not bit-exact). part holds
+// attn_split_scratch_bytes() bytes.
+bool attn_split_fits(int64_t head_dim, int64_t n_head, int64_t n_head_kv);
+void attn_split_shape(int64_t n_kv, int64_t n_head_kv, int32_t* n_splits, int32_t* per_split);
+size_t attn_split_scratch_bytes(int64_t n_head, int64_t n_kv, int64_t n_head_kv, int64_t head_dim);
+cudaError_t launch_attn_split(const float* q, const float* ck, const float* cv, int64_t D, int64_t H, int64_t HKV,
+                              int64_t n_kv, float scale, const ExpTab& et, float* part, float* out,
+                              cudaStream_t s);
+
 // ---------------------------------------------------------------------------
 // Fused QKV projection + decode attention (executor, one GPU)
 // ---------------------------------------------------------------------------

@@ -425,6 +425,24 @@ int mi_cuda_attention_decode(const float* d_q, const float* d_cache_k, const flo
   return cuda_status(launch_attn_decode(p, false, S(s), false), "attention_decode");
 }
 
+size_t mi_cuda_attention_decode_split_scratch_bytes(int64_t n_head, int64_t n_head_kv, int64_t n_kv,
+                                                    int64_t head_dim) {
+  if (n_head <= 0 || n_head_kv <= 0 || n_kv <= 0 || head_dim <= 0) return 0;
+  return attn_split_scratch_bytes(n_head, n_kv, n_head_kv, head_dim);
+}
+
+int mi_cuda_attention_decode_split(const float* d_q, const float* d_cache_k, const float* d_cache_v,
+                                   int64_t head_dim, int64_t n_head, int64_t n_head_kv, int64_t n_kv,
+                                   float scale, void* d_scratch, float* d_dst, mi_cuda_stream s) {
+  MI_CTX(c);
+  MI_REQUIRE(d_q && d_cache_k && d_cache_v && d_scratch && d_dst && n_kv > 0 && n_kv < (1ll << 31) &&
+                 attn_split_fits(head_dim, n_head, n_head_kv),
+             "mi_cuda_attention_decode_split: bad arguments");
+  return cuda_status(launch_attn_split(d_q, d_cache_k, d_cache_v, head_dim, n_head, n_head_kv, n_kv, scale,
+                                       c->et, (float*)d_scratch, d_dst, S(s)),
+                     "attention_decode_split");
+}
+
 int mi_cuda_argmax(const float* d_x, int64_t n, int32_t* d_out, mi_cuda_stream s) {
   MI_CTX(c);
   MI_REQUIRE(d_x && d_out && n > 0 && n < (1ll << 31), "mi_cuda_argmax: bad arguments");

@@ -68,6 +68,8 @@ _SIGS = {
     "mi_cuda_attention_decode_scratch_bytes": (SZ, [I64, I64]),
     "mi_cuda_attention_decode": (I32, [P, P, P, I64, I64, I64, I64, F32, P, P, P]),
     "mi_cuda_attention_decode_noalloc": (I32, [P, P, P, I64, I64, I64, I64, F32, P, P]),
+    "mi_cuda_attention_decode_split_scratch_bytes": (SZ, [I64, I64, I64, I64]),
+    "mi_cuda_attention_decode_split": (I32, [P, P, P, I64, I64, I64, I64, F32, P, P, P]),
     "mi_cuda_argmax": (I32, [P, I64, P, P]),
     "mi_cuda_expf": (I32, [P, I64, P, P]),
     "mi_cuda_expf_verify": (I32, [U64, U64, P]),
@@ -293,6 +295,19 @@ def attention_decode(q, cache_k, cache_v, n_head_kv: int, n_kv: int, scale_: flo
     out = torch.empty((H, D), dtype=torch.float32, device=q.device)
     check(lib().mi_cuda_attention_decode(_p(q), _p(cache_k), _p(cache_v), D, H, n_head_kv, n_kv, scale_,
                                          _p(scratch), _p(out), _stream()))
+    return out
+
+
+def attention_decode_split(q, cache_k, cache_v, n_head_kv: int, n_kv: int, scale_: float, scratch=None):
+    """Split-over-positions fast mode of attention_decode (regrouped sums, not bit-exact)."""
+    torch = _torch()
+    H, D = q.shape
+    if scratch is None:
+        nb = lib().mi_cuda_attention_decode_split_scratch_bytes(H, n_head_kv, n_kv, D)
+        scratch = torch.empty(nb, dtype=torch.uint8, device=q.device)
+    out = torch.empty((H, D), dtype=torch.float32, device=q.device)
+    check(lib().mi_cuda_attention_decode_split(_p(q), _p(cache_k), _p(cache_v), D, H, n_head_kv, n_kv, scale_,
+                                               _p(scratch), _p(out), _stream()))
     return out
 
 

@@ -233,6 +233,25 @@ def test_attention_decode_config2(mc, S, torch_cuda, n_kv):
     assert np.array_equal(bits(got), bits(want[0]))
 
 
+@pytest.mark.parametrize("n_kv,H,HKV,D", [(1, 14, 2, 64), (33, 14, 2, 64), (1024, 14, 2, 64), (32768, 14, 2, 64),
+                                          (4100, 28, 4, 128), (300, 4, 4, 16)])
+def test_attention_decode_split_mode_tolerance(mc, S, torch_cuda, n_kv, H, HKV, D):
+    """The split-over-positions fast mode against the reference-order oracle:
+    regrouped sums, so within max-abs 1e-5 and cosine >= 0.999999 of the exact
+    output rather than bit-identical."""
+    torch = torch_cuda
+    rng = np.random.default_rng(n_kv + H)
+    q = rng.standard_normal((1, H, D), dtype=np.float32)
+    k = rng.standard_normal((n_kv, HKV, D), dtype=np.float32)
+    v = rng.standard_normal((n_kv, HKV, D), dtype=np.float32)
+    scale = float(np.float32(1.0 / np.sqrt(D)))
+    _, _, want = S.attention(q, k, v, HKV, n_kv - 1, 1, scale)
+    got = mc.attention_decode_split(dev(torch, q[0]), dev(torch, k), dev(torch, v), HKV, n_kv, scale).cpu().numpy()
+    a, b = got.astype(np.float64).ravel(), want[0].astype(np.float64).ravel()
+    assert np.max(np.abs(a - b)) <= 1e-5
+    assert a @ b / (np.linalg.norm(a) * np.linalg.norm(b)) >= 0.999999
+
+
 def test_argmax_first_max(mc, torch_cuda):
     torch = torch_cuda
     rng = np.random.default_rng(1)
