@@ -39,6 +39,11 @@ def test_pure_host_entry_points_without_gpu():
     assert L.mi_cuda_q8_0_packed_bytes(896, 4) == 8 * 896 * 34 // 32  # rows padded to 8
     assert L.mi_cuda_q8_0_packed_bytes(33, 4) == 0
     assert L.mi_cuda_attention_decode_scratch_bytes(14, 128) == 14 * 128 * 4
+    # split mode: 32768 positions over 2 KV heads -> 256 splits of 128 positions,
+    # each (maximum, denominator, 64 value sums) per query head
+    assert L.mi_cuda_attention_decode_split_scratch_bytes(14, 2, 32768, 64) == 14 * 256 * 66 * 4
+    assert L.mi_cuda_attention_decode_split_scratch_bytes(14, 2, 1, 64) == 14 * 1 * 66 * 4
+    assert L.mi_cuda_attention_decode_split_scratch_bytes(0, 2, 1, 64) == 0
     import numpy as np
     logits = np.array([1.0, 3.0, 3.0, -1.0], dtype=np.float32)
     assert mi_cuda.sample_greedy(logits) == 1  # first index of the maximum
