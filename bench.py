@@ -246,6 +246,57 @@ def run_reference_arm_7b(args):
     }), flush=True)
 
 
+def _time_host(fn, n_copies: int, budget_s: float, min_calls: int = 3):
+    """Seconds per call of fn(copy_index), rotating copies, for about budget_s."""
+    fn(0)
+    n, t0 = 0, time.perf_counter()
+    while n < min_calls or time.perf_counter() - t0 < budget_s:
+        fn(n % n_copies)
+        n += 1
+    return (time.perf_counter() - t0) / n
+
+
+def run_reference_arm_gemv(args):
+    """Config 1 on the reference: its quantize + mul_mat nodes (mi_compute_forward,
+    one thread, as tools/bench_matvec times them), weights rotated through copies
+    larger than the host's last-level cache."""
+    import mi_oracle
+    import mi_gguf
+    R = mi_oracle.Reference()
+    for n, k in [tuple(int(v) for v in sh.split("x")) for sh in args.shapes.split(",")]:
+        rng = np.random.default_rng(n + 3 * k)
+        wbytes = n * k // 32 * 34
+        n_copies = max(1, min(512, -(-256 * 2 ** 20 // wbytes)))  # >= 256 MB of weights in rotation
+        ws = [mi_gguf.quantize_q8_0(rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)).view(np.uint8)
+              for _ in range(min(n_copies, 2))]
+        ws = [ws[i % len(ws)].copy() for i in range(n_copies)]
+        x = rng.standard_normal((1, k), dtype=np.float32)
+        sec = _time_host(lambda i: R.mul_mat(ws[i], k, n, x), n_copies, 1.0)
+        algo = wbytes + k // 32 * 36 + 4 * n + 4 * k
+        print(json.dumps({"config": "gemv", "impl": "reference", "n": n, "k": k, "us_per_call": sec * 1e6,
+                          "bytes_per_call": algo, "achieved_gbs": algo / sec / 1e9, "cores": 1,
+                          "sample": f"mi_compute_forward quantize + mul_mat, 1 thread, {n_copies} weight copies"}),
+              flush=True)
+
+
+def run_reference_arm_attention(args):
+    """Config 2 on the reference: its ATTN_QK, SOFTMAX, ATTN_KQV nodes on one
+    thread (mi_compute_forward), 14 query / 2 KV heads, head_dim 64."""
+    import mi_oracle
+    R = mi_oracle.Reference()
+    H, HKV, D = 14, 2, 64
+    for n_kv in [int(v) for v in args.nkv.split(",")]:
+        rng = np.random.default_rng(n_kv)
+        q = rng.standard_normal((1, H, D), dtype=np.float32)
+        k = rng.standard_normal((n_kv, HKV, D), dtype=np.float32)
+        v = rng.standard_normal((n_kv, HKV, D), dtype=np.float32)
+        sec = _time_host(lambda i: R.attention(q, k, v, HKV, n_kv - 1, 1, 0.125), 1, 1.0)
+        algo = 2 * n_kv * HKV * D * 4 + 2 * H * D * 4
+        print(json.dumps({"config": "attention", "impl": "reference", "n_kv": n_kv, "us_per_call": sec * 1e6,
+                          "bytes_per_call": algo, "achieved_gbs": algo / sec / 1e9, "cores": 1,
+                          "sample": "mi_compute_forward attn_qk + softmax + attn_kqv, 1 thread"}), flush=True)
+
+
 def run_reference_arm(args, rank: int):
     if rank != 0:
         return
@@ -253,6 +304,10 @@ def run_reference_arm(args, rank: int):
         return run_reference_arm_prefill(args)
     if args.config == "tp7b":
         return run_reference_arm_7b(args)
+    if args.config == "gemv":
+        return run_reference_arm_gemv(args)
+    if args.config == "attention":
+        return run_reference_arm_attention(args)
     path = ensure_model(0, None)
     threads = os.cpu_count() or 1
     tps, _, sample = reference_decode(path, args.steps, args.warmup, threads)
@@ -615,9 +670,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.config == "gemv":
+    if args.config == "gemv" and args.impl == "ours":
         return run_gemv_sweep(args)
-    if args.config == "attention":
+    if args.config == "attention" and args.impl == "ours":
         return run_attention(args)
     if args.config == "tp7b" and args.impl == "ours":
         return run_tp7b(args)

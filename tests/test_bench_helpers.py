@@ -41,3 +41,21 @@ def test_prefill_macs():
     head = 151936 * 896
     assert b.prefill_macs(hp05, 1) == per_token + head
     assert b.prefill_macs(hp05, 1024) == 1024 * per_token + head
+
+
+def test_reference_arms_for_ops_print_json(capsys):
+    """Configs 1 and 2 on the reference's own single-thread ops print one line
+    per shape with the metric fields the GPU arms print."""
+    import json
+    import types
+    b = _bench()
+    args = types.SimpleNamespace(shapes="128x896", nkv="64")
+    b.run_reference_arm_gemv(args)
+    b.run_reference_arm_attention(args)
+    lines = [json.loads(x) for x in capsys.readouterr().out.splitlines() if x.startswith("{")]
+    assert [d["config"] for d in lines] == ["gemv", "attention"]
+    for d in lines:
+        assert d["impl"] == "reference" and d["cores"] == 1
+        assert d["us_per_call"] > 0 and d["achieved_gbs"] > 0
+    assert lines[0]["bytes_per_call"] == 128 * 896 // 32 * 34 + 896 // 32 * 36 + 4 * 128 + 4 * 896
+    assert lines[1]["bytes_per_call"] == 2 * 64 * 2 * 64 * 4 + 2 * 14 * 64 * 4
