@@ -120,6 +120,10 @@ struct mi_cuda_kv_cache {
   int32_t* tokens = nullptr;
   StepState* state = nullptr;
   StepState* h_state = nullptr;  // pinned
+  // pinned: the device state as read back by the last check_state_error; valid
+  // (seen_valid) until the next call that enqueues work on the stream
+  StepState* h_seen = nullptr;
+  bool seen_valid = false;
   int32_t* h_tokens = nullptr;   // pinned staging, n_ctx + 1
   cudaGraphExec_t g_head = nullptr, g_nohead = nullptr;
   int32_t kernels_per_step = 0;
@@ -982,12 +986,14 @@ int graphs_ready(mi_cuda_kv_cache* kv) {
 }
 
 int check_state_error(mi_cuda_kv_cache* kv) {
-  // The error word into pinned memory behind the stream's work: one host
-  // round trip per call.
-  CK(cudaMemcpyAsync(&kv->h_state->err, &kv->state->err, sizeof(int32_t), cudaMemcpyDeviceToHost,
-                     kv->stream));
+  // The step state (error word, next token) into pinned memory behind the
+  // stream's work: one host round trip per call, and mi_cuda_qwen2_last_token
+  // right after needs none.
+  kv->seen_valid = false;
+  CK(cudaMemcpyAsync(kv->h_seen, kv->state, sizeof(StepState), cudaMemcpyDeviceToHost, kv->stream));
   CK(cudaStreamSynchronize(kv->stream));
-  const int32_t err = kv->h_state->err;
+  const int32_t err = kv->h_seen->err;
+  if (!err) kv->seen_valid = true;
   if (err) {
     CK(cudaMemset(&kv->state->err, 0, 4));
     if (err == MI_CUDA_ERR_TIMEOUT) return fail(MI_CUDA_ERR_TIMEOUT, "a device-side wait timed out");
@@ -1085,6 +1091,7 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
   build_rope_table(0, n_ctx, (int32_t)D, hp.rope_freq_base, cs.data());
   CK(cudaMemcpy(kv->rope, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
   CK(cudaMallocHost(&kv->h_state, sizeof(StepState)));
+  CK(cudaMallocHost(&kv->h_seen, sizeof(StepState)));
   CK(cudaMallocHost(&kv->h_tokens, (size_t)(n_ctx + 1) * 4));
   CK(cudaStreamCreateWithFlags(&kv->stream, cudaStreamNonBlocking));
   for (auto& e : kv->ev) CK(cudaEventCreate(&e));
@@ -1182,6 +1189,7 @@ void mi_cuda_kv_cache_free(mi_cuda_kv_cache* kv) {
     if (e) cudaEventDestroy(e);
   if (kv->stream) cudaStreamDestroy(kv->stream);
   if (kv->h_state) cudaFreeHost(kv->h_state);
+  if (kv->h_seen) cudaFreeHost(kv->h_seen);
   if (kv->h_tokens) cudaFreeHost(kv->h_tokens);
   cudaFree(kv->buf);
   delete kv;
@@ -1191,6 +1199,7 @@ int mi_cuda_qwen2_set_position(mi_cuda_kv_cache* kv, const int32_t* h_tokens, in
                                int32_t pos) {
   if (!kv || n < 0 || n > kv->n_ctx + 1 || pos < 0 || pos > kv->n_ctx || (n > 0 && !h_tokens))
     return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_set_position: bad arguments");
+  kv->seen_valid = false;
   CK(cudaSetDevice(kv->model->device));
   CK(cudaStreamSynchronize(kv->stream));
   if (n > 0) {
@@ -1209,6 +1218,7 @@ int mi_cuda_qwen2_decode_steps(mi_cuda_kv_cache* kv, int32_t n_steps, int32_t po
   if (!kv || n_steps < 0 || period < 0 || pos0 < 0 || pos0 >= kv->n_ctx)
     return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_decode_steps: bad arguments");
   if (int rc = graphs_ready(kv)) return rc;
+  kv->seen_valid = false;
   CK(cudaSetDevice(kv->model->device));
   for (int32_t i = 0; i < n_steps; i++) {
     if (period > 0 && i > 0 && i % period == 0) CK(launch_set_pos(&kv->state->pos, pos0, kv->stream));
@@ -1256,6 +1266,7 @@ int mi_cuda_qwen2_forward(mi_cuda_model* m, mi_cuda_kv_cache* kv, const int32_t*
   for (int32_t i = 0; i < n_tokens; i++)
     if (h_tokens[i] < 0 || h_tokens[i] >= m->hp.n_vocab)
       return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_forward: token id out of range");
+  kv->seen_valid = false;
   CK(cudaSetDevice(m->device));
   CK(cudaStreamSynchronize(kv->stream));
   std::memcpy(kv->h_tokens + n_past, h_tokens, (size_t)n_tokens * 4);
@@ -1294,6 +1305,10 @@ int mi_cuda_qwen2_forward(mi_cuda_model* m, mi_cuda_kv_cache* kv, const int32_t*
 
 int mi_cuda_qwen2_last_token(mi_cuda_kv_cache* kv, int32_t* h_token_out) {
   if (!kv || !h_token_out) return fail(MI_CUDA_ERR_ARG, "null argument");
+  if (kv->seen_valid) {  // nothing enqueued since the state was read back
+    *h_token_out = kv->h_seen->next_token;
+    return MI_CUDA_OK;
+  }
   CK(cudaSetDevice(kv->model->device));
   CK(cudaMemcpyAsync(&kv->h_state->next_token, &kv->state->next_token, 4, cudaMemcpyDeviceToHost,
                      kv->stream));
