@@ -50,10 +50,10 @@ SEED_MODEL, SEED_PROMPT = 1234, 7
 N_CTX, N_PROMPT, N_PREDICT = 2048, 32, 128
 PERIOD = N_PREDICT - 1  # decode forwards per generated sequence
 METRIC = "decode tok/s (0.5B-shape Q8_0, ctx 2048)"
-PUBLISHED_BEST = 64.035  # reference Q8_0 decode tok/s, 4 threads (README.md:106)
-# DRAM bytes (read + write) of one decode step, summed from ncu captures of every
-# kernel of one step at n_kv = 33 (profiles/decode_step_qwen2_05b.md):
-# 24 x 17.24 MB per layer + 150.3 MB for the LM head.
+PUBLISHED_BEST = 64.035  # reference Q8_0 decode tok/s, 4 threads (reference README.md:106)
+# DRAM bytes (read + write) of one decode step, summed from `ncu --set full`
+# captures (dram__bytes_read.sum + dram__bytes_write.sum) of every kernel of one
+# step at n_kv = 33: 24 x 17.24 MB per layer + 150.3 MB for the LM head.
 TRAFFIC_PER_STEP = 24 * 17.24e6 + 150.3e6
 
 
