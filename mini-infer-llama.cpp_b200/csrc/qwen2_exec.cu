@@ -209,6 +209,13 @@ void shard_range(int64_t units, int rank, int world, int64_t* first, int64_t* co
 
 namespace {
 
+struct ModelDeleter {
+  void operator()(mi_cuda_model* m) const { mi_cuda_qwen2_model_free(m); }
+};
+struct KvCacheDeleter {
+  void operator()(mi_cuda_kv_cache* kv) const { mi_cuda_kv_cache_free(kv); }
+};
+
 int load_model(const char* gguf_path, int device, int rank, int world, mi_cuda_model** out) {
   if (!gguf_path || !out) return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_model_load: null argument");
   if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
@@ -263,7 +270,8 @@ int load_model(const char* gguf_path, int device, int rank, int world, mi_cuda_m
     return MI_CUDA_OK;
   };
 
-  auto m = std::make_unique<mi_cuda_model>();
+  // Any early return releases the partly loaded model with its device memory.
+  std::unique_ptr<mi_cuda_model, ModelDeleter> m(new mi_cuda_model());
   m->device = device;
   m->ctx = ctx;
   m->hp = hp;
@@ -348,7 +356,6 @@ int load_model(const char* gguf_path, int device, int rank, int world, mi_cuda_m
   };
   if (e != cudaSuccess) {
     cleanup();
-    cudaFree(m->buf);
     return fail(MI_CUDA_ERR_CUDA, "staging allocation failed");
   }
   rc = upload_q8(te, m->embed, 0, 4, d_stage, h_stage, stage, s);
@@ -418,10 +425,7 @@ int load_model(const char* gguf_path, int device, int rank, int world, mi_cuda_m
   }
   cleanup();
   if (!rc && cudaGetLastError() != cudaSuccess) rc = fail(MI_CUDA_ERR_CUDA, "weight upload failed");
-  if (rc) {
-    cudaFree(m->buf);
-    return rc;
-  }
+  if (rc) return rc;
   *out = m.release();
   return MI_CUDA_OK;
 }
@@ -1013,7 +1017,8 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
   CK(cudaSetDevice(m->device));
   const mi_cuda_qwen2_hparams& hp = m->hp;
   const int64_t E = hp.n_embd, D = hp.head_dim, kvd = (int64_t)hp.n_head_kv * D, FF = hp.n_ff;
-  auto kv = std::make_unique<mi_cuda_kv_cache>();
+  // Any early return releases the partly built cache with everything it holds.
+  std::unique_ptr<mi_cuda_kv_cache, KvCacheDeleter> kv(new mi_cuda_kv_cache());
   kv->model = m;
   kv->n_ctx = n_ctx;
   // MI_CUDA_NO_PDL=1 captures the step without programmatic dependent launch
