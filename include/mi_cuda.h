@@ -260,7 +260,10 @@ int mi_cuda_qwen2_forward(mi_cuda_model* model, mi_cuda_kv_cache* kv, const int3
                           int32_t n_tokens, int32_t n_past, int32_t last_logits_only,
                           float* h_logits_out);
 
-/* Greedy token of the last forward (device argmax of its last logits row). */
+/* Greedy token of the last forward (device argmax of its last logits row), or
+ * of the last device-resident step. Right after mi_cuda_qwen2_forward,
+ * _generate or _read_tokens it comes from the state those calls already read
+ * back (no device round trip); otherwise it waits for the stream. */
 int mi_cuda_qwen2_last_token(mi_cuda_kv_cache* kv, int32_t* h_token_out);
 
 /* mi_qwen2_sample_greedy (ref src/model_qwen2.cpp:690-700), on host logits. */
