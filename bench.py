@@ -4,10 +4,10 @@
 
 A step is one decode token: one replay of the captured decode-step graph
 (embedding, 24 layers, LM head, greedy argmax fed back on the device). The
-workload is BASELINE config 0: random-init 0.5B-shape Q8_0 GGUF (seed 1234),
-a 32-token uniform-random prompt (seed 7), greedy decode at positions
-32..158 (the reference CLI's 127 decode forwards of a 128-token run); a run of
-K steps cycles through that position range on the device.
+workload: random-init 0.5B-shape Q8_0 GGUF (seed 1234), a 32-token
+uniform-random prompt (seed 7), greedy decode at positions 32..158 (the
+reference CLI's 127 decode forwards of a 128-token run); a run of K steps
+cycles through that position range on the device.
 
 Printed JSON (rank 0, one line):
   value     device-timed decode tok/s (CUDA events on the executor stream,
@@ -18,10 +18,17 @@ Printed JSON (rank 0, one line):
             row instead and samples on the host, as the reference's loop does
   roofline  algorithmic bytes per decode step / step time vs the measured
             HBM copy bandwidth (MEASURED_PEAKS.json)
+  parity    the 128 greedy tokens of one full untimed generation (127 decode
+            steps from the prompt) against the reference's, whatever K is
   cpu_baseline  the reference's own CPU decode (compiled from its sources,
             oracle/_ref) on this host's cores, same model and prompt
-With --gpus N > 1 (torchrun) every rank runs an independent replica (the
-0.5B decode does not shard); value is the sum of tokens over the max time.
+  tp7b      the 7B-shape decode row-sharded over all N ranks (one request):
+            tok/s, ms per token, GB/s, greedy-token parity
+  sweeps    (N = 1) the isolated GEMV shapes (GB/s, cold), decode attention
+            at n_kv 128..32768 (µs), the 1024-token prefill (tok/s)
+With --gpus N > 1 (torchrun) every rank runs an independent 0.5B replica (the
+0.5B decode does not shard; value is the sum of tokens over the max time), and
+then all ranks run the 7B shape together, row-sharded (the tp7b object).
 """
 from __future__ import annotations
 
@@ -51,10 +58,12 @@ N_CTX, N_PROMPT, N_PREDICT = 2048, 32, 128
 PERIOD = N_PREDICT - 1  # decode forwards per generated sequence
 METRIC = "decode tok/s (0.5B-shape Q8_0, ctx 2048)"
 PUBLISHED_BEST = 64.035  # reference Q8_0 decode tok/s, 4 threads (reference README.md:106)
-# DRAM bytes (read + write) of one decode step, summed from `ncu --set full`
-# captures (dram__bytes_read.sum + dram__bytes_write.sum) of every kernel of one
-# step at n_kv = 33: 24 x 17.24 MB per layer + 150.3 MB for the LM head.
+# DRAM bytes (read + write) of one decode step: dram__bytes_read.sum +
+# dram__bytes_write.sum of every kernel of one step, from an ncu capture of the
+# decode graph at n_kv = 33 (profiles/decode_step_qwen2_05b.md gives the command
+# and the per-kernel figures).
 TRAFFIC_PER_STEP = 24 * 17.24e6 + 150.3e6
+TRAFFIC_SOURCE = "ncu dram__bytes_read+write, one step, n_kv 33"
 
 
 def step_bytes(hp, n_kv: int) -> int:
@@ -77,7 +86,10 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks and throttle reasons, sampled every 100 ms while the
+    context is open. The bench opens it before the warm-up and closes it after
+    the untimed passes that follow the timed region (parity, e2e), so a timed
+    region of a few milliseconds still lies inside a sampled busy span."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -102,6 +114,13 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+
+    def wait_first(self, timeout_s: float = 3.0):
+        """Blocks until the first sample arrived (nvidia-smi takes a moment to
+        start), so the span that follows is sampled from its beginning."""
+        t0 = time.time()
+        while self.proc and not self.lines and time.time() - t0 < timeout_s:
+            time.sleep(0.02)
 
     def __exit__(self, *a):
         if self.proc:
@@ -193,58 +212,19 @@ def step_trace_summary(kv) -> dict:
     return trace
 
 
-def run_reference_arm_prefill(args):
-    """Config 3 on the reference: its mi_qwen2_forward of the 1024-token prompt
-    (last logits) on all host cores; at most 3 timed forwards (bounded)."""
-    import mi_oracle
-    path = ensure_model(0, None)
-    threads = os.cpu_count() or 1
-    m = mi_oracle.ReferenceModel(path, n_ctx=N_CTX, n_threads=threads)
-    prompt = np.random.default_rng(SEED_PROMPT).integers(0, m.n_vocab, N_PREFILL).astype(np.int32)
-    steps = max(1, min(args.steps, 3))
-    m.forward(prompt, 0, last_logits_only=True)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        m.forward(prompt, 0, last_logits_only=True)
-    s = (time.perf_counter() - t0) / steps
-    m.close()
-    tps = N_PREFILL / s
-    print(json.dumps({
-        "metric": METRIC_PREFILL, "value": tps, "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
-        "steps": steps, "warmup": 1, "ms_per_step": s * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": tps / PUBLISHED_PREFILL, "dtype": "i8*i8->f32", "data": "synthetic",
-        "config": {"workload": "qwen2.5-0.5b-shape Q8_0 prefill, 1024-token prompt, ctx 2048, last logits",
-                   "parallelism": "cpu threads"},
-        "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": "reference",
-                         "sample": f"{steps} forwards of the 1024-token prompt, {threads} threads"},
-        "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }), flush=True)
 
 
-def run_reference_arm_7b(args):
-    """Config 4 on the reference: its decode loop over the 7B-shape model on all
-    host cores (one process; no GPUs), bounded to 16 decode forwards."""
-    import mi_oracle
-    path = os.path.join(MODEL_DIR, f"qwen2_7b_seed{SEED_MODEL}_fast.gguf")
-    mi_gguf.ensure_qwen2_gguf(path, mi_gguf.QWEN2_7B, SEED_MODEL, fast=True)
-    threads = os.cpu_count() or 1
-    m = mi_oracle.ReferenceModel(path, n_ctx=N_CTX_7B, n_threads=threads)
-    prompt = np.random.default_rng(SEED_PROMPT).integers(0, m.n_vocab, N_PROMPT_7B).astype(np.int32)
-    n_dec = max(1, min(args.steps, 16))
-    _, pre_ms, dec_ms = m.generate(prompt, n_dec + 1)
-    m.close()
-    tps = n_dec / (dec_ms / 1e3)
-    print(json.dumps({
-        "metric": METRIC_7B, "value": tps, "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
-        "steps": n_dec, "warmup": 0, "ms_per_step": dec_ms / n_dec, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "i8*i8->f32", "data": "synthetic",
-        "config": {"workload": "qwen2.5-7b-shape Q8_0 greedy decode, ctx 4096, prompt 64", "parallelism": "cpu threads"},
-        "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": "reference",
-                         "sample": f"{n_dec} decode forwards after the 64-token prefill ({pre_ms / 1e3:.1f} s), "
-                                   f"{threads} threads"},
-        "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }), flush=True)
+def decode_config() -> dict:
+    """The decode workload, the same dict on both arms."""
+    return {"workload": "qwen2.5-0.5b-shape Q8_0 greedy decode, ctx 2048, prompt 32, positions 32..158",
+            "n_ctx": N_CTX, "prompt": N_PROMPT, "n_predict": N_PREDICT,
+            "l2": "inputs larger than L2: 527 MB of weights streamed from HBM every step"}
 
+
+# ---------------------------------------------------------------------------
+# Reference arm: the reference's own CPU code (compiled from its sources into
+# oracle/_ref) on this host's cores.
+# ---------------------------------------------------------------------------
 
 def _time_host(fn, n_copies: int, budget_s: float, min_calls: int = 3):
     """Seconds per call of fn(copy_index), rotating copies, for about budget_s."""
@@ -256,14 +236,14 @@ def _time_host(fn, n_copies: int, budget_s: float, min_calls: int = 3):
     return (time.perf_counter() - t0) / n
 
 
-def run_reference_arm_gemv(args):
+def reference_gemv_rows(shapes, budget_s: float) -> list:
     """Config 1 on the reference: its quantize + mul_mat nodes (mi_compute_forward,
     one thread, as tools/bench_matvec times them), weights rotated through copies
     larger than the host's last-level cache."""
     import mi_oracle
-    import mi_gguf
     R = mi_oracle.Reference()
-    for n, k in [tuple(int(v) for v in sh.split("x")) for sh in args.shapes.split(",")]:
+    rows = []
+    for n, k in shapes:
         rng = np.random.default_rng(n + 3 * k)
         wbytes = n * k // 32 * 34
         n_copies = max(1, min(512, -(-256 * 2 ** 20 // wbytes)))  # >= 256 MB of weights in rotation
@@ -271,58 +251,134 @@ def run_reference_arm_gemv(args):
               for _ in range(min(n_copies, 2))]
         ws = [ws[i % len(ws)].copy() for i in range(n_copies)]
         x = rng.standard_normal((1, k), dtype=np.float32)
-        sec = _time_host(lambda i: R.mul_mat(ws[i], k, n, x), n_copies, 1.0)
+        sec = _time_host(lambda i: R.mul_mat(ws[i], k, n, x), n_copies, budget_s)
         algo = wbytes + k // 32 * 36 + 4 * n + 4 * k
-        print(json.dumps({"config": "gemv", "impl": "reference", "n": n, "k": k, "us_per_call": sec * 1e6,
-                          "bytes_per_call": algo, "achieved_gbs": algo / sec / 1e9, "cores": 1,
-                          "sample": f"mi_compute_forward quantize + mul_mat, 1 thread, {n_copies} weight copies"}),
-              flush=True)
+        rows.append({"shape": f"{n}x{k}", "us_per_call": sec * 1e6, "bytes_per_call": algo,
+                     "achieved_gbs": algo / sec / 1e9, "cores": 1,
+                     "sample": f"mi_compute_forward quantize + mul_mat, 1 thread, {n_copies} weight copies"})
+        del ws
+    return rows
 
 
-def run_reference_arm_attention(args):
+def reference_attention_rows(nkvs, budget_s: float) -> list:
     """Config 2 on the reference: its ATTN_QK, SOFTMAX, ATTN_KQV nodes on one
     thread (mi_compute_forward), 14 query / 2 KV heads, head_dim 64."""
     import mi_oracle
     R = mi_oracle.Reference()
     H, HKV, D = 14, 2, 64
-    for n_kv in [int(v) for v in args.nkv.split(",")]:
+    rows = []
+    for n_kv in nkvs:
         rng = np.random.default_rng(n_kv)
         q = rng.standard_normal((1, H, D), dtype=np.float32)
         k = rng.standard_normal((n_kv, HKV, D), dtype=np.float32)
         v = rng.standard_normal((n_kv, HKV, D), dtype=np.float32)
-        sec = _time_host(lambda i: R.attention(q, k, v, HKV, n_kv - 1, 1, 0.125), 1, 1.0)
+        sec = _time_host(lambda i: R.attention(q, k, v, HKV, n_kv - 1, 1, 0.125), 1, budget_s, min_calls=2)
         algo = 2 * n_kv * HKV * D * 4 + 2 * H * D * 4
-        print(json.dumps({"config": "attention", "impl": "reference", "n_kv": n_kv, "us_per_call": sec * 1e6,
-                          "bytes_per_call": algo, "achieved_gbs": algo / sec / 1e9, "cores": 1,
-                          "sample": "mi_compute_forward attn_qk + softmax + attn_kqv, 1 thread"}), flush=True)
+        rows.append({"n_kv": n_kv, "us_per_call": sec * 1e6, "bytes_per_call": algo,
+                     "achieved_gbs": algo / sec / 1e9, "cores": 1,
+                     "sample": "mi_compute_forward attn_qk + softmax + attn_kqv, 1 thread"})
+    return rows
+
+
+def reference_prefill(path: str, steps: int, threads: int) -> dict:
+    """Config 3 on the reference: its mi_qwen2_forward of the 1024-token prompt
+    (last logits) on `threads` host threads, after one untimed forward."""
+    import mi_oracle
+    m = mi_oracle.ReferenceModel(path, n_ctx=N_CTX, n_threads=threads)
+    prompt = np.random.default_rng(SEED_PROMPT).integers(0, m.n_vocab, N_PREFILL).astype(np.int32)
+    m.forward(prompt, 0, last_logits_only=True)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        m.forward(prompt, 0, last_logits_only=True)
+    s = (time.perf_counter() - t0) / steps
+    m.close()
+    return {"value": N_PREFILL / s, "unit": "tok/s", "ms_per_prompt": s * 1e3, "cores": threads,
+            "sample": f"{steps} forwards of the {N_PREFILL}-token prompt (last logits), {threads} threads"}
+
+
+def reference_7b(n_dec: int, threads: int) -> dict:
+    """Config 4 on the reference: its decode loop over the 7B-shape model on
+    `threads` host cores (one process, no GPUs), n_dec decode forwards."""
+    import mi_oracle
+    path = ensure_7b_model(0, None)
+    m = mi_oracle.ReferenceModel(path, n_ctx=N_CTX_7B, n_threads=threads)
+    prompt = np.random.default_rng(SEED_PROMPT).integers(0, m.n_vocab, N_PROMPT_7B).astype(np.int32)
+    toks, pre_ms, dec_ms = m.generate(prompt, n_dec + 1)
+    m.close()
+    return {"value": n_dec / (dec_ms / 1e3), "unit": "tok/s", "ms_per_token": dec_ms / n_dec, "cores": threads,
+            "tokens": [int(t) for t in toks],
+            "sample": f"{n_dec} decode forwards at positions 64..{64 + n_dec - 1} after the 64-token prefill "
+                      f"({pre_ms / 1e3:.1f} s), {threads} threads"}
 
 
 def run_reference_arm(args, rank: int):
+    """--impl reference: rank 0 times the reference's CPU path of the chosen
+    config on the host cores and prints the line; other ranks exit."""
     if rank != 0:
         return
-    if args.config == "prefill":
-        return run_reference_arm_prefill(args)
-    if args.config == "tp7b":
-        return run_reference_arm_7b(args)
-    if args.config == "gemv":
-        return run_reference_arm_gemv(args)
-    if args.config == "attention":
-        return run_reference_arm_attention(args)
-    path = ensure_model(0, None)
     threads = os.cpu_count() or 1
+    if args.config == "gemv":
+        for r in reference_gemv_rows(parse_shapes(args.shapes), 1.0):
+            print(json.dumps({"config": "gemv", "impl": "reference", **r}), flush=True)
+        return
+    if args.config == "attention":
+        for r in reference_attention_rows([int(v) for v in args.nkv.split(",")], 1.0):
+            print(json.dumps({"config": "attention", "impl": "reference", **r}), flush=True)
+        return
+    if args.config == "prefill":
+        r = reference_prefill(ensure_model(0, None), max(1, min(args.steps, 3)), threads)
+        tps = r["value"]
+        print(json.dumps({
+            "metric": METRIC_PREFILL, "value": tps, "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": max(1, min(args.steps, 3)), "warmup": 1, "ms_per_step": r["ms_per_prompt"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": tps / PUBLISHED_PREFILL,
+            "dtype": "i8*i8->f32", "data": "synthetic", "config": prefill_config(),
+            "parallelism": f"cpu threads x{threads}",
+            "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": "reference",
+                             "sample": r["sample"]},
+            "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    if args.config == "tp7b":
+        r = reference_7b(max(1, min(args.steps, 16)), threads)
+        tps = r["value"]
+        print(json.dumps({
+            "metric": METRIC_7B, "value": tps, "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": max(1, min(args.steps, 16)), "warmup": 0, "ms_per_step": r["ms_per_token"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "i8*i8->f32",
+            "data": "synthetic", "config": tp7b_config(), "parallelism": f"cpu threads x{threads}",
+            "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": "reference",
+                             "sample": r["sample"]},
+            "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    path = ensure_model(0, None)
     tps, _, sample = reference_decode(path, args.steps, args.warmup, threads)
-    print(json.dumps({
+    line = {
         "metric": METRIC, "value": tps, "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / tps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": tps / PUBLISHED_BEST, "dtype": "i8*i8->f32", "data": "synthetic",
-        "config": {"workload": "qwen2.5-0.5b-shape Q8_0 greedy decode, ctx 2048, prompt 32, positions 32..158",
-                   "parallelism": "cpu threads"},
+        "scaling": "weak", "vs_baseline": tps / PUBLISHED_BEST, "dtype": "i8*i8->f32",
+        "data": "synthetic: random-init N(0,0.02) Q8_0 GGUF (seed 1234), 32 uniform prompt ids (seed 7)",
+        "config": decode_config(), "parallelism": f"cpu threads x{threads}",
         "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": "reference", "sample": sample},
         "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }), flush=True)
+    }
+    if not args.no_sweeps:
+        line["sweeps"] = {
+            "gemv": reference_gemv_rows(parse_shapes(args.shapes), 0.5),
+            "attention": reference_attention_rows([int(v) for v in args.nkv.split(",")], 0.3),
+            "prefill": reference_prefill(path, 1, threads)}
+    if not args.no_tp7b:
+        line["tp7b"] = reference_7b(8, threads)
+    print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
 L2_BYTES = 126 * 2 ** 20
+
+
+def parse_shapes(spec: str):
+    return [tuple(int(v) for v in s.split("x")) for s in spec.split(",")]
 
 
 def _time_rotating(torch, fn, n_copies, launches, warmup):
@@ -339,18 +395,18 @@ def _time_rotating(torch, fn, n_copies, launches, warmup):
     return e0.elapsed_time(e1) / launches
 
 
-def run_gemv_sweep(args):
+def gemv_rows(shapes, launches: int, warmup: int, cold: bool) -> list:
     """Config 1: isolated Q8_0 GEMV (activation quantize fused) at the 0.5B shapes;
     distinct weight copies rotate so every launch reads its weights from HBM."""
     import torch
     import mi_cuda
-    mi_cuda.init(0)
     peak, peak_kind = load_peaks()
-    shapes = [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",")]
+    L = mi_cuda.lib()
+    rows = []
     for n, k in shapes:
-        nb = mi_cuda.lib().mi_cuda_q8_0_packed_bytes(k, n)
+        nb = L.mi_cuda_q8_0_packed_bytes(k, n)
         npad = (n + 7) // 8 * 8
-        n_copies = max(1, -(-4 * L2_BYTES // nb)) if args.cold else 1
+        n_copies = max(1, -(-4 * L2_BYTES // nb)) if cold else 1
         g = torch.Generator(device="cuda").manual_seed(n + k)
         copies = []
         for _ in range(n_copies):
@@ -362,44 +418,44 @@ def run_gemv_sweep(args):
             copies.append(buf)
         x = torch.randn(k, generator=g, device="cuda")
         out = torch.empty(n, dtype=torch.float32, device="cuda")
-        L = mi_cuda.lib()
         st = torch.cuda.current_stream().cuda_stream
 
         def fn(i):
             mi_cuda.check(L.mi_cuda_mul_mat_q8_0_f32(copies[i].data_ptr(), k, n, x.data_ptr(), 1, out.data_ptr(), st))
 
-        ms = _time_rotating(torch, fn, n_copies, args.steps, args.warmup)
+        ms = _time_rotating(torch, fn, n_copies, launches, warmup)
         algo = n * k * 34 // 32 + 4 * k + 4 * n
         gbs = algo / (ms / 1e3) / 1e9
-        print(json.dumps({"config": "gemv", "shape": f"{n}x{k}", "us_per_launch": ms * 1e3,
-                          "bytes_per_launch": algo, "achieved_gbs": gbs, "peak_gbs": peak,
-                          "frac": gbs / peak, "peak_kind": peak_kind, "weight_copies": n_copies,
-                          "launches": args.steps}), flush=True)
+        rows.append({"shape": f"{n}x{k}", "us_per_launch": ms * 1e3, "bytes_per_launch": algo,
+                     "achieved_gbs": gbs, "peak_gbs": peak, "frac": gbs / peak, "peak_kind": peak_kind,
+                     "weight_copies": n_copies, "launches": launches})
         del copies
+    return rows
 
 
-def run_attention(args):
+def attention_rows(nkvs, launches: int, warmup: int, cold: bool) -> list:
     """Config 2: fused decode attention, 14 query / 2 KV heads, head_dim 64, F32 KV,
-    one query token; K/V copies rotate so each launch reads its cache from HBM."""
+    one query token; K/V copies rotate so each launch reads its cache from HBM.
+    exact: the reference's summation order (bit-identical); split: positions
+    split over CTAs, sums regrouped (labelled fast mode, not bit-identical)."""
     import torch
     import mi_cuda
-    mi_cuda.init(0)
     peak, peak_kind = load_peaks()
     H, HKV, D = 14, 2, 64
-    for n_kv in [int(v) for v in args.nkv.split(",")]:
+    L = mi_cuda.lib()
+    rows = []
+    for n_kv in nkvs:
         kvb = 2 * n_kv * HKV * D * 4
-        n_copies = max(1, -(-4 * L2_BYTES // kvb)) if args.cold else 1
+        n_copies = max(1, -(-4 * L2_BYTES // kvb)) if cold else 1
         g = torch.Generator(device="cuda").manual_seed(n_kv)
         ks = [torch.randn((n_kv, HKV, D), generator=g, device="cuda") for _ in range(n_copies)]
         vs = [torch.randn((n_kv, HKV, D), generator=g, device="cuda") for _ in range(n_copies)]
         q = torch.randn((H, D), generator=g, device="cuda")
         out = torch.empty((H, D), dtype=torch.float32, device="cuda")
-        L = mi_cuda.lib()
         scratch = torch.empty(L.mi_cuda_attention_decode_scratch_bytes(H, n_kv), dtype=torch.uint8, device="cuda")
-        st = torch.cuda.current_stream().cuda_stream
-
         split_scratch = torch.empty(L.mi_cuda_attention_decode_split_scratch_bytes(H, HKV, n_kv, D),
                                     dtype=torch.uint8, device="cuda")
+        st = torch.cuda.current_stream().cuda_stream
 
         def fn(i):
             mi_cuda.check(L.mi_cuda_attention_decode(q.data_ptr(), ks[i].data_ptr(), vs[i].data_ptr(), D, H, HKV,
@@ -411,22 +467,40 @@ def run_attention(args):
                                                            out.data_ptr(), st))
 
         algo = kvb + 2 * H * D * 4
-        # exact: the reference's summation order (bit-identical); split: positions
-        # split over CTAs, sums regrouped (labelled fast mode, not bit-identical)
         for mode, f in (("exact", fn), ("split", fn_split)):
-            ms = _time_rotating(torch, f, n_copies, args.steps, args.warmup)
+            ms = _time_rotating(torch, f, n_copies, launches, warmup)
             gbs = algo / (ms / 1e3) / 1e9
-            print(json.dumps({"config": "attention", "mode": mode, "n_kv": n_kv, "us_per_launch": ms * 1e3,
-                              "bytes_per_launch": algo, "achieved_gbs": gbs, "peak_gbs": peak,
-                              "frac": gbs / peak, "peak_kind": peak_kind, "kv_copies": n_copies,
-                              "launches": args.steps}), flush=True)
+            rows.append({"mode": mode, "n_kv": n_kv, "us_per_launch": ms * 1e3, "bytes_per_launch": algo,
+                         "achieved_gbs": gbs, "peak_gbs": peak, "frac": gbs / peak, "peak_kind": peak_kind,
+                         "kv_copies": n_copies, "launches": launches})
         del ks, vs
+    return rows
+
+
+def run_gemv_sweep(args):
+    import mi_cuda
+    mi_cuda.init(0)
+    for r in gemv_rows(parse_shapes(args.shapes), args.steps, args.warmup, bool(args.cold)):
+        print(json.dumps({"config": "gemv", **r}), flush=True)
+
+
+def run_attention(args):
+    import mi_cuda
+    mi_cuda.init(0)
+    for r in attention_rows([int(v) for v in args.nkv.split(",")], args.steps, args.warmup, bool(args.cold)):
+        print(json.dumps({"config": "attention", **r}), flush=True)
 
 
 # Config 3: batched prefill of a 1024-token prompt (0.5B shape, ctx 2048).
 N_PREFILL = 1024
 METRIC_PREFILL = "prefill tok/s (0.5B-shape Q8_0, 1024-token prompt, ctx 2048)"
 PUBLISHED_PREFILL = 46.855  # reference Q8_0 prefill tok/s, 1024 tokens, 4 threads (docs/stage6.md:734)
+
+
+def prefill_config() -> dict:
+    return {"workload": "qwen2.5-0.5b-shape Q8_0 prefill, 1024-token prompt, ctx 2048, last logits",
+            "n_ctx": N_CTX, "prompt": N_PREFILL,
+            "l2": "weights 527 MB > L2; activations of a layer re-read per weight tile"}
 
 
 def prefill_macs(hp, n: int) -> int:
@@ -438,30 +512,22 @@ def prefill_macs(hp, n: int) -> int:
     return n * per_token + V * E
 
 
-def run_prefill(args):
-    """Config 3: mi_cuda_qwen2_forward of a 1024-token prompt (last-position
-    logits), timed on the device; each step re-runs the whole prompt."""
+def prefill_measure(path: str, model, kv, steps: int, warmup: int, with_cpu: bool) -> dict:
+    """mi_cuda_qwen2_forward of a 1024-token prompt (last-position logits),
+    timed on the device; each step re-runs the whole prompt."""
     import torch
-    import mi_cuda
-    mi_cuda.init(0)
-    path = ensure_model(0, None)
-    model = mi_cuda.Qwen2Model(path)
     hp = model.hparams
-    kv = mi_cuda.KVCache(model, N_CTX)
     prompt = np.random.default_rng(SEED_PROMPT).integers(0, hp.n_vocab, N_PREFILL).astype(np.int32)
-    stream = torch.cuda.ExternalStream(kv.stream_handle, device="cuda:0")
-    for _ in range(args.warmup):
+    stream = torch.cuda.ExternalStream(kv.stream_handle, device=f"cuda:{model.device}")
+    for _ in range(warmup):
         kv.forward(prompt, 0, last_logits_only=True, want_logits=False)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0 = time.perf_counter()
-    with ClockSampler(0) as clk:
-        e0.record(stream)
-        for _ in range(args.steps):
-            kv.forward(prompt, 0, last_logits_only=True, want_logits=False)
-        e1.record(stream)
-        torch.cuda.synchronize()
-    wall = time.perf_counter() - t0
+    e0.record(stream)
+    for _ in range(steps):
+        kv.forward(prompt, 0, last_logits_only=True, want_logits=False)
+    e1.record(stream)
+    torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
     logits = kv.forward(prompt, 0, last_logits_only=True)
     # e2e: logits D2H included (the call a user makes)
@@ -470,7 +536,7 @@ def run_prefill(args):
         kv.forward(prompt, 0, last_logits_only=True)
     e2e_s = (time.perf_counter() - t0) / 3
     cpu = parity = None
-    if not args.no_cpu_baseline:
+    if with_cpu:
         import mi_oracle
         threads = os.cpu_count() or 1
         m = mi_oracle.ReferenceModel(path, n_ctx=N_CTX, n_threads=threads)
@@ -485,29 +551,39 @@ def run_prefill(args):
         parity = {"last_logits_max_abs": float(np.max(np.abs(a - b))), "last_logits_cos": cos,
                   "bit_identical": bool(np.array_equal(logits[0].view(np.uint32), want[0].view(np.uint32))),
                   "vs": "reference AVX2 CPU path (oracle/_ref)"}
-    value = N_PREFILL * args.steps / (ms / 1e3)
+    value = N_PREFILL * steps / (ms / 1e3)
     peak_tops = 2 * load_peaks_bf16()
-    ops = 2 * prefill_macs(hp, N_PREFILL) * args.steps / (ms / 1e3) / 1e12
-    line = {
-        "metric": METRIC_PREFILL, "value": value, "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": value / PUBLISHED_PREFILL, "dtype": "i8*i8->f32",
-        "data": "synthetic: random-init N(0,0.02) Q8_0 GGUF (seed 1234), 1024 uniform prompt ids (seed 7)",
-        "config": {"workload": "qwen2.5-0.5b-shape Q8_0 prefill, 1024-token prompt, ctx 2048, last logits",
-                   "n_ctx": N_CTX, "prompt": N_PREFILL, "parallelism": "1 GPU",
-                   "l2": "weights 527 MB > L2; activations of a layer re-read per weight tile"},
+    ops = 2 * prefill_macs(hp, N_PREFILL) * steps / (ms / 1e3) / 1e12
+    return {
+        "value": value, "unit": "tok/s", "steps": steps, "warmup": warmup, "ms_per_step": ms / steps,
         "roofline": {"bound": "tensor", "achieved": ops, "peak": peak_tops, "unit": "TOPS",
                      "frac": ops / peak_tops, "traffic": None,
-                     "peak_kind": "2 x measured bf16 TF/s (int8 tensor rate); the exact lane-partial arithmetic "
-                                  "runs on the CUDA cores (dp4a), not the tensor cores",
+                     "peak_kind": "2 x measured bf16 TF/s (the int8 tensor rate)",
                      "kernel": "prefill (24 layers x (norm, QKV GEMM, RoPE/KV, attention, O GEMM, norm, "
                                "gate/up GEMM, down GEMM) + LM head)",
                      "ops_per_step": 2 * prefill_macs(hp, N_PREFILL)},
         "e2e": {"value": N_PREFILL / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": N_PREFILL * 4 + 36,
                 "d2h_bytes_per_step": hp.n_vocab * 4 + 4, "api": "mi_cuda_qwen2_forward (1024 tokens, last logits)"},
-        "gpu_launches": args.steps * (hp.n_layer * 8 + 1),
-        "clocks": clk.summary(), "cpu_baseline": cpu, "parity": parity, "wall_s": wall,
-    }
+        "gpu_launches": steps * (hp.n_layer * 8 + 1),
+        "cpu_baseline": cpu, "parity": parity}
+
+
+def run_prefill(args):
+    """Config 3 as its own bench line."""
+    import mi_cuda
+    mi_cuda.init(0)
+    path = ensure_model(0, None)
+    model = mi_cuda.Qwen2Model(path)
+    kv = mi_cuda.KVCache(model, N_CTX)
+    t0 = time.perf_counter()
+    with ClockSampler(0) as clk:
+        clk.wait_first()
+        r = prefill_measure(path, model, kv, args.steps, args.warmup, not args.no_cpu_baseline)
+    line = {"metric": METRIC_PREFILL, "n_gpus": 1, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": r["value"] / PUBLISHED_PREFILL, "dtype": "i8*i8->f32",
+            "data": "synthetic: random-init N(0,0.02) Q8_0 GGUF (seed 1234), 1024 uniform prompt ids (seed 7)",
+            "config": prefill_config(), "parallelism": "1 GPU", **r, "clocks": clk.summary(),
+            "wall_s": time.perf_counter() - t0}
     print(json.dumps(line), flush=True)
     kv.free()
     model.free()
@@ -524,29 +600,36 @@ def load_peaks_bf16() -> float:
 # one request, its weights split by rows across the GPUs).
 N_CTX_7B, N_PROMPT_7B = 4096, 64
 METRIC_7B = "decode tok/s (7B-shape Q8_0, ctx 4096, one request, row-sharded over the GPUs)"
+N_PARITY_7B = 8  # decode forwards compared with the reference (its CPU path runs ~14 tok/s)
 
 
-def run_tp7b(args):
-    import datetime
-    import torch
-    import mi_cuda
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import torch.distributed as td
-        td.init_process_group("nccl", timeout=datetime.timedelta(seconds=900))
-        dist = td
-    mi_cuda.init(local)
+def tp7b_config() -> dict:
+    return {"workload": "qwen2.5-7b-shape Q8_0 greedy decode, ctx 4096, prompt 64, positions 64..190",
+            "n_ctx": N_CTX_7B, "prompt": N_PROMPT_7B,
+            "l2": "inputs larger than L2: 7.5 GB of weights streamed every step"}
+
+
+def ensure_7b_model(rank: int, dist) -> str:
     path = os.path.join(MODEL_DIR, f"qwen2_7b_seed{SEED_MODEL}_fast.gguf")
-    t0 = time.time()
     if rank == 0:
         mi_gguf.ensure_qwen2_gguf(path, mi_gguf.QWEN2_7B, SEED_MODEL, fast=True)
-    gen_s = time.time() - t0
-    if dist:
+    if dist is not None:
         dist.barrier()
+    return path
+
+
+def tp7b_measure(dist, rank: int, world: int, local: int, steps: int, warmup: int, e2e_steps: int,
+                 with_cpu: bool, trace: bool = False, clk=None):
+    """Config 4 on `world` GPUs, one rank each (every rank calls this): the 7B
+    shape row-sharded over the ranks, decode timed on the device (max over
+    ranks). Greedy-token parity from a dedicated untimed pass of N_PARITY_7B
+    decode steps, against the reference's CPU path. Returns the result dict on
+    rank 0, None elsewhere."""
+    import torch
+    import mi_cuda
+    t0 = time.time()
+    path = ensure_7b_model(rank, dist)
+    gen_s = time.time() - t0
     t0 = time.time()
     model = mi_cuda.Qwen2Model(path, device=local, rank=rank, world=world)
     hp = model.hparams
@@ -560,7 +643,7 @@ def run_tp7b(args):
     seed_tokens = np.concatenate([prompt, [first]]).astype(np.int32)
     stream = torch.cuda.ExternalStream(kv.stream_handle, device=f"cuda:{local}")
     kv.set_position(seed_tokens, N_PROMPT_7B)
-    kv.decode_steps(args.warmup, N_PROMPT_7B, PERIOD)
+    kv.decode_steps(warmup, N_PROMPT_7B, PERIOD)
     torch.cuda.synchronize()
     kv.set_position(seed_tokens, N_PROMPT_7B)
     torch.cuda.synchronize()
@@ -568,22 +651,24 @@ def run_tp7b(args):
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        e0.record(stream)
-        kv.decode_steps(args.steps, N_PROMPT_7B, PERIOD)
-        e1.record(stream)
-        torch.cuda.synchronize()
+    e0.record(stream)
+    kv.decode_steps(steps, N_PROMPT_7B, PERIOD)
+    e1.record(stream)
+    torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
     if dist:
         t = torch.tensor([ms], device=f"cuda:{local}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    gen = kv.read_tokens(N_PROMPT_7B, N_PREDICT)
-    trace = step_trace_summary(kv) if args.trace else None
+    tr = step_trace_summary(kv) if trace else None
+    # parity pass, independent of `steps`: the first N_PARITY_7B decode steps again
+    kv.set_position(seed_tokens, N_PROMPT_7B)
+    kv.decode_steps(N_PARITY_7B)
+    gen = kv.read_tokens(N_PROMPT_7B, N_PARITY_7B + 1)
 
     # e2e through the public per-token API: token H2D, the device's greedy
     # token D2H (4 bytes; the logits stay sharded on the GPUs)
-    n_e2e = max(1, min(args.e2e_steps, PERIOD))
+    n_e2e = max(1, min(e2e_steps, PERIOD))
     tok = first
     if dist:
         dist.barrier()
@@ -597,117 +682,92 @@ def run_tp7b(args):
         t = torch.tensor([e2e_s], device=f"cuda:{local}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-
-    cpu = parity = None
-    if rank == 0 and not args.no_cpu_baseline:
-        import mi_oracle
-        threads = os.cpu_count() or 1
-        n_dec = 8
-        m = mi_oracle.ReferenceModel(path, n_ctx=N_CTX_7B, n_threads=threads)
-        ref_tok, pre_ms, dec_ms = m.generate(prompt, n_dec + 1)
-        m.close()
-        cpu = {"value": n_dec / (dec_ms / 1e3), "unit": "tok/s", "cores": threads, "kind": "reference",
-               "sample": f"{n_dec} decode forwards at positions 64..{64 + n_dec - 1} after the 64-token prefill "
-                         f"({pre_ms / 1e3:.1f} s), {threads} threads"}
-        parity = {"greedy_tokens_identical": bool(np.array_equal(ref_tok, gen[:n_dec + 1])),
-                  "n_tokens": n_dec + 1, "vs": "reference AVX2 CPU path (oracle/_ref)"}
-
-    value = args.steps / (ms / 1e3)
-    n_kvs = [N_PROMPT_7B + (i % PERIOD) + 1 for i in range(args.steps)]
-    total_bytes = sum(step_bytes(hp, n) for n in n_kvs)
-    peak, peak_kind = load_peaks()
-    achieved = total_bytes / (ms / 1e3) / 1e9
-    if rank == 0:
-        line = {
-            "metric": METRIC_7B, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "i8*i8->f32",
-            "data": f"synthetic: random-init N(0,0.02) Q8_0 GGUF (mi_gguf_gen, seed {SEED_MODEL}), "
-                    f"64 uniform prompt ids (seed {SEED_PROMPT})",
-            "config": {"workload": "qwen2.5-7b-shape Q8_0 greedy decode, ctx 4096, prompt 64, positions "
-                                   "64..190 cycled on the device", "n_ctx": N_CTX_7B, "prompt": N_PROMPT_7B,
-                       "parallelism": f"tp{world} (row-sharded GEMVs, peer-store exchange)",
-                       "l2": "inputs larger than L2: 7.5 GB of weights streamed every step"},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * world, "unit": "GB/s",
-                         "frac": achieved / (peak * world), "traffic": None, "peak_kind": f"{peak_kind} x {world}",
-                         "kernel": f"decode step graph ({kv.kernels_per_step} kernels per rank)",
-                         "bytes_per_step": total_bytes / args.steps},
-            "e2e": {"value": n_e2e / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 + 36,
-                    "d2h_bytes_per_step": 4, "api": "mi_cuda_qwen2_forward (no logits) + mi_cuda_qwen2_last_token"},
-            "gpu_launches": args.steps * kv.kernels_per_step * world,
-            "clocks": clk.summary(),
-            "cpu_baseline": cpu,
-            "parity": parity,
-            "setup_s": {"gguf_write": gen_s, "load_and_connect": load_s},
-        }
-        if trace is not None:
-            line["trace"] = trace
-        print(json.dumps(line), flush=True)
+    kernels = kv.kernels_per_step
     kv.free()
     model.free()
+
+    out = None
+    if rank == 0:
+        cpu = parity = None
+        if with_cpu:
+            r = reference_7b(N_PARITY_7B, os.cpu_count() or 1)
+            ref_tok = np.array(r.pop("tokens"), dtype=np.int32)
+            cpu = {**r, "kind": "reference"}
+            parity = {"greedy_tokens_identical": bool(np.array_equal(ref_tok, gen)),
+                      "n_tokens": int(gen.size), "vs": "reference AVX2 CPU path (oracle/_ref)"}
+        value = steps / (ms / 1e3)
+        n_kvs = [N_PROMPT_7B + (i % PERIOD) + 1 for i in range(steps)]
+        total_bytes = sum(step_bytes(hp, n) for n in n_kvs)
+        peak, peak_kind = load_peaks()
+        achieved = total_bytes / (ms / 1e3) / 1e9
+        out = {
+            "metric": METRIC_7B, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms / steps, "scaling": "strong",
+            "parallelism": f"tp{world} (row-sharded GEMVs, peer-store exchange)", "config": tp7b_config(),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * world, "unit": "GB/s",
+                         "frac": achieved / (peak * world), "per_rank_gbs": achieved / world,
+                         "peak_kind": f"{peak_kind} x {world}",
+                         "kernel": f"decode step graph ({kernels} kernels per rank)",
+                         "bytes_per_step": total_bytes / steps},
+            "e2e": {"value": n_e2e / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 + 36,
+                    "d2h_bytes_per_step": 4, "api": "mi_cuda_qwen2_forward (no logits) + mi_cuda_qwen2_last_token"},
+            "gpu_launches": steps * kernels * world,
+            "cpu_baseline": cpu, "parity": parity,
+            "setup_s": {"gguf_write": gen_s, "load_and_connect": load_s}}
+        if tr is not None:
+            out["trace"] = tr
+    return out
+
+
+def init_dist(world: int, local: int):
+    import datetime
+    import torch
+    torch.cuda.set_device(local)
+    if world <= 1:
+        return None
+    import torch.distributed as td
+    td.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    return td
+
+
+def run_tp7b(args):
+    """Config 4 as its own bench line (`--config tp7b`, torchrun for N > 1)."""
+    import mi_cuda
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = init_dist(world, local)
+    mi_cuda.init(local)
+    with ClockSampler(local) as clk:
+        clk.wait_first()
+        r = tp7b_measure(dist, rank, world, local, args.steps, args.warmup, args.e2e_steps,
+                         not args.no_cpu_baseline, args.trace)
+    if rank == 0:
+        print(json.dumps({**r, "higher_is_better": True, "vs_baseline": None, "dtype": "i8*i8->f32",
+                          "data": f"synthetic: random-init N(0,0.02) Q8_0 GGUF (mi_gguf_gen, seed {SEED_MODEL}), "
+                                  f"64 uniform prompt ids (seed {SEED_PROMPT})",
+                          "clocks": clk.summary()}), flush=True)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=PERIOD * 16)
-    ap.add_argument("--warmup", type=int, default=PERIOD)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--e2e-steps", type=int, default=PERIOD)
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", choices=["decode", "gemv", "attention", "prefill", "tp7b"], default="decode",
-                    help="decode: config 0 (default); gemv: config-1 GEMV sweep; attention: config 2; "
-                         "prefill: config 3, 1024-token prompt; tp7b: config 4, 7B shape tensor-parallel over the "
-                         "torchrun ranks")
-    ap.add_argument("--shapes", default="896x896,128x896,4864x896,896x4864,151936x896",
-                    help="gemv: NxK list")
-    ap.add_argument("--nkv", default="128,1024,4096,32768", help="attention: n_kv list")
-    ap.add_argument("--cold", type=int, default=1, help="gemv/attention: rotate copies past L2")
-    ap.add_argument("--trace", action="store_true", help="decode: add the last step's kernel timeline")
-    args = ap.parse_args()
-    if args.warmup < 3:
-        args.warmup = 3
-    if args.config == "gemv" and args.impl == "ours":
-        return run_gemv_sweep(args)
-    if args.config == "attention" and args.impl == "ours":
-        return run_attention(args)
-    if args.config == "tp7b" and args.impl == "ours":
-        return run_tp7b(args)
-    if args.config == "prefill" and args.impl == "ours":
-        return run_prefill(args)
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "reference":
-        run_reference_arm(args, rank)
-        return
-
+def decode_measure(args, dist, rank: int, world: int, local: int) -> dict:
+    """Config 0 on this rank's GPU (an independent replica when world > 1)."""
     import torch
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as td
-        torch.cuda.set_device(local)
-        td.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
-        dist = td
     import mi_cuda
-    mi_cuda.init(local)
-    torch.cuda.set_device(local)
     path = ensure_model(rank, dist)
-
     model = mi_cuda.Qwen2Model(path, device=local)
     hp = model.hparams
     kv = mi_cuda.KVCache(model, N_CTX)
     prompt = prompt_ids(hp.n_vocab)
-    logits = kv.forward(prompt, 0, last_logits_only=True)
+    kv.forward(prompt, 0, last_logits_only=True, want_logits=False)
     first = kv.last_token()
     seed_tokens = np.concatenate([prompt, [first]]).astype(np.int32)
     stream = torch.cuda.ExternalStream(kv.stream_handle, device=f"cuda:{local}")
 
+    clk = ClockSampler(local).__enter__()
+    clk.wait_first()
     # warm-up, then the timed decode steps
     kv.set_position(seed_tokens, N_PROMPT)
     kv.decode_steps(args.warmup, N_PROMPT, PERIOD)
@@ -718,19 +778,22 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        e0.record(stream)
-        kv.decode_steps(args.steps, N_PROMPT, PERIOD)
-        e1.record(stream)
-        torch.cuda.synchronize()
+    e0.record(stream)
+    kv.decode_steps(args.steps, N_PROMPT, PERIOD)
+    e1.record(stream)
+    torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
     if dist:
         dist.barrier()
         t = torch.tensor([ms], device=f"cuda:{local}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    gen = kv.read_tokens(N_PROMPT, N_PREDICT)
     trace = step_trace_summary(kv) if args.trace else None
+    # parity pass, untimed and independent of --steps: one full generation
+    # (127 decode steps from the prompt and its greedy token), all 128 tokens
+    kv.set_position(seed_tokens, N_PROMPT)
+    kv.decode_steps(PERIOD)
+    gen = kv.read_tokens(N_PROMPT, N_PREDICT)
 
     # roofline: algorithmic bytes of the timed steps over their device time
     n_kvs = [N_PROMPT + (i % PERIOD) + 1 for i in range(args.steps)]
@@ -765,48 +828,103 @@ def main():
 
     e2e_tps = e2e_run(False)
     e2e_logits_tps = e2e_run(True)
+    clk.__exit__(None, None, None)
+    kernels = kv.kernels_per_step
 
-    cpu = None
-    parity = None
+    sweeps = None
+    if world == 1 and not args.no_sweeps:
+        # configs 1-3 on the same GPU, outside the timed region
+        sweeps = {"gemv": gemv_rows(parse_shapes(args.shapes), 50, 10, True),
+                  "attention": attention_rows([int(v) for v in args.nkv.split(",")], 20, 5, True)}
+        p = prefill_measure(path, model, kv, 3, 1, not args.no_cpu_baseline)
+        sweeps["prefill"] = {k: p[k] for k in ("value", "unit", "ms_per_step", "roofline", "cpu_baseline", "parity")}
+    kv.free()
+    model.free()
+
+    cpu = parity = None
     if rank == 0 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         tps, ref_tokens, sample = reference_decode(path, PERIOD, 0, threads)
         cpu = {"value": tps, "unit": "tok/s", "cores": threads, "kind": "reference", "sample": sample}
         parity = {"greedy_tokens_identical": bool(np.array_equal(ref_tokens, gen)),
-                  "n_tokens": int(gen.size), "vs": "reference AVX2 CPU path (oracle/_ref)"}
+                  "n_tokens": int(gen.size), "vs": "reference AVX2 CPU path (oracle/_ref)",
+                  "run": "one untimed generation: prompt, then 127 device decode steps"}
 
     value = args.steps * world / (ms / 1e3)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": value / PUBLISHED_BEST, "dtype": "i8*i8->f32",
+        "data": "synthetic: random-init N(0,0.02) Q8_0 GGUF (seed 1234), 32 uniform prompt ids (seed 7)",
+        "config": decode_config(), "parallelism": f"replicas x{world}",
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": TRAFFIC_PER_STEP, "traffic_source": TRAFFIC_SOURCE,
+                     "peak_kind": peak_kind, "kernel": f"decode step graph ({kernels} kernels)",
+                     "bytes_per_step": total_bytes / args.steps},
+        "e2e": {"value": e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": 4 + 32, "d2h_bytes_per_step": 4 + 4,
+                "api": "mi_cuda_qwen2_forward (token in) + mi_cuda_qwen2_last_token (greedy token out)"},
+        "e2e_logits": {"value": e2e_logits_tps, "unit": "tok/s", "h2d_bytes_per_step": 4 + 32,
+                       "d2h_bytes_per_step": hp.n_vocab * 4 + 4,
+                       "api": "mi_cuda_qwen2_forward (logits row out) + host greedy, as the reference loop"},
+        "gpu_launches": args.steps * kernels + (args.steps - 1) // PERIOD,
+        "clocks": {**clk.summary(), "span": "warm-up, timed steps, parity pass and e2e runs"},
+        "cpu_baseline": cpu,
+        "parity": parity,
+    }
+    if trace is not None:
+        line["trace"] = trace
+    if sweeps is not None:
+        line["sweeps"] = sweeps
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=PERIOD * 16)
+    ap.add_argument("--warmup", type=int, default=PERIOD)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=PERIOD)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tp7b", action="store_true", help="decode: skip the 7B tensor-parallel object")
+    ap.add_argument("--no-sweeps", action="store_true", help="decode: skip the configs 1-3 sweeps")
+    ap.add_argument("--config", choices=["decode", "gemv", "attention", "prefill", "tp7b"], default="decode",
+                    help="decode: config 0 (default); gemv: config-1 GEMV sweep; attention: config 2; "
+                         "prefill: config 3, 1024-token prompt; tp7b: config 4, 7B shape tensor-parallel over the "
+                         "torchrun ranks")
+    ap.add_argument("--shapes", default="896x896,128x896,4864x896,896x4864,151936x896",
+                    help="gemv: NxK list")
+    ap.add_argument("--nkv", default="128,1024,4096,32768", help="attention: n_kv list")
+    ap.add_argument("--cold", type=int, default=1, help="gemv/attention: rotate copies past L2")
+    ap.add_argument("--trace", action="store_true", help="decode: add the last step's kernel timeline")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference_arm(args, rank)
+    if args.config == "gemv":
+        return run_gemv_sweep(args)
+    if args.config == "attention":
+        return run_attention(args)
+    if args.config == "tp7b":
+        return run_tp7b(args)
+    if args.config == "prefill":
+        return run_prefill(args)
+
+    import mi_cuda
+    dist = init_dist(world, local)
+    mi_cuda.init(local)
+    line = decode_measure(args, dist, rank, world, local)
+    if not args.no_tp7b:
+        # the path that shards: the 7B shape row-sharded over all ranks
+        tp = tp7b_measure(dist, rank, world, local, PERIOD, 10, 10, not args.no_cpu_baseline)
+        if rank == 0:
+            line["tp7b"] = tp
     if rank == 0:
-        line = {
-            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": value / PUBLISHED_BEST, "dtype": "i8*i8->f32",
-            "data": "synthetic: random-init N(0,0.02) Q8_0 GGUF (seed 1234), 32 uniform prompt ids (seed 7)",
-            "config": {"workload": "qwen2.5-0.5b-shape Q8_0 greedy decode, ctx 2048, prompt 32, "
-                                   "positions 32..158 cycled on the device",
-                       "n_ctx": N_CTX, "prompt": N_PROMPT, "parallelism": f"replicas x{world}",
-                       "l2": "inputs larger than L2: 527 MB of weights streamed from HBM every step"},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": TRAFFIC_PER_STEP,
-                         "traffic_source": "ncu dram__bytes_read+write, one step, n_kv 33",
-                         "peak_kind": peak_kind,
-                         "kernel": f"decode step graph ({kv.kernels_per_step} kernels)",
-                         "bytes_per_step": total_bytes / args.steps},
-            "e2e": {"value": e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": 4 + 32, "d2h_bytes_per_step": 4 + 4,
-                    "api": "mi_cuda_qwen2_forward (token in) + mi_cuda_qwen2_last_token (greedy token out)"},
-            "e2e_logits": {"value": e2e_logits_tps, "unit": "tok/s", "h2d_bytes_per_step": 4 + 32,
-                           "d2h_bytes_per_step": hp.n_vocab * 4 + 4,
-                           "api": "mi_cuda_qwen2_forward (logits row out) + host greedy, as the reference loop"},
-            "gpu_launches": args.steps * kv.kernels_per_step + (args.steps - 1) // PERIOD,
-            "clocks": clk.summary(),
-            "cpu_baseline": cpu,
-            "parity": parity,
-        }
-        if trace is not None:
-            line["trace"] = trace
         print(json.dumps(line), flush=True)
-    kv.free()
-    model.free()
     if dist:
         dist.barrier()
         dist.destroy_process_group()

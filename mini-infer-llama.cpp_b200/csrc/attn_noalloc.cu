@@ -49,7 +49,8 @@ extern "C" int mi_cuda_attention_decode_noalloc(const float* d_q, const float* d
                                                 int64_t n_head, int64_t n_head_kv, int64_t n_kv,
                                                 float scale, float* d_dst, mi_cuda_stream s) {
   if (!d_q || !d_cache_k || !d_cache_v || !d_dst || head_dim <= 0 || head_dim > 256 ||
-      head_dim % 4 != 0 || n_head_kv <= 0 || n_head % n_head_kv != 0 || n_kv <= 0)
+      head_dim % 4 != 0 || n_head <= 0 || n_head >= (1ll << 31) || n_head_kv <= 0 ||
+      n_head % n_head_kv != 0 || n_kv <= 0 || n_kv >= (1ll << 31))
     return fail(MI_CUDA_ERR_ARG, "mi_cuda_attention_decode_noalloc: bad arguments");
   if (n_head * n_kv > kMaxScratchFloats)
     return fail(MI_CUDA_ERR_ARG,

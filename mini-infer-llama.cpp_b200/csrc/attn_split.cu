@@ -162,8 +162,9 @@ __global__ void __launch_bounds__(kCombineNT) attn_split_combine_kernel(const fl
 }  // namespace
 
 bool attn_split_fits(int64_t head_dim, int64_t n_head, int64_t n_head_kv) {
-  return head_dim >= 4 && head_dim <= kSplitMaxD && head_dim % 4 == 0 && n_head_kv > 0 &&
-         n_head % n_head_kv == 0 && n_head / n_head_kv <= kSplitMaxRep;
+  return head_dim >= 4 && head_dim <= kSplitMaxD && head_dim % 4 == 0 && n_head > 0 &&
+         n_head < (1ll << 31) && n_head_kv > 0 && n_head % n_head_kv == 0 &&
+         n_head / n_head_kv <= kSplitMaxRep;
 }
 
 // Splits of whole tiles, about four CTAs per SM of a 148-SM B200 in total

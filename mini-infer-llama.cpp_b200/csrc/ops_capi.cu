@@ -405,8 +405,8 @@ int mi_cuda_attention_decode(const float* d_q, const float* d_cache_k, const flo
                              float scale, void* d_scratch, float* d_dst, mi_cuda_stream s) {
   MI_CTX(c);
   MI_REQUIRE(d_q && d_cache_k && d_cache_v && d_scratch && d_dst && head_dim > 0 &&
-                 head_dim <= 256 && head_dim % 4 == 0 && n_head_kv > 0 &&
-                 n_head % n_head_kv == 0 && n_kv > 0 && n_kv < (1ll << 31),
+                 head_dim <= 256 && head_dim % 4 == 0 && n_head > 0 && n_head < (1ll << 31) &&
+                 n_head_kv > 0 && n_head % n_head_kv == 0 && n_kv > 0 && n_kv < (1ll << 31),
              "mi_cuda_attention_decode: bad arguments");
   AttnParams p{};
   p.q_rot = d_q;

@@ -55,7 +55,8 @@ class Qwen2Shape:
         return self.n_embd // self.n_head
 
 
-# BASELINE configs 0/3 (Qwen2.5-0.5B architecture) and 4 (Qwen2.5-7B).
+# The decode, prefill and sweep workloads (Qwen2.5-0.5B architecture) and the
+# tensor-parallel workload (Qwen2.5-7B architecture).
 QWEN2_05B = Qwen2Shape(n_layer=24, n_embd=896, n_head=14, n_head_kv=2, n_ff=4864, n_vocab=151936)
 QWEN2_7B = Qwen2Shape(n_layer=28, n_embd=3584, n_head=28, n_head_kv=4, n_ff=18944, n_vocab=152064,
                       tied=False)

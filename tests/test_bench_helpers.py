@@ -49,9 +49,11 @@ def test_reference_arms_for_ops_print_json(capsys):
     import json
     import types
     b = _bench()
-    args = types.SimpleNamespace(shapes="128x896", nkv="64")
-    b.run_reference_arm_gemv(args)
-    b.run_reference_arm_attention(args)
+    args = types.SimpleNamespace(shapes="128x896", nkv="64", config="gemv")
+    b.run_reference_arm(args, 0)
+    args.config = "attention"
+    b.run_reference_arm(args, 0)
+    b.run_reference_arm(args, 1)  # other ranks print nothing
     lines = [json.loads(x) for x in capsys.readouterr().out.splitlines() if x.startswith("{")]
     assert [d["config"] for d in lines] == ["gemv", "attention"]
     for d in lines:
@@ -59,3 +61,12 @@ def test_reference_arms_for_ops_print_json(capsys):
         assert d["us_per_call"] > 0 and d["achieved_gbs"] > 0
     assert lines[0]["bytes_per_call"] == 128 * 896 // 32 * 34 + 896 // 32 * 36 + 4 * 128 + 4 * 896
     assert lines[1]["bytes_per_call"] == 2 * 64 * 2 * 64 * 4 + 2 * 14 * 64 * 4
+
+
+def test_decode_config_is_the_same_on_both_arms():
+    """The reference arm and the GPU arm describe the decode workload with one
+    dict, so a comparison of their lines sees the same configuration."""
+    b = _bench()
+    c = b.decode_config()
+    assert c == b.decode_config()
+    assert c["n_ctx"] == 2048 and c["prompt"] == 32 and c["n_predict"] == 128

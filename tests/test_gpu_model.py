@@ -167,8 +167,11 @@ def test_decode_past_context_reports_state_error(mc, model_path, qkv_attn_path):
 
 @pytest.mark.slow
 def test_qwen2_05b_decode_matches_reference(mc, model_path):
-    """Config 0 model: greedy tokens identical over the generated span, logits
-    bit-identical (and so within max-abs 1e-2 / cosine 0.9999)."""
+    """Config 0 model and run: logits bit-identical (and so within max-abs 1e-2
+    / cosine 0.9999) for the prompt and the first decode steps, and the greedy
+    tokens identical over the whole generated span -- the reference CLI's
+    128-token run (src/main.cpp:409-423), both through the host-driven
+    generation and through the device-resident decode steps the bench times."""
     path = model_path("QWEN2_05B", 1234)
     ref = mi_oracle.ReferenceModel(path, n_ctx=2048, n_threads=os.cpu_count() or 1)
     model = mc.Qwen2Model(path)
@@ -187,9 +190,39 @@ def test_qwen2_05b_decode_matches_reference(mc, model_path):
         tok = mc.sample_greedy(w[0])
     ref.close()
     ref = mi_oracle.ReferenceModel(path, n_ctx=2048, n_threads=os.cpu_count() or 1)
-    want_tok, _, _ = ref.generate(prompt, 64)
-    got_tok, _, _ = kv.generate(prompt, 64)
+    want_tok, _, _ = ref.generate(prompt, 128)
+    got_tok, _, _ = kv.generate(prompt, 128)
     assert np.array_equal(got_tok, want_tok)
+    kv.set_position(np.concatenate([prompt, want_tok[:1]]), 32)
+    kv.decode_steps(127)
+    assert np.array_equal(kv.read_tokens(32, 128), want_tok)
+    ref.close()
+    kv.free()
+    model.free()
+
+
+@pytest.mark.slow
+def test_qwen2_05b_decode_at_long_context(mc, model_path):
+    """Config 0 model near the end of its 2048-position context: a 1990-token
+    prompt, then decode steps at n_past 1990..1995, where the fused attention
+    walks its cached K/V in 13 shared-memory tiles. Logits bit-identical to the
+    reference's mi_qwen2_forward at every step."""
+    path = model_path("QWEN2_05B", 1234)
+    ref = mi_oracle.ReferenceModel(path, n_ctx=2048, n_threads=os.cpu_count() or 1)
+    model = mc.Qwen2Model(path)
+    kv = mc.KVCache(model, 2048)
+    n_prompt = 1990
+    prompt = np.random.default_rng(77).integers(0, 151936, n_prompt).astype(np.int32)
+    want = ref.forward(prompt, 0, last_logits_only=True)
+    got = kv.forward(prompt, 0, last_logits_only=True)
+    assert np.array_equal(bits(got), bits(want))
+    tok = mc.sample_greedy(want[0])
+    for step in range(6):
+        w = ref.forward([tok], n_prompt + step)
+        g = kv.forward([tok], n_prompt + step)
+        assert np.array_equal(bits(g), bits(w)), f"step {step}"
+        assert kv.last_token() == mc.sample_greedy(w[0])
+        tok = mc.sample_greedy(w[0])
     ref.close()
     kv.free()
     model.free()
