@@ -52,18 +52,35 @@ for _p in (PKG, ORACLE):
 
 import mi_gguf  # noqa: E402
 
-MODEL_DIR = os.environ.get("MI_B200_MODEL_DIR", "/tmp/mi_b200_models")
+def _model_dir() -> str:
+    """Where the seeded GGUF files are written: MI_B200_MODEL_DIR, else a RAM
+    file system with room for the 7.5 GB 7B-shape file (writing it to a slow
+    disk took minutes), else /tmp."""
+    if os.environ.get("MI_B200_MODEL_DIR"):
+        return os.environ["MI_B200_MODEL_DIR"]
+    try:
+        st = os.statvfs("/dev/shm")
+        if st.f_bavail * st.f_frsize > 24 * 2 ** 30:
+            return "/dev/shm/mi_b200_models"
+    except OSError:
+        pass
+    return "/tmp/mi_b200_models"
+
+
+MODEL_DIR = _model_dir()
 SEED_MODEL, SEED_PROMPT = 1234, 7
 N_CTX, N_PROMPT, N_PREDICT = 2048, 32, 128
 PERIOD = N_PREDICT - 1  # decode forwards per generated sequence
 METRIC = "decode tok/s (0.5B-shape Q8_0, ctx 2048)"
 PUBLISHED_BEST = 64.035  # reference Q8_0 decode tok/s, 4 threads (reference README.md:106)
 # DRAM bytes (read + write) of one decode step: dram__bytes_read.sum +
-# dram__bytes_write.sum of every kernel of one step, from an ncu capture of the
-# decode graph at n_kv = 33 (profiles/decode_step_qwen2_05b.md gives the command
-# and the per-kernel figures).
-TRAFFIC_PER_STEP = 24 * 17.24e6 + 150.3e6
-TRAFFIC_SOURCE = "ncu dram__bytes_read+write, one step, n_kv 33"
+# dram__bytes_write.sum summed over the 97 launches of one step at n_kv = 33,
+# from an ncu capture of this build's decode graph (ncu flushes the caches
+# before every replayed launch, so operands a real step finds in L2 count as
+# DRAM reads here); profiles/decode_step_qwen2_05b.md gives the command and the
+# per-kernel figures.
+TRAFFIC_PER_STEP = 564_573_440
+TRAFFIC_SOURCE = "ncu dram__bytes_read+write, 97 launches of one step at n_kv 33 (caches flushed per launch)"
 
 
 def step_bytes(hp, n_kv: int) -> int:
