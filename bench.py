@@ -199,10 +199,36 @@ def reference_decode(path: str, steps: int, warmup: int, threads: int):
     return total_steps / (total_ms / 1e3), first, f"{total_steps} decode forwards at positions 32..158, {threads} threads"
 
 
+def persist_trace_summary(kv) -> dict:
+    """Phase timeline of the last timed persistent step (one kernel): per
+    layer, from attention CTA 0 and the first projection CTA, means over the
+    layers in microseconds."""
+    t = kv.step_trace().astype(np.int64)
+    L = kv.model.hparams.n_layer
+    a, g, h = t[0:2 * L:2], t[1:2 * L:2], t[2 * L]
+    us = lambda v: float(np.mean(v)) / 1e3
+    return {
+        "schedule": "persistent (one kernel per step)",
+        "step_us": float(h[2] - a[0, 0]) / 1e3,
+        "per_layer_us": us(np.diff(a[:, 1])) if L > 1 else None,
+        "attention_cta_us": {"x_wait": us(a[1:, 1] - g[:-1, 6]) if L > 1 else None,
+                             "norm_quant": us(a[:, 2] - a[:, 1]), "qkv_rows": us(a[:, 3] - a[:, 2]),
+                             "kv_handover": us(a[:, 4] - a[:, 3]), "scores_exp": us(a[:, 5] - a[:, 4]),
+                             "softmax_sum": us(a[:, 6] - a[:, 5]), "values_quant_signal": us(a[:, 7] - a[:, 6])},
+        "projection_cta_us": {"o_wait_after_heads": us(g[:, 0] - a[:, 7]), "o": us(g[:, 1] - g[:, 0]),
+                              "gate_up_wait": us(g[:, 2] - g[:, 1]), "gate_up_norm_quant": us(g[:, 3] - g[:, 2]),
+                              "gate_up_rows": us(g[:, 4] - g[:, 3]), "down_wait": us(g[:, 5] - g[:, 4]),
+                              "down": us(g[:, 6] - g[:, 5])},
+        "lm_head_us": {"wait": float(h[0] - g[-1, 6]) / 1e3, "norm_quant": float(h[1] - h[0]) / 1e3,
+                       "rows_argmax": float(h[2] - h[1]) / 1e3}}
+
+
 def step_trace_summary(kv) -> dict:
     """Per-kernel timeline of the last timed step (first CTA of each kernel):
     dependency wait -> prologue done, prologue -> epilogue, hand-off from the
     predecessor, and the attention phases."""
+    if kv.kernels_per_step == 1:
+        return persist_trace_summary(kv)
     t = kv.step_trace().astype(np.int64)
     per = (t.shape[0] - 1) // kv.model.hparams.n_layer
     # 4 kernels a layer when QKV and attention run as one cluster kernel

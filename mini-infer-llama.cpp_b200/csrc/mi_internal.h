@@ -210,6 +210,74 @@ cudaError_t launch_qkv_attn(const QkvAttnParams& p, const QkvAttnPlan& plan, cud
 cudaError_t prepare_qkv_attn_kernel(int optin);
 
 // ---------------------------------------------------------------------------
+// Persistent decode step (decode_persist.cu): one launch per decode step on
+// one GPU. CTAs stay resident for the whole step; phases hand over through
+// device counters instead of kernel boundaries, and every CTA streams the
+// weights of its coming work items into a shared-memory ring a layer ahead.
+// ---------------------------------------------------------------------------
+struct PersistLayer {
+  const uint8_t* qkv;     // packed Q | K | V rows, n_pad qkv_npad
+  const float* bqkv;
+  const float* attn_norm;
+  const uint8_t* o;       // packed, E rows
+  const uint8_t* gateup;  // packed gate/up rows interleaved by groups of 4
+  const float* ffn_norm;
+  const uint8_t* down;    // packed, E rows of K = n_ff
+};
+
+struct PersistParams {
+  int32_t n_layer, E, H, HKV, D, FF, V, n_ctx;
+  int64_t qkv_npad, gu_npad, head_npad;
+  float eps, scale;
+  const PersistLayer* layers;  // device array of n_layer
+  const uint8_t* embed;        // packed Q8_0 embedding [E x V]
+  int64_t embed_npad;
+  const uint8_t* head;         // packed LM head [E x V]
+  const float* out_norm;
+  float* cache;                // [layer][k|v][n_ctx][HKV][D]
+  const float2* rope;          // [pos][D/2]
+  float* x;                    // residual stream (layer input / down output)
+  float* x2;                   // residual stream after attention
+  uint8_t* attn_q;             // Q8_0_ACT: the O projection's input
+  uint8_t* act_q;              // Q8_0_ACT: the down projection's input
+  float* logits;
+  float* scores;               // [H][n_ctx] when the scores do not fit on chip
+  float* part_val;             // per-CTA LM-head winners
+  int32_t* part_idx;
+  int32_t* tokens;
+  int32_t tokens_len;
+  int32_t with_head;           // 0: the step only writes the KV cache and advances pos
+  int32_t* pos;
+  int32_t* next_token;
+  const int32_t* feedback;
+  int32_t* err;
+  uint32_t* ticket;            // CTAs finished with the step (the last one closes it)
+  unsigned long long* epoch;   // steps completed since the counters were zeroed
+  unsigned long long* ctr;     // [n_layer][4] hand-over counters
+  // schedule: CTAs [0, n_attn) run the attention of one head (clusters of
+  // n_rep + 1: n_rep query heads and one k/v CTA), the other n_gemv CTAs the
+  // O, gate/up and down projections; all of them share the LM head
+  int32_t n_attn, n_gemv;
+  int32_t kv_tile, scores_in_smem;
+  int32_t ring_gemv, ring_attn;  // weight-ring bytes of the two roles
+  ExpTab et;
+  uint64_t* trace;             // optional: 8 stamps per slot, 2 slots per layer + 1
+};
+
+struct PersistPlan {
+  bool ok;
+  int32_t grid, cluster, n_attn, n_gemv, kv_tile, scores_in_smem, ring_gemv, ring_attn;
+  size_t smem;
+};
+// The persistent kernel's plan for a model shape on this device, or ok ==
+// false when the shape does not fit it (then the executor keeps the
+// kernel-per-phase graph).
+PersistPlan plan_persist(int64_t E, int32_t D, int32_t H, int32_t HKV, int64_t FF, int64_t V, int32_t n_layer,
+                         int32_t n_ctx, int num_sms);
+cudaError_t launch_persist(const PersistParams& p, const PersistPlan& plan, cudaStream_t s);
+cudaError_t prepare_persist_kernel(int optin);
+
+// ---------------------------------------------------------------------------
 // Batched prefill (prefill.cu)
 // ---------------------------------------------------------------------------
 // Exact Q8_0 GEMM over M tokens: out[t * out_stride + r] = dot(W row r, act t)

@@ -143,6 +143,14 @@ struct mi_cuda_kv_cache {
   // cluster kernel per layer (qkv_attn.cu).
   QkvAttnPlan plan_fused{};
   bool fused = false;
+  // One GPU, shapes that fit: the whole step as one persistent kernel
+  // (decode_persist.cu); its hand-over counters (never reset between steps:
+  // targets grow with the step epoch), the epoch, the closing ticket, and the
+  // layers' weight pointers.
+  PersistPlan plan_persist{};
+  bool persist = false;
+  unsigned long long* pctr = nullptr;  // [n_layer][4] | epoch | ticket
+  PersistLayer* d_layers = nullptr;
   cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
   // Batched-prefill workspace, allocated on first use and grown to the largest
   // batch: residual streams X / X2 [T][E], q|k|v [T][E + 2kvd], rotated q
@@ -491,6 +499,52 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     for (int r = 0; r < m->world; r++) g.out_ll[r] = kv->peer[r] + off;
   };
   auto local = [&](size_t off) -> const uint64_t* { return kv->xbuf + off; };
+  if (kv->persist) {
+    PersistParams q{};
+    q.n_layer = hp.n_layer;
+    q.E = (int32_t)E;
+    q.H = hp.n_head;
+    q.HKV = hp.n_head_kv;
+    q.D = (int32_t)D;
+    q.FF = (int32_t)FF;
+    q.V = hp.n_vocab;
+    q.n_ctx = kv->n_ctx;
+    q.qkv_npad = m->layers[0].qkv.npad;
+    q.gu_npad = m->layers[0].gateup.npad;
+    q.head_npad = m->lm_head.npad;
+    q.eps = hp.rms_eps;
+    q.scale = 1.0f / std::sqrt((float)hp.head_dim);
+    q.layers = kv->d_layers;
+    q.embed = m->embed.w;
+    q.embed_npad = m->embed.npad;
+    q.head = m->lm_head.w;
+    q.out_norm = m->output_norm;
+    q.cache = kv->cache;
+    q.rope = kv->rope;
+    q.x = kv->x;
+    q.x2 = kv->x2;
+    q.attn_q = kv->attn_q;
+    q.act_q = kv->act_q;
+    q.logits = kv->logits;
+    q.scores = kv->scores;
+    q.part_val = kv->part_val;
+    q.part_idx = kv->part_idx;
+    q.tokens = kv->tokens;
+    q.tokens_len = kv->n_ctx + 1;
+    q.with_head = with_head ? 1 : 0;
+    q.pos = &kv->state->pos;
+    q.next_token = &kv->state->next_token;
+    q.feedback = &kv->state->feedback;
+    q.err = err;
+    q.ctr = kv->pctr;
+    q.epoch = kv->pctr + (size_t)hp.n_layer * 4;
+    q.ticket = (uint32_t*)(kv->pctr + (size_t)hp.n_layer * 4 + 1);
+    q.et = et;
+    q.trace = kv->trace;
+    CK(launch_persist(q, kv->plan_persist, kv->stream));
+    if (n_kernels) *n_kernels = 1;
+    return MI_CUDA_OK;
+  }
   int count = 0;
   bool pdl = false;  // the first kernel of a step has no in-graph predecessor
   for (int l = 0; l < hp.n_layer; l++) {
@@ -1050,6 +1104,17 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
     }
   }
 
+  // The persistent one-kernel step where the shape fits it (one GPU), with
+  // MI_CUDA_PERSIST=1; otherwise the kernel-per-phase graph.
+  if (m->world == 1) {
+    const char* pe = std::getenv("MI_CUDA_PERSIST");
+    if (pe && std::atoi(pe) != 0) {
+      kv->plan_persist = plan_persist(E, (int32_t)D, hp.n_head, hp.n_head_kv, FF, hp.n_vocab, hp.n_layer, n_ctx,
+                                      sms);
+      kv->persist = kv->plan_persist.ok;
+    }
+  }
+
   const size_t cache_bytes = (size_t)hp.n_layer * 2 * n_ctx * kvd * 4;
   const size_t rope_bytes = (size_t)n_ctx * (D / 2) * 8;
   size_t off = 0;
@@ -1065,7 +1130,9 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
                o_pi = slot(1024 * 4), o_tok = slot((size_t)(n_ctx + 1) * 4),
                o_state = slot(sizeof(StepState)), o_attnq = slot(E / 32 * 36),
                o_actq = slot(FF / 32 * 36),
-               o_trace = slot((size_t)(6 * hp.n_layer + 1) * kTraceStamps * 8), o_epoch = slot(4);
+               o_trace = slot((size_t)(6 * hp.n_layer + 1) * kTraceStamps * 8), o_epoch = slot(4),
+               o_pctr = slot(((size_t)hp.n_layer * 4 + 2) * 8),
+               o_play = slot((size_t)hp.n_layer * sizeof(PersistLayer));
   CK(cudaMalloc(&kv->buf, off));
   CK(cudaMemset(kv->buf, 0, off));
   kv->cache = (float*)(kv->buf + o_cache);
@@ -1086,8 +1153,18 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
   kv->trace = (uint64_t*)(kv->buf + o_trace);
   // one slot per kernel of a step; the fused QKV + attention kernel adds two
   // detail slots per layer after the step's slots
-  kv->trace_slots = 6 * hp.n_layer + 1;
+  kv->trace_slots = kv->persist ? 2 * hp.n_layer + 1 : 6 * hp.n_layer + 1;
   kv->epoch = (uint32_t*)(kv->buf + o_epoch);
+  kv->pctr = (unsigned long long*)(kv->buf + o_pctr);
+  kv->d_layers = (PersistLayer*)(kv->buf + o_play);
+  {
+    std::vector<PersistLayer> pl((size_t)hp.n_layer);
+    for (int l = 0; l < hp.n_layer; l++) {
+      const Layer& L = m->layers[(size_t)l];
+      pl[(size_t)l] = PersistLayer{L.qkv.w, L.bqkv, L.attn_norm, L.o.w, L.gateup.w, L.ffn_norm, L.down.w};
+    }
+    CK(cudaMemcpy(kv->d_layers, pl.data(), pl.size() * sizeof(PersistLayer), cudaMemcpyHostToDevice));
+  }
   const uint32_t one = 1u;  // exchange words start zeroed: tag 0 is never current
   CK(cudaMemcpy(kv->epoch, &one, 4, cudaMemcpyHostToDevice));
   if (kv->plan_head.grid > 1024) return fail(MI_CUDA_ERR_ARG, "LM head grid too large");
@@ -1118,6 +1195,15 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
   }
   int rc = capture(kv.get(), true, &kv->g_head, &kv->kernels_per_step);
   if (!rc) rc = capture(kv.get(), false, &kv->g_nohead, nullptr);
+  if (rc && kv->persist) {
+    // Retry with the kernel-per-phase step if the persistent launch was refused.
+    kv->persist = false;
+    if (kv->g_head) cudaGraphExecDestroy(kv->g_head);
+    kv->g_head = nullptr;
+    cudaGetLastError();
+    rc = capture(kv.get(), true, &kv->g_head, &kv->kernels_per_step);
+    if (!rc) rc = capture(kv.get(), false, &kv->g_nohead, nullptr);
+  }
   if (rc && kv->fused) {
     // Retry with the two-kernel QKV + attention path if the cluster launch was refused.
     kv->fused = false;
@@ -1215,6 +1301,9 @@ int mi_cuda_qwen2_set_position(mi_cuda_kv_cache* kv, const int32_t* h_tokens, in
   kv->h_state->pos = pos;
   kv->h_state->feedback = 1;
   CK(cudaMemcpyAsync(kv->state, kv->h_state, sizeof(StepState), cudaMemcpyHostToDevice, kv->stream));
+  // a fresh start for the persistent step's hand-over counters (a step that
+  // gave up part-way leaves them behind their targets)
+  CK(cudaMemsetAsync(kv->pctr, 0, ((size_t)kv->model->hp.n_layer * 4 + 2) * 8, kv->stream));
   return MI_CUDA_OK;
 }
 

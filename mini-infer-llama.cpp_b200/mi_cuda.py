@@ -432,10 +432,16 @@ class KVCache:
         return int(lib().mi_cuda_qwen2_kernels_per_step(self.h))
 
     def step_trace(self) -> np.ndarray:
-        """[kernels, 8] globaltimer stamps (ns) of the last step (first CTA):
-        entry, predecessor done, prologue done, epilogue start, then the
-        kernel's own phase marks (attention: scores, exp, sum, KV done)."""
-        n = self.kernels_per_step
+        """[slots, 8] globaltimer stamps (ns) of the last step. Kernel-per-phase
+        step: one slot per kernel (first CTA): entry, predecessor done,
+        prologue done, epilogue start, then the kernel's own phase marks
+        (attention: scores, exp, sum, KV done). Persistent step (one kernel):
+        two slots per layer -- attention CTA 0 (layer start, x ready, prologue
+        done, rows done, k/v received, exp done, sum done, head signalled) and
+        the first projection CTA (O wait done, O signalled, gate/up wait done,
+        its prologue done, gate/up signalled, down wait done, down signalled)
+        -- then the LM head (wait done, prologue done, rows done, step closed)."""
+        n = 6 * self.model.hparams.n_layer + 1
         out = np.zeros((n, 8), dtype=np.uint64)
         got = C.c_int32()
         check(lib().mi_cuda_qwen2_step_trace(self.h, out.ctypes.data, n, C.byref(got)))

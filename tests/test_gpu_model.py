@@ -29,19 +29,39 @@ def logits_close(a, b):
 
 
 def kernels_per_layer(kv, model):
+    if kv.kernels_per_step == 1:
+        return 0  # the persistent step: one kernel for every layer and the head
     return (kv.kernels_per_step - 1) // model.hparams.n_layer
 
 
-@pytest.fixture(params=["fused", "fused_small_tile", "pair"])
+class StepPath(int):
+    """Expected kernels per layer of a decode-step schedule (0: persistent)."""
+
+
+@pytest.fixture(params=["persist", "persist_small_tile", "fused", "fused_small_tile", "pair"])
 def qkv_attn_path(request, monkeypatch):
-    """Runs a test with the fused QKV + attention cluster kernel (4 kernels a
-    layer; fused_small_tile: a 44 KB shared-memory budget, which leaves the
-    SMALL shape a 32-position K/V tile, so attention walks several tiles) and
-    with the QKV GEMV + attention kernel pair (5 a layer)."""
+    """Runs a test with each decode-step schedule: the persistent one-kernel
+    step (shapes with head_dim a multiple of 32; TINY falls back to the fused
+    schedule; persist_small_tile: 32-position K / V tiles, so attention walks
+    several), the fused QKV + attention cluster kernel (4 kernels a layer;
+    fused_small_tile: a 44 KB shared-memory budget, which leaves the SMALL
+    shape a 32-position K/V tile, so attention walks several tiles) and the
+    QKV GEMV + attention kernel pair (5 a layer)."""
+    monkeypatch.setenv("MI_CUDA_PERSIST", "1" if request.param.startswith("persist") else "0")
+    if request.param == "persist_small_tile":
+        monkeypatch.setenv("MI_CUDA_PERSIST_KV_TILE", "32")
     monkeypatch.setenv("MI_CUDA_FUSED_ATTN", "0" if request.param == "pair" else "1")
     if request.param == "fused_small_tile":
         monkeypatch.setenv("MI_CUDA_FUSED_SMEM_KB", "44")
-    return 5 if request.param == "pair" else 4
+    return {"persist": StepPath(0), "persist_small_tile": StepPath(0), "pair": StepPath(5)}.get(request.param,
+                                                                                             StepPath(4))
+
+
+def expected_per_layer(path, model):
+    """The persistent step needs head_dim % 32 == 0 (TINY runs fused)."""
+    if path == 0 and model.hparams.head_dim % 32 != 0:
+        return 4
+    return path
 
 
 @pytest.mark.parametrize("shape,seed,n_ctx", [("TINY", 1, 64), ("SMALL", 4, 256)])
@@ -50,7 +70,7 @@ def test_forward_prefill_and_decode_bitexact(mc, model_path, qkv_attn_path, shap
     ref = mi_oracle.ReferenceModel(path, n_ctx=n_ctx)
     model = mc.Qwen2Model(path)
     kv = mc.KVCache(model, n_ctx)
-    assert kernels_per_layer(kv, model) == qkv_attn_path
+    assert kernels_per_layer(kv, model) == expected_per_layer(qkv_attn_path, model)
     rng = np.random.default_rng(seed)
     prompt = rng.integers(0, ref.n_vocab, 9).astype(np.int32)
     want = ref.forward(prompt, 0)
@@ -78,7 +98,7 @@ def test_generate_token_identical(mc, model_path, qkv_attn_path, shape, seed, n_
     ref = mi_oracle.ReferenceModel(path, n_ctx=n_ctx, n_threads=os.cpu_count() or 1)
     model = mc.Qwen2Model(path)
     kv = mc.KVCache(model, n_ctx)
-    assert kernels_per_layer(kv, model) == qkv_attn_path
+    assert kernels_per_layer(kv, model) == expected_per_layer(qkv_attn_path, model)
     prompt = np.random.default_rng(seed).integers(0, ref.n_vocab, n_prompt).astype(np.int32)
     want, _, _ = ref.generate(prompt, n_predict)
     got, pre_ms, dec_ms = kv.generate(prompt, n_predict)
@@ -101,17 +121,30 @@ def test_step_trace(mc, model_path, qkv_attn_path):
     kv.decode_steps(3)
     t = kv.step_trace().astype(np.int64)
     per = qkv_attn_path
-    assert t.shape == (kv.kernels_per_step, 8) == (per * 4 + 1, 8)
-    assert np.all(t[:, :4] > 0)
-    assert np.all(np.diff(t[:, :4], axis=1) >= 0)    # entry <= dep done <= prologue <= epilogue
-    if per == 5:
-        attn = t[1::5][:4]                           # attention phases: scores, exp, sum, KV
-        assert np.all(np.diff(attn[:, [2, 4, 5, 6, 7]], axis=1) >= 0)
+    L = model.hparams.n_layer
+    if per == 0:
+        # persistent step: per layer the attention CTA's and the first
+        # projection CTA's phase stamps, then the LM head's
+        assert kv.kernels_per_step == 1
+        assert t.shape == (2 * L + 1, 8)
+        attn, proj = t[0:2 * L:2], t[1:2 * L:2]
+        assert np.all(attn > 0) and np.all(proj[:, :7] > 0) and np.all(t[-1, :3] > 0)
+        assert np.all(np.diff(attn, axis=1) >= 0) and np.all(np.diff(proj[:, :7], axis=1) >= 0)
+        assert np.all(proj[:, 0] >= attn[:, 7] - 2000)   # O starts after the heads are done
+        assert np.all(attn[1:, 1] >= proj[:-1, 6] - 2000)  # a layer starts after the previous down
+        assert t[-1, 2] - attn[0, 0] < 10_000_000
     else:
-        fused = t[0::4][:4]                          # prologue, k/v handed over, scores, exp, sum, KV
-        assert np.all(np.diff(fused[:, [2, 4, 5, 6, 7, 3]], axis=1) >= 0)
-    assert np.all(t[1:, 1] >= t[:-1, 1])             # kernels' dependent sections run in order
-    assert t[-1, 3] - t[0, 0] < 10_000_000           # the step took less than 10 ms
+        assert t.shape == (kv.kernels_per_step, 8) == (per * 4 + 1, 8)
+        assert np.all(t[:, :4] > 0)
+        assert np.all(np.diff(t[:, :4], axis=1) >= 0)    # entry <= dep done <= prologue <= epilogue
+        if per == 5:
+            attn = t[1::5][:4]                           # attention phases: scores, exp, sum, KV
+            assert np.all(np.diff(attn[:, [2, 4, 5, 6, 7]], axis=1) >= 0)
+        else:
+            fused = t[0::4][:4]                          # prologue, k/v handed over, scores, exp, sum, KV
+            assert np.all(np.diff(fused[:, [2, 4, 5, 6, 7, 3]], axis=1) >= 0)
+        assert np.all(t[1:, 1] >= t[:-1, 1])             # kernels' dependent sections run in order
+        assert t[-1, 3] - t[0, 0] < 10_000_000           # the step took less than 10 ms
     kv.free()
     model.free()
 
