@@ -59,7 +59,7 @@ __host__ __device__ inline size_t groups_bytes(int G, int64_t K) {
 // [256,512) ring bookkeeping, then the activation region, then the weight
 // ring; query CTAs add the K / V tiles and the scores after their ring.
 struct PSmem {
-  size_t lay, aq, ad, xs, sq, spec, res, ring, total;
+  size_t lay, aq, ad, xs, sq, spec, res, xloc, x2loc, ring, total;
 };
 constexpr int kMaxLayers = 128;
 __host__ __device__ inline PSmem persist_smem(int64_t E, int64_t FF, int n_layer) {
@@ -79,6 +79,10 @@ __host__ __device__ inline PSmem persist_smem(int64_t E, int64_t FF, int n_layer
   L.spec = off;
   off += up16((size_t)spec_sum_scratch_bytes(kNW, 2));
   L.res = off;
+  off += (size_t)kMaxRes * 4;
+  L.xloc = off;  // a projection CTA's own rows of x and x2 (the next residuals)
+  off += (size_t)kMaxRes * 4;
+  L.x2loc = off;
   off += (size_t)kMaxRes * 4;
   L.ring = up128(off);
   L.total = L.ring;
@@ -167,6 +171,7 @@ __device__ inline uint32_t item_bytes(const ItemDesc& d) {
 struct RingState {
   uint32_t head, tail;  // monotonic byte positions (issued / freed)
   int32_t next, freed;  // next item to issue, items freed
+  uint32_t R;           // ring bytes (query CTAs: grows once their tiles are free)
   uint32_t off[kQ], end[kQ];
 };
 
@@ -176,8 +181,10 @@ __device__ inline unsigned long long ld_acquire_u64(const unsigned long long* p)
   return v;
 }
 
-__device__ inline void pstamp(const PersistParams& p, int slot, int point) {
-  if (p.trace) p.trace[(size_t)slot * kTracePoints + point] = globaltimer_ns();
+// Step trace: per layer 32 stamps (16 of attention CTA 0, 16 of the first
+// projection CTA), then the LM head's; see persist_trace_points.
+__device__ inline void pstamp(const PersistParams& p, int layer, int point) {
+  if (p.trace) p.trace[(size_t)layer * 32 + point] = globaltimer_ns();
 }
 
 __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParams p) {
@@ -203,6 +210,8 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
   float* xs = (float*)(smem + L.xs);
   float* sq = (float*)(smem + L.sq);
   float* res = (float*)(smem + L.res);
+  float* xloc = (float*)(smem + L.xloc);
+  float* x2loc = (float*)(smem + L.x2loc);
   uint8_t* ring = smem + L.ring;
   PersistLayer* lay = (PersistLayer*)(smem + L.lay);
   for (int i = tid; i < p.n_layer * (int)(sizeof(PersistLayer) / 8); i += kNT)
@@ -218,23 +227,23 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
     r.kv = c == n_rep;
     r.h = r.kvh * n_rep + c;
     r.n_main = p.n_layer;
-    r.n_items = r.n_main;
   } else {
     const int wi = cta - p.n_attn;
-    const int GO = E / 4, GV = (int)(p.head_npad / 4);
+    const int GO = E / 4;
     r.o_g0 = (int)((int64_t)wi * GO / W);
     r.o_g1 = (int)((int64_t)(wi + 1) * GO / W);
     r.gu_b0 = (int)((int64_t)wi * nbF / W);
     r.gu_b1 = (int)((int64_t)(wi + 1) * nbF / W);
-    r.hd_g0 = (int)((int64_t)wi * GV / W);
-    r.hd_g1 = (int)((int64_t)(wi + 1) * GV / W);
     r.n_main = 3 * p.n_layer;
+  }
+  {
+    // every CTA streams a contiguous share of the LM head's rows
+    const int GV = (int)(p.head_npad / 4);
+    r.hd_g0 = (int)((int64_t)cta * GV / G);
+    r.hd_g1 = (int)((int64_t)(cta + 1) * GV / G);
     r.n_items = r.n_main + (p.with_head ? (r.hd_g1 - r.hd_g0 + kHeadChunkGroups - 1) / kHeadChunkGroups : 0);
   }
   const bool query = r.attn && !r.kv;
-  // ring bytes: the whole space after the activation region, except in query
-  // CTAs, whose K / V tiles and scores follow a ring of ring_attn bytes
-  const uint32_t R = query ? (uint32_t)p.ring_attn : (uint32_t)p.ring_gemv;
   const int KT = p.kv_tile, KP = D + 1;
   float* Ks = (float*)(ring + p.ring_attn);
   float* Vs = Ks + (size_t)KT * KP;
@@ -254,6 +263,10 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
     fence_mbar_init();
     rs->head = rs->tail = 0u;
     rs->next = rs->freed = 0;
+    // ring bytes: the whole space after the activation region, except in
+    // query CTAs, whose K / V tiles and scores follow a ring of ring_attn
+    // bytes until their last layer
+    rs->R = query ? (uint32_t)p.ring_attn : (uint32_t)p.ring_gemv;
     s_dead = 0;
   }
   __syncthreads();
@@ -266,6 +279,14 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
   auto issue_more = [&]() {
     fence_proxy_async_smem();
     while (rs->next < r.n_items && rs->next - rs->freed < kQ) {
+      if (rs->next == r.n_main && r.attn) {
+        // the LM head after the last layer: an attention CTA's tiles are free
+        // now; start over with the whole space once its last item is freed
+        if (rs->freed < r.n_main) break;
+        rs->head = rs->tail = 0u;
+        rs->R = (uint32_t)p.ring_gemv;
+      }
+      const uint32_t R = rs->R;
       const ItemDesc d = item_desc(p, lay, r, rs->next);
       const uint32_t bytes = item_bytes(d);
       const uint32_t off0 = rs->head % R;
@@ -327,12 +348,11 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
     }
     __syncthreads();
   };
+  // After the CTA barrier, one release add publishes every thread's stores
+  // made before it (the barrier orders them before thread 0's release).
   auto signal_ctr = [&](unsigned long long* c) {
     __syncthreads();
-    if (tid == 0) {
-      __threadfence();
-      atomicAdd(c, 1ull);
-    }
+    if (tid == 0) asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(c), "l"(1ull) : "memory");
   };
 
   // ---- building blocks ----
@@ -344,7 +364,9 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
 #pragma unroll
     for (int u = 0; u < 4; u++) nw[u] = warp + u * kNW < nbE ? norm_w[(warp + u * kNW) * 32 + lane] : 0.0f;
   };
-  auto norm_quant = [&](const float* x, bool embed, const float (&nw)[4], float* x_out) {
+  // (tl >= 0: trace stamps tp, tp + 1, tp + 2 of layer tl: x loaded, sum of
+  // squares done, quantized)
+  auto norm_quant = [&](const float* x, bool embed, const float (&nw)[4], float* x_out, int tl, int tp) {
     if (embed) {
       // mi_compute_get_rows on the Q8_0 embedding (ref src/ops_cpu.cpp:128-139)
       int tok = n_past < p.tokens_len ? p.tokens[n_past] : -1;
@@ -362,11 +384,13 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       for (int k = tid; k < E / 4; k += kNT) ((float4*)xs)[k] = __ldcg((const float4*)x + k);
     }
     __syncthreads();
+    if (tl >= 0 && tid == 0) pstamp(p, tl, tp);
     for (int k = tid; k < E; k += kNT) sq[k] = __fmul_rn(xs[k], xs[k]);
     __syncthreads();
     const float ss = spec_ordered_sum<kNT, 2>(sq, E, smem + L.spec);
     if (tid == 0) misc[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)E), p.eps)));
     __syncthreads();
+    if (tl >= 0 && tid == 0) pstamp(p, tl, tp + 1);
     const float scale = misc[0];
     // four blocks per warp at once overlap the quantizer's divisions
     float v[4], d[4];
@@ -387,6 +411,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       }
     }
     __syncthreads();
+    if (tl >= 0 && tid == 0) pstamp(p, tl, tp + 2);
   };
   // Q8_0_ACT blocks from global memory (coherent loads) into aq / ad.
   auto load_act = [&](const uint8_t* g, int nb) {
@@ -461,7 +486,6 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
 
   if (r.attn) {
     // ===================== attention CTAs =====================
-    const float* bias_base = nullptr;
     for (int l = 0; l < p.n_layer; l++) {
       const PersistLayer& Ly = lay[l];
       float* cache_k = p.cache + (size_t)l * 2 * p.n_ctx * HKV * D;
@@ -469,9 +493,9 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       const float* kbase = cache_k + (size_t)r.kvh * D;
       const float* vbase = cache_v + (size_t)r.kvh * D;
       const size_t rsd = (size_t)HKV * D;
-      if (tr_attn) pstamp(p, 2 * l, 0);
+      if (tr_attn) pstamp(p, l, 0);
       // operands that do not depend on this step's previous phases
-      bias_base = Ly.bqkv + (r.kv ? E + r.kvh * D : r.h * D);
+      const float* bias_base = Ly.bqkv + (r.kv ? E + r.kvh * D : r.h * D);
       const int half = D / 2;
       float2 rc = make_float2(0.0f, 0.0f);
       float b_lo = 0.0f, b_hi = 0.0f, b_v = 0.0f;
@@ -482,8 +506,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       }
       if (r.kv && tid < D) b_v = Ly.bqkv[E + HKV * D + r.kvh * D + tid];
       // cached K / V rows [c0, c0 + rows) into the tiles (position n_past,
-      // this step's, comes from kr / vr)
-      // (with_k / with_v: which of the two tiles to fill)
+      // this step's, comes from kr / vr) (with_k / with_v: which tiles)
       auto load_kv = [&](int c0, int rows, bool with_k, bool with_v) {
         const int D4 = D / 4, total = rows * D4;
         for (int e0 = tid; e0 < total; e0 += 4 * kNT) {
@@ -520,15 +543,15 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       load_nw(Ly.attn_norm, nw);
       // ---- x of this layer: the embedding (layer 0) or the down output ----
       if (l > 0) wait_ctr(&ctr[(size_t)(l - 1) * 4 + 3], tW);
-      if (tr_attn) pstamp(p, 2 * l, 1);
-      norm_quant(p.x, l == 0, nw, l == 0 && cta == 0 ? p.x : nullptr);
-      if (tr_attn) pstamp(p, 2 * l, 2);
+      if (tr_attn) pstamp(p, l, 1);
+      norm_quant(p.x, l == 0, nw, l == 0 && cta == 0 ? p.x : nullptr, tr_attn ? l : -1, 2);
       // ---- the CTA's q rows, or k and v rows ----
       const ItemDesc d = item_desc(p, lay, r, l);
       const uint8_t* wbase = wait_item(l);
+      if (tr_attn) pstamp(p, l, 5);
       rows_2t(wbase, d);  // ends with a CTA barrier: the item may be reused
       free_item(l);
-      if (tr_attn) pstamp(p, 2 * l, 3);
+      if (tr_attn) pstamp(p, l, 6);
       // ---- bias, RoPE (ref src/ops_cpu.cpp:286-297), v ----
       if (tid < half) {
         const float a0 = __fadd_rn(res[tid], b_lo), a1 = __fadd_rn(res[tid + half], b_hi);
@@ -538,6 +561,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       }
       if (r.kv && tid < D) vr[tid] = __fadd_rn(res[D + tid], b_v);
       __syncthreads();
+      if (tr_attn) pstamp(p, l, 7);
       if (r.kv) {
         // k / v into every query CTA of the cluster (st.async, counted on the
         // receiver's bar_kv), then the KV-cache append
@@ -563,7 +587,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         Vs[(size_t)n_past * D + tid] = vr[tid];
       }
       __syncthreads();
-      if (tr_attn) pstamp(p, 2 * l, 4);
+      if (tr_attn) pstamp(p, l, 8);
       float* sc = p.scores_in_smem ? scs : p.scores + (size_t)r.h * p.n_ctx;
       const int n_chunks = (n_kv + KT - 1) / KT;
       float lmax = -INFINITY;
@@ -583,14 +607,16 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
           lmax = fmaxf(lmax, v);
         }
       }
+      if (tr_attn) pstamp(p, l, 9);
       lmax = warp_max(lmax);
       if (lane == 0) red_f[warp] = lmax;
       __syncthreads();
       float mx = red_f[0];
       for (int w = 1; w < kNW; w++) mx = fmaxf(mx, red_f[w]);
+      if (tr_attn) pstamp(p, l, 10);
       for (int i = tid; i < n_kv; i += kNT) sc[i] = expf_exact(__fsub_rn(sc[i], mx), p.et);
       __syncthreads();
-      if (tr_attn) pstamp(p, 2 * l, 5);
+      if (tr_attn) pstamp(p, l, 11);
       // the softmax denominator: one ordered chain (src/ops_cpu.cpp:331-336)
       if (tid == 0) {
         float sum = 0.0f;
@@ -604,7 +630,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       }
       __syncthreads();
       const float inv = misc[1];
-      if (tr_attn) pstamp(p, 2 * l, 6);
+      if (tr_attn) pstamp(p, l, 12);
       // out[o] = sum_t V[o, kvh, t] * P[t], t ascending (src/ops_cpu.cpp:402-406);
       // the K / V tiles of the next layer replace these only after this loop
       float acc = 0.0f;
@@ -619,6 +645,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         }
         if (tid < D) acc = ordered_dot_scaled(acc, Vs + tid, D, sc + c0, inv, rows);
       }
+      if (tr_attn) pstamp(p, l, 13);
       // the O projection's quantize node (src/ops_cpu.cpp:462-479) for this
       // head's outputs: warp w holds block h*D/32 + w
       if (tid < D) {
@@ -628,26 +655,41 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         ((int8_t*)blk)[4 + lane] = q;
         if (lane == 0) *(float*)blk = dq;
       }
+      if (tr_attn) pstamp(p, l, 14);
       signal_ctr(&ctr[(size_t)l * 4 + 0]);
-      if (tr_attn) pstamp(p, 2 * l, 7);
+      if (tr_attn) pstamp(p, l, 15);
     }
   } else {
     // ===================== projection CTAs =====================
+    // Rows [4 o_g0, 4 o_g1) of the O and down projections are this CTA's in
+    // every layer, so the residual each of them adds is the row this CTA
+    // stored one phase earlier (kept in xloc / x2loc), except the embedding
+    // rows that layer 0's O adds.
+    const int rows_o = 4 * (r.o_g1 - r.o_g0), r0 = 4 * r.o_g0;
+    constexpr int tb = 16;  // projection stamps are points 16..31 of a layer
     for (int l = 0; l < p.n_layer; l++) {
       const PersistLayer& Ly = lay[l];
       // ---- O projection + residual: x2 = x + W_o . attn ----
       {
         const ItemDesc d = item_desc(p, lay, r, 3 * l);
-        const int rows = 4 * d.G[0], r0 = 4 * d.g0[0];
         wait_ctr(&ctr[(size_t)l * 4 + 0], tH);
-        if (tr_gemv) pstamp(p, 2 * l + 1, 0);
+        if (tr_gemv) pstamp(p, l, tb + 0);
         load_act(p.attn_q, nbE);
+        if (l == 0)
+          for (int i = tid; i < rows_o; i += kNT) xloc[i] = __ldcg(p.x + r0 + i);
+        if (tr_gemv) pstamp(p, l, tb + 1);
         const uint8_t* wb = wait_item(3 * l);
-        if (rows > 0) rows_2t(wb, d);
-        for (int i = tid; i < rows; i += kNT) p.x2[r0 + i] = __fadd_rn(__ldcg(p.x + r0 + i), res[i]);
+        if (tr_gemv) pstamp(p, l, tb + 2);
+        if (rows_o > 0) rows_2t(wb, d);
+        if (tr_gemv) pstamp(p, l, tb + 3);
+        for (int i = tid; i < rows_o; i += kNT) {
+          const float v = __fadd_rn(xloc[i], res[i]);
+          x2loc[i] = v;
+          p.x2[r0 + i] = v;
+        }
         signal_ctr(&ctr[(size_t)l * 4 + 1]);
         free_item(3 * l);
-        if (tr_gemv) pstamp(p, 2 * l + 1, 1);
+        if (tr_gemv) pstamp(p, l, tb + 4);
       }
       // ---- gate/up: rms_norm(x2) * ffn_norm, quantize; silu(gate) * up, quantize ----
       {
@@ -655,11 +697,11 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         float nw[4];
         load_nw(Ly.ffn_norm, nw);
         wait_ctr(&ctr[(size_t)l * 4 + 1], tW);
-        if (tr_gemv) pstamp(p, 2 * l + 1, 2);
-        norm_quant(p.x2, false, nw, nullptr);
-        if (tr_gemv) pstamp(p, 2 * l + 1, 3);
+        if (tr_gemv) pstamp(p, l, tb + 5);
+        norm_quant(p.x2, false, nw, nullptr, tr_gemv ? l : -1, tb + 6);
         const uint8_t* wb = wait_item(3 * l + 1);
         if (d.G[0] > 0) rows_2t(wb, d);
+        if (tr_gemv) pstamp(p, l, tb + 9);
         // each 64 packed rows are the gate / up rows of one 32-element block:
         // act[a] = silu(gate) * up, then the down projection's quantize node
         for (int j = warp; j < r.gu_b1 - r.gu_b0; j += kNW) {
@@ -672,78 +714,85 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
           ((int8_t*)blk)[4 + lane] = q;
           if (lane == 0) *(float*)blk = dq;
         }
+        if (tr_gemv) pstamp(p, l, tb + 10);
         signal_ctr(&ctr[(size_t)l * 4 + 2]);
         free_item(3 * l + 1);
-        if (tr_gemv) pstamp(p, 2 * l + 1, 4);
+        if (tr_gemv) pstamp(p, l, tb + 11);
       }
       // ---- down projection + residual: x = x2 + W_down . act ----
       {
         const ItemDesc d = item_desc(p, lay, r, 3 * l + 2);
-        const int rows = 4 * d.G[0], r0 = 4 * d.g0[0];
         wait_ctr(&ctr[(size_t)l * 4 + 2], tW);
-        if (tr_gemv) pstamp(p, 2 * l + 1, 5);
+        if (tr_gemv) pstamp(p, l, tb + 12);
         load_act(p.act_q, nbF);
         const uint8_t* wb = wait_item(3 * l + 2);
-        if (rows > 0) rows_8t(wb, d);
-        for (int i = tid; i < rows; i += kNT) p.x[r0 + i] = __fadd_rn(__ldcg(p.x2 + r0 + i), res[i]);
+        if (tr_gemv) pstamp(p, l, tb + 13);
+        if (rows_o > 0) rows_8t(wb, d);
+        if (tr_gemv) pstamp(p, l, tb + 14);
+        for (int i = tid; i < rows_o; i += kNT) {
+          const float v = __fadd_rn(x2loc[i], res[i]);
+          xloc[i] = v;
+          p.x[r0 + i] = v;
+        }
         signal_ctr(&ctr[(size_t)l * 4 + 3]);
         free_item(3 * l + 2);
-        if (tr_gemv) pstamp(p, 2 * l + 1, 6);
+        if (tr_gemv) pstamp(p, l, tb + 15);
       }
     }
-    // ---- LM head: rms_norm(x) * output_norm, quantize; logits; argmax ----
-    if (p.with_head) {
-      float nw[4];
-      load_nw(p.out_norm, nw);
-      wait_ctr(&ctr[(size_t)(p.n_layer - 1) * 4 + 3], tW);
-      if (tr_gemv) pstamp(p, 2 * p.n_layer, 0);
-      norm_quant(p.x, false, nw, nullptr);
-      if (tr_gemv) pstamp(p, 2 * p.n_layer, 1);
-      float bv = -INFINITY;
-      int32_t bi = 0x7fffffff;
-      for (int it = r.n_main; it < r.n_items; it++) {
-        const ItemDesc d = item_desc(p, lay, r, it);
-        const uint8_t* wb = wait_item(it);
-        rows_2t(wb, d);  // ends with a CTA barrier: the item may be reused
-        free_item(it);
-        const int r0 = 4 * d.g0[0];
-        for (int i = tid; i < 4 * d.G[0]; i += kNT) {
-          const int row = r0 + i;
-          if (row >= p.V) continue;
-          const float v = res[i];
-          p.logits[row] = v;
-          if (v > bv || bi == 0x7fffffff) {  // rows ascend per thread: first maximum
-            bv = v;
-            bi = row;
-          }
+  }
+  // ---- LM head (every CTA, its own rows): rms_norm(x) * output_norm,
+  // quantize; logits; the CTA's first maximum ----
+  if (p.with_head) {
+    float nw[4];
+    load_nw(p.out_norm, nw);
+    wait_ctr(&ctr[(size_t)(p.n_layer - 1) * 4 + 3], tW);
+    if (tr_gemv) pstamp(p, p.n_layer, 0);
+    norm_quant(p.x, false, nw, nullptr, -1, 0);
+    if (tr_gemv) pstamp(p, p.n_layer, 1);
+    float bv = -INFINITY;
+    int32_t bi = 0x7fffffff;
+    for (int it = r.n_main; it < r.n_items; it++) {
+      const ItemDesc d = item_desc(p, lay, r, it);
+      const uint8_t* wb = wait_item(it);
+      rows_2t(wb, d);  // ends with a CTA barrier: the item may be reused
+      free_item(it);
+      const int hr0 = 4 * d.g0[0];
+      for (int i = tid; i < 4 * d.G[0]; i += kNT) {
+        const int row = hr0 + i;
+        if (row >= p.V) continue;
+        const float v = res[i];
+        p.logits[row] = v;
+        if (v > bv || bi == 0x7fffffff) {  // rows ascend per thread: first maximum
+          bv = v;
+          bi = row;
         }
-        __syncthreads();  // res is rewritten by the next chunk
       }
+      __syncthreads();  // res is rewritten by the next chunk
+    }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(FULL, bv, o);
-        const int32_t oi = __shfl_xor_sync(FULL, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) {
-          bv = ov;
-          bi = oi;
-        }
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(FULL, bv, o);
+      const int32_t oi = __shfl_xor_sync(FULL, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
       }
-      if (lane == 0) {
-        red_f[warp] = bv;
-        red_i[warp] = bi;
-      }
-      __syncthreads();
-      if (tid == 0) {
-        for (int w = 1; w < kNW; w++)
-          if (red_f[w] > bv || (red_f[w] == bv && red_i[w] < bi)) {
-            bv = red_f[w];
-            bi = red_i[w];
-          }
-        p.part_val[cta - p.n_attn] = bv;
-        p.part_idx[cta - p.n_attn] = bi;
-      }
-      if (tr_gemv) pstamp(p, 2 * p.n_layer, 2);
     }
+    if (lane == 0) {
+      red_f[warp] = bv;
+      red_i[warp] = bi;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      for (int w = 1; w < kNW; w++)
+        if (red_f[w] > bv || (red_f[w] == bv && red_i[w] < bi)) {
+          bv = red_f[w];
+          bi = red_i[w];
+        }
+      p.part_val[cta] = bv;
+      p.part_idx[cta] = bi;
+    }
+    if (tr_gemv) pstamp(p, p.n_layer, 2);
   }
 
   // ---- close the step: the last CTA to finish advances the state ----
@@ -760,10 +809,10 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
   if (s_ticket == (uint32_t)G - 1 && tid == 0) {
     __threadfence();
     if (p.with_head) {
-      // the first maximum over the projection CTAs, whose row ranges ascend
+      // the first maximum over the CTAs, whose row ranges ascend
       float best = __ldcg(&p.part_val[0]);
       int32_t besti = __ldcg(&p.part_idx[0]);
-      for (int c = 1; c < W; c++) {
+      for (int c = 1; c < G; c++) {
         const float v = __ldcg(&p.part_val[c]);
         const int32_t i = __ldcg(&p.part_idx[c]);
         if (v > best || (v == best && i < besti)) {
@@ -777,7 +826,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
     *p.pos = n_past + 1;
     *p.epoch = epoch + 1ull;
     *p.ticket = 0u;
-    if (tr_gemv || tr_attn) pstamp(p, 2 * p.n_layer, 3);
+    if (tr_gemv || tr_attn) pstamp(p, p.n_layer, 3);
   }
   // peers may still store into this CTA's shared memory (k / v hand-over)
   // until every CTA of the cluster is here

@@ -1130,7 +1130,8 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
                o_pi = slot(1024 * 4), o_tok = slot((size_t)(n_ctx + 1) * 4),
                o_state = slot(sizeof(StepState)), o_attnq = slot(E / 32 * 36),
                o_actq = slot(FF / 32 * 36),
-               o_trace = slot((size_t)(6 * hp.n_layer + 1) * kTraceStamps * 8), o_epoch = slot(4),
+               o_trace = slot((size_t)std::max(6 * hp.n_layer + 1, 4 * hp.n_layer + 4) * kTraceStamps * 8),
+               o_epoch = slot(4),
                o_pctr = slot(((size_t)hp.n_layer * 4 + 2) * 8),
                o_play = slot((size_t)hp.n_layer * sizeof(PersistLayer));
   CK(cudaMalloc(&kv->buf, off));
@@ -1153,7 +1154,7 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
   kv->trace = (uint64_t*)(kv->buf + o_trace);
   // one slot per kernel of a step; the fused QKV + attention kernel adds two
   // detail slots per layer after the step's slots
-  kv->trace_slots = kv->persist ? 2 * hp.n_layer + 1 : 6 * hp.n_layer + 1;
+  kv->trace_slots = kv->persist ? 4 * hp.n_layer + 4 : 6 * hp.n_layer + 1;
   kv->epoch = (uint32_t*)(kv->buf + o_epoch);
   kv->pctr = (unsigned long long*)(kv->buf + o_pctr);
   kv->d_layers = (PersistLayer*)(kv->buf + o_play);
