@@ -22,11 +22,13 @@
 //    FFN gate/up (rms_norm + quantize prologue, SiLU * up + quantize epilogue)
 //    and the down projection (+ residual), each CTA its own rows; then all of
 //    them share the LM head and its argmax.
-//  * phases hand over through monotonic device counters (one per layer and
-//    phase): a producer CTA's threads store their outputs, the CTA
-//    synchronizes, one thread fences and increments; a consumer's thread 0
-//    polls with acquire loads until the count of this step is reached. Every
-//    poll is bounded (kSpinLimit) and records MI_CUDA_ERR_TIMEOUT on expiry.
+//  * phases hand over through tagged words: every value a phase passes on
+//    (the residual streams, the quantized attention and FFN activations) is
+//    stored as one 8-byte word, value bits | tag << 32, with a single 64-bit
+//    store (single-copy atomic), the tag naming the step and layer; a consumer
+//    polls each word it needs until it carries that tag. No flag, counter or
+//    fence sits between producer and consumer. Every poll is bounded
+//    (kSpinLimit) and records MI_CUDA_ERR_TIMEOUT on expiry.
 //  * every CTA streams the weights of its coming work items, in order, into
 //    a ring in shared memory with bulk async copies (one mbarrier per item),
 //    so weights arrive ahead of the phases that need them.
@@ -175,11 +177,6 @@ struct RingState {
   uint32_t off[kQ], end[kQ];
 };
 
-__device__ inline unsigned long long ld_acquire_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
 
 // Step trace: per layer 32 stamps (16 of attention CTA 0, 16 of the first
 // projection CTA), then the LM head's; see persist_trace_points.
@@ -257,8 +254,8 @@ __device__ __noinline__ void ring_issue(CtaState* cs, uint8_t* smem) {
 // token) -> xs; rms_norm(x) * norm weights (nw0..3: this lane's weights of
 // blocks warp + u * kNW); quantized into aq / ad (src/ops_cpu.cpp:128-139,
 // 154-160, 462-479). tl >= 0: trace stamps tp .. tp + 2 of layer tl.
-__device__ __noinline__ void norm_quant(CtaState* cs, uint8_t* smem, const float* x, int embed, float nw0, float nw1,
-                                        float nw2, float nw3, float* x_out, int tl, int tp) {
+__device__ __noinline__ void norm_quant(CtaState* cs, uint8_t* smem, const uint64_t* xw, uint32_t tag, int embed,
+                                        float nw0, float nw1, float nw2, float nw3, uint64_t* x_out, int tl, int tp) {
   const PersistParams& p = cs->p;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int E = p.E, nbE = E / 32;
@@ -278,10 +275,12 @@ __device__ __noinline__ void norm_quant(CtaState* cs, uint8_t* smem, const float
       const float v = __fmul_rn((float)packed_qs(p.embed, E, tok, k >> 5)[k & 31],
                                 packed_scale(p.embed, E, p.embed_npad, tok, k >> 5));
       xs[k] = v;
-      if (x_out) x_out[k] = v;
+      if (x_out) ll_store(x_out + k, __float_as_uint(v), tag);
     }
   } else {
-    for (int k = tid; k < E / 4; k += kNT) ((float4*)xs)[k] = __ldcg((const float4*)x + k);
+    bool dead = cs->dead != 0;
+    for (int k = tid; k < E; k += kNT) xs[k] = __uint_as_float(ll_wait(xw + k, tag, p.err, dead));
+    if (dead) cs->dead = 1;
   }
   __syncthreads();
   if (tl >= 0 && tid == 0) pstamp(p, tl, tp);
@@ -315,18 +314,31 @@ __device__ __noinline__ void norm_quant(CtaState* cs, uint8_t* smem, const float
   if (tl >= 0 && tid == 0) pstamp(p, tl, tp + 2);
 }
 
-// Q8_0_ACT blocks from global memory (coherent loads) into aq / ad.
-__device__ __noinline__ void load_act(uint8_t* smem, const CtaState* cs, const uint8_t* g, int nb) {
+// Q8_0_ACT blocks as tagged words (word 0 the scale, 1..8 the quants, four
+// to a word) into aq / ad, once every word carries `tag`.
+__device__ __noinline__ void load_act(uint8_t* smem, CtaState* cs, const uint64_t* w, int nb, uint32_t tag) {
   int8_t* aq = (int8_t*)(smem + cs->L.aq);
   float* ad = (float*)(smem + cs->L.ad);
-  const uint32_t* w = (const uint32_t*)g;
+  bool dead = cs->dead != 0;
   for (int e = threadIdx.x; e < nb * 9; e += kNT) {
-    const uint32_t v = __ldcg(w + e);
+    const uint32_t v = ll_wait(w + e, tag, cs->p.err, dead);
     const int b = e / 9, k = e - b * 9;
     if (k == 0) ad[b] = __uint_as_float(v);
     else ((uint32_t*)(aq + 32 * b))[k - 1] = v;
   }
+  if (dead) cs->dead = 1;
   __syncthreads();
+}
+
+// One quantized 32-element block held by a warp (lane i: element i, q its
+// quant, d the block scale) as 9 tagged words at w.
+__device__ __forceinline__ void put_block(uint64_t* w, int8_t q, float d, uint32_t tag) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t b0 = (uint8_t)q;
+  const uint32_t b1 = __shfl_down_sync(FULL, b0, 1), b2 = __shfl_down_sync(FULL, b0, 2),
+                 b3 = __shfl_down_sync(FULL, b0, 3);
+  if (lane == 0) ll_store(w, __float_as_uint(d), tag);
+  if ((lane & 3) == 0) ll_store(w + 1 + (lane >> 2), b0 | (b1 << 8) | (b2 << 16) | (b3 << 24), tag);
 }
 
 // Rows of a ring item of one or two group ranges (G0 then G1 groups of 4
@@ -422,23 +434,6 @@ __device__ __noinline__ void load_kv(const float* kbase, const float* vbase, int
       }
     }
   }
-}
-
-// Thread 0 polls a hand-over counter until it reaches target (bounded), then
-// the CTA synchronizes; after the barrier every thread sees what the
-// producers stored before their release add.
-__device__ __noinline__ void wait_ctr(CtaState* cs, const unsigned long long* c, unsigned long long target) {
-  if (threadIdx.x == 0 && !cs->dead) {
-    uint32_t it = 0;
-    while (ld_acquire_u64(c) < target) {
-      if (++it >= kSpinLimit || ((it & 1023u) == 0 && *(volatile int32_t*)cs->p.err != 0)) {
-        atomicExch(cs->p.err, 5 /* MI_CUDA_ERR_TIMEOUT */);
-        cs->dead = 1;
-        break;
-      }
-    }
-  }
-  __syncthreads();
 }
 
 __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParams p) {
@@ -549,20 +544,15 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
   };
   if (tid == 0) ring_issue(&cs, smem);
 
-  // After the CTA barrier, one release add publishes every thread's stores
-  // made before it (the barrier orders them before thread 0's release).
-  auto signal_ctr = [&](unsigned long long* c) {
-    __syncthreads();
-    if (tid == 0) asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(c), "l"(1ull) : "memory");
-  };
+
   // this lane's norm weights of blocks warp + u * kNW, loaded before a wait
   auto nwl = [&](const float* norm_w, int u) {
     return warp + u * kNW < nbE ? norm_w[(warp + u * kNW) * 32 + lane] : 0.0f;
   };
 
-  unsigned long long* const ctr = p.ctr;
-  const unsigned long long tH = (epoch + 1ull) * (unsigned long long)p.H;
-  const unsigned long long tW = (epoch + 1ull) * (unsigned long long)W;
+  // tags: the embedding base, layer l's outputs base + l + 1 (words start
+  // zeroed and base >= 1, so a word never matches before its first store)
+  const uint32_t base = (uint32_t)(epoch * (unsigned long long)(p.n_layer + 1) + 1ull);
 
   if (r.attn) {
     // ===================== attention CTAs =====================
@@ -591,9 +581,9 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       const float n0 = nwl(Ly.attn_norm, 0), n1 = nwl(Ly.attn_norm, 1), n2 = nwl(Ly.attn_norm, 2),
                   n3 = nwl(Ly.attn_norm, 3);
       // ---- x of this layer: the embedding (layer 0) or the down output ----
-      if (l > 0) wait_ctr(&cs, &ctr[(size_t)(l - 1) * 4 + 3], tW);
       if (tr_attn) pstamp(p, l, 1);
-      norm_quant(&cs, smem, p.x, l == 0, n0, n1, n2, n3, l == 0 && cta == 0 ? p.x : nullptr, tr_attn ? l : -1, 2);
+      norm_quant(&cs, smem, p.xw, base + (uint32_t)l, l == 0, n0, n1, n2, n3, l == 0 && cta == 0 ? p.xw : nullptr,
+                 tr_attn ? l : -1, 2);
       // ---- the CTA's q rows, or k and v rows ----
       const ItemDesc d = item_desc(p, lay, r, l);
       const uint8_t* wbase = wait_item(l);
@@ -698,12 +688,10 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       if (tid < D) {
         float dq;
         const int8_t q = quantize_lane(acc, &dq);
-        uint8_t* blk = p.attn_q + ((size_t)r.h * (D / 32) + (tid >> 5)) * 36;
-        ((int8_t*)blk)[4 + lane] = q;
-        if (lane == 0) *(float*)blk = dq;
+        put_block(p.attw + ((size_t)r.h * (D / 32) + (tid >> 5)) * 9, q, dq, base + (uint32_t)l + 1u);
       }
       if (tr_attn) pstamp(p, l, 14);
-      signal_ctr(&ctr[(size_t)l * 4 + 0]);
+      __syncthreads();  // the tiles and scores are reused by the next layer
       if (tr_attn) pstamp(p, l, 15);
     }
   } else {
@@ -716,12 +704,15 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
     constexpr int tb = 16;  // projection stamps are points 16..31 of a layer
     for (int l = 0; l < p.n_layer; l++) {
       const PersistLayer& Ly = lay[l];
+      const uint32_t tag = base + (uint32_t)l + 1u;
       // ---- O projection + residual: x2 = x + W_o . attn ----
-      wait_ctr(&cs, &ctr[(size_t)l * 4 + 0], tH);
       if (tr_gemv) pstamp(p, l, tb + 0);
-      load_act(smem, &cs, p.attn_q, nbE);
-      if (l == 0)
-        for (int i = tid; i < rows_o; i += kNT) xloc[i] = __ldcg(p.x + r0 + i);
+      if (l == 0) {
+        bool dead = cs.dead != 0;
+        for (int i = tid; i < rows_o; i += kNT) xloc[i] = __uint_as_float(ll_wait(p.xw + r0 + i, base, p.err, dead));
+        if (dead) cs.dead = 1;
+      }
+      load_act(smem, &cs, p.attw, nbE, tag);
       if (tr_gemv) pstamp(p, l, tb + 1);
       const uint8_t* wb = wait_item(3 * l);
       if (tr_gemv) pstamp(p, l, tb + 2);
@@ -730,19 +721,17 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       for (int i = tid; i < rows_o; i += kNT) {
         const float v = __fadd_rn(xloc[i], res[i]);
         x2loc[i] = v;
-        p.x2[r0 + i] = v;
+        ll_store(p.x2w + r0 + i, __float_as_uint(v), tag);
       }
-      signal_ctr(&ctr[(size_t)l * 4 + 1]);
-      free_item(3 * l);
+      free_item(3 * l);  // rows_2t ended with a CTA barrier
       if (tr_gemv) pstamp(p, l, tb + 4);
       // ---- gate/up: rms_norm(x2) * ffn_norm, quantize; silu(gate) * up, quantize ----
       const int nblk = r.gu_b1 - r.gu_b0;
       {
         const float n0 = nwl(Ly.ffn_norm, 0), n1 = nwl(Ly.ffn_norm, 1), n2 = nwl(Ly.ffn_norm, 2),
                     n3 = nwl(Ly.ffn_norm, 3);
-        wait_ctr(&cs, &ctr[(size_t)l * 4 + 1], tW);
         if (tr_gemv) pstamp(p, l, tb + 5);
-        norm_quant(&cs, smem, p.x2, 0, n0, n1, n2, n3, nullptr, tr_gemv ? l : -1, tb + 6);
+        norm_quant(&cs, smem, p.x2w, tag, 0, n0, n1, n2, n3, nullptr, tr_gemv ? l : -1, tb + 6);
       }
       wb = wait_item(3 * l + 1);
       if (nblk > 0) rows_2t(smem, &cs, wb, 16 * nblk, 0, E);
@@ -755,18 +744,15 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         const float v = __fmul_rn(silu_exact(res[lr], p.et), res[lr + 4]);
         float dq;
         const int8_t q = quantize_lane(v, &dq);
-        uint8_t* blk = p.act_q + (size_t)(r.gu_b0 + j) * 36;
-        ((int8_t*)blk)[4 + lane] = q;
-        if (lane == 0) *(float*)blk = dq;
+        put_block(p.actw + (size_t)(r.gu_b0 + j) * 9, q, dq, tag);
       }
       if (tr_gemv) pstamp(p, l, tb + 10);
-      signal_ctr(&ctr[(size_t)l * 4 + 2]);
+      __syncthreads();  // res is rewritten by the down rows
       free_item(3 * l + 1);
       if (tr_gemv) pstamp(p, l, tb + 11);
       // ---- down projection + residual: x = x2 + W_down . act ----
-      wait_ctr(&cs, &ctr[(size_t)l * 4 + 2], tW);
       if (tr_gemv) pstamp(p, l, tb + 12);
-      load_act(smem, &cs, p.act_q, nbF);
+      load_act(smem, &cs, p.actw, nbF, tag);
       wb = wait_item(3 * l + 2);
       if (tr_gemv) pstamp(p, l, tb + 13);
       if (rows_o > 0) rows_8t(smem, &cs, wb, rows_o / 4, FF);
@@ -774,10 +760,9 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       for (int i = tid; i < rows_o; i += kNT) {
         const float v = __fadd_rn(x2loc[i], res[i]);
         xloc[i] = v;
-        p.x[r0 + i] = v;
+        ll_store(p.xw + r0 + i, __float_as_uint(v), tag);
       }
-      signal_ctr(&ctr[(size_t)l * 4 + 3]);
-      free_item(3 * l + 2);
+      free_item(3 * l + 2);  // rows_8t ended with a CTA barrier
       if (tr_gemv) pstamp(p, l, tb + 15);
     }
   }
@@ -785,9 +770,8 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
   // quantize; logits; the CTA's first maximum ----
   if (p.with_head) {
     const float n0 = nwl(p.out_norm, 0), n1 = nwl(p.out_norm, 1), n2 = nwl(p.out_norm, 2), n3 = nwl(p.out_norm, 3);
-    wait_ctr(&cs, &ctr[(size_t)(p.n_layer - 1) * 4 + 3], tW);
     if (tr_gemv) pstamp(p, p.n_layer, 0);
-    norm_quant(&cs, smem, p.x, 0, n0, n1, n2, n3, nullptr, -1, 0);
+    norm_quant(&cs, smem, p.xw, base + (uint32_t)p.n_layer, 0, n0, n1, n2, n3, nullptr, -1, 0);
     if (tr_gemv) pstamp(p, p.n_layer, 1);
     float bv = -INFINITY;
     int32_t bi = 0x7fffffff;

@@ -149,7 +149,8 @@ struct mi_cuda_kv_cache {
   // layers' weight pointers.
   PersistPlan plan_persist{};
   bool persist = false;
-  unsigned long long* pctr = nullptr;  // [n_layer][4] | epoch | ticket
+  unsigned long long* pctr = nullptr;  // epoch | ticket, then the hand-over words
+  size_t pctr_words = 0;
   PersistLayer* d_layers = nullptr;
   cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
   // Batched-prefill workspace, allocated on first use and grown to the largest
@@ -521,10 +522,10 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     q.out_norm = m->output_norm;
     q.cache = kv->cache;
     q.rope = kv->rope;
-    q.x = kv->x;
-    q.x2 = kv->x2;
-    q.attn_q = kv->attn_q;
-    q.act_q = kv->act_q;
+    q.xw = (uint64_t*)kv->pctr + 2;
+    q.x2w = q.xw + E;
+    q.attw = q.x2w + E;
+    q.actw = q.attw + (E / 32) * 9;
     q.logits = kv->logits;
     q.scores = kv->scores;
     q.part_val = kv->part_val;
@@ -536,9 +537,8 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     q.next_token = &kv->state->next_token;
     q.feedback = &kv->state->feedback;
     q.err = err;
-    q.ctr = kv->pctr;
-    q.epoch = kv->pctr + (size_t)hp.n_layer * 4;
-    q.ticket = (uint32_t*)(kv->pctr + (size_t)hp.n_layer * 4 + 1);
+    q.epoch = kv->pctr;
+    q.ticket = (uint32_t*)(kv->pctr + 1);
     q.et = et;
     q.trace = kv->trace;
     CK(launch_persist(q, kv->plan_persist, kv->stream));
@@ -1132,7 +1132,7 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
                o_actq = slot(FF / 32 * 36),
                o_trace = slot((size_t)std::max(6 * hp.n_layer + 1, 4 * hp.n_layer + 4) * kTraceStamps * 8),
                o_epoch = slot(4),
-               o_pctr = slot(((size_t)hp.n_layer * 4 + 2) * 8),
+               o_pctr = slot((2 + 2 * (size_t)E + (size_t)(E / 32 + FF / 32) * 9) * 8),
                o_play = slot((size_t)hp.n_layer * sizeof(PersistLayer));
   CK(cudaMalloc(&kv->buf, off));
   CK(cudaMemset(kv->buf, 0, off));
@@ -1157,6 +1157,7 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
   kv->trace_slots = kv->persist ? 4 * hp.n_layer + 4 : 6 * hp.n_layer + 1;
   kv->epoch = (uint32_t*)(kv->buf + o_epoch);
   kv->pctr = (unsigned long long*)(kv->buf + o_pctr);
+  kv->pctr_words = 2 + 2 * (size_t)E + (size_t)(E / 32 + FF / 32) * 9;
   kv->d_layers = (PersistLayer*)(kv->buf + o_play);
   {
     std::vector<PersistLayer> pl((size_t)hp.n_layer);
@@ -1302,9 +1303,9 @@ int mi_cuda_qwen2_set_position(mi_cuda_kv_cache* kv, const int32_t* h_tokens, in
   kv->h_state->pos = pos;
   kv->h_state->feedback = 1;
   CK(cudaMemcpyAsync(kv->state, kv->h_state, sizeof(StepState), cudaMemcpyHostToDevice, kv->stream));
-  // a fresh start for the persistent step's hand-over counters (a step that
-  // gave up part-way leaves them behind their targets)
-  CK(cudaMemsetAsync(kv->pctr, 0, ((size_t)kv->model->hp.n_layer * 4 + 2) * 8, kv->stream));
+  // a fresh start for the persistent step: epoch 0, and no hand-over word
+  // carrying a tag the restarted epochs will use again
+  CK(cudaMemsetAsync(kv->pctr, 0, kv->pctr_words * 8, kv->stream));
   return MI_CUDA_OK;
 }
 
