@@ -208,20 +208,20 @@ def persist_trace_summary(kv) -> dict:
     a, g, h = st[:L, :16], st[:L, 16:], st[L]
     us = lambda v: round(float(np.mean(v)) / 1e3, 3)
     d = lambda m, i, j: us(m[:, j] - m[:, i])
-    att = ["layer_start", "x_ready", "x_loaded", "sum_squares", "quantized", "weights_ready", "qkv_rows",
-           "bias_rope", "kv_received", "scores", "max", "exp", "softmax_sum", "values", "out_quantized", "signalled"]
-    prj = ["o_wait", "o_input", "o_weights", "o_rows", "o_signalled", "gu_wait", "gu_x2_loaded", "gu_sum_squares",
-           "gu_quantized", "gu_rows", "gu_silu_quant", "gu_signalled", "down_wait", "down_input", "down_rows",
-           "down_signalled"]
+    att = ["layer_start", "prefetch", "x_received", "sum_squares", "quantized", "weights_ready", "qkv_rows",
+           "bias_rope", "kv_received", "scores", "max", "exp", "softmax_sum", "values", "out_stored", "synced"]
+    prj = ["o_start", "o_input_received", "o_weights", "o_rows", "o_stored", "gu_start", "gu_x2_received",
+           "gu_sum_squares", "gu_quantized", "gu_rows", "gu_silu_quant_stored", "gu_synced", "down_start",
+           "down_input_received", "down_rows", "down_stored"]
     return {
         "schedule": "persistent (one kernel per step)",
         "step_us": float(h[2] - a[0, 0]) / 1e3,
         "per_layer_us": us(np.diff(a[:, 0])) if L > 1 else None,
         "attention_cta_us": {att[j]: d(a, j - 1, j) for j in range(1, 16)},
-        "attention_x_wait_after_down_us": us(a[1:, 1] - g[:-1, 15]) if L > 1 else None,
-        "projection_cta_us": {"o_wait_after_heads": us(g[:, 0] - a[:, 15]),
+        "attention_x_after_down_rows_us": us(a[1:, 2] - g[:-1, 14]) if L > 1 else None,
+        "projection_cta_us": {"o_input_after_heads": us(g[:, 1] - a[:, 13]),
                               **{prj[j]: d(g, j - 1, j) for j in range(1, 16)}},
-        "lm_head_us": {"wait": float(h[0] - g[-1, 15]) / 1e3, "norm_quant": float(h[1] - h[0]) / 1e3,
+        "lm_head_us": {"start": float(h[0] - g[-1, 15]) / 1e3, "norm_quant": float(h[1] - h[0]) / 1e3,
                        "rows_argmax": float(h[2] - h[1]) / 1e3}}
 
 

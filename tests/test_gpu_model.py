@@ -131,8 +131,8 @@ def test_step_trace(mc, model_path, qkv_attn_path):
         attn, proj, head = st[:L, :16], st[:L, 16:], st[L, :3]
         assert np.all(attn > 0) and np.all(proj > 0) and np.all(head > 0)
         assert np.all(np.diff(attn, axis=1) >= 0) and np.all(np.diff(proj, axis=1) >= 0)
-        assert np.all(proj[:, 0] >= attn[:, 15] - 2000)   # O starts after the heads are done
-        assert np.all(attn[1:, 1] >= proj[:-1, 15] - 2000)  # a layer starts after the previous down
+        assert np.all(proj[:, 1] >= attn[:, 13] - 2000)   # O's input arrives after the heads are done
+        assert np.all(attn[1:, 2] >= proj[:-1, 14] - 2000)  # x arrives after the previous layer's down rows
         assert head[2] - attn[0, 0] < 10_000_000
     else:
         assert t.shape == (kv.kernels_per_step, 8) == (per * 4 + 1, 8)
