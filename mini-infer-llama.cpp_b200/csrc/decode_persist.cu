@@ -250,6 +250,49 @@ __device__ __noinline__ void ring_issue(CtaState* cs, uint8_t* smem) {
   }
 }
 
+// Every thread's words of w[0, n) (indices tid, tid + kNT, ...) once each
+// carries `tag`: the loads of a batch are all issued before any is checked,
+// so an arrival costs one memory round trip, not one per word. act == 0: the
+// values into dst (floats); act == 1: Q8_0_ACT blocks of 9 words (the scale,
+// then the quants four to a word) into aq / ad. Bounded like ll_wait.
+__device__ __noinline__ void poll_words(CtaState* cs, const uint64_t* w, int n, uint32_t tag, int act, float* dst,
+                                        int8_t* aq, float* ad) {
+  constexpr int B = 8;
+  const int tid = threadIdx.x;
+  int dead = cs->dead;
+  for (int e0 = 0; e0 < n; e0 += B * kNT) {
+    uint64_t v[B];
+#pragma unroll
+    for (int u = 0; u < B; u++) {
+      const int e = e0 + tid + u * kNT;
+      v[u] = e < n ? ll_load(w + e) : ((uint64_t)tag << 32);
+    }
+#pragma unroll
+    for (int u = 0; u < B; u++) {
+      const int e = e0 + tid + u * kNT;
+      if (e >= n) continue;
+      uint32_t it = 0;
+      while ((uint32_t)(v[u] >> 32) != tag && !dead) {
+        v[u] = ll_load(w + e);
+        if (++it >= kSpinLimit || ((it & 1023u) == 0 && *(volatile int32_t*)cs->p.err != 0)) {
+          atomicExch(cs->p.err, 5 /* MI_CUDA_ERR_TIMEOUT */);
+          dead = 1;
+        }
+      }
+      const uint32_t x = (uint32_t)v[u];
+      if (!act) {
+        dst[e] = __uint_as_float(x);
+      } else {
+        const int b = e / 9, k = e - b * 9;
+        if (k == 0) ad[b] = __uint_as_float(x);
+        else ((uint32_t*)(aq + 32 * b))[k - 1] = x;
+      }
+    }
+  }
+  if (dead) cs->dead = 1;
+  __syncthreads();
+}
+
 // x (coherent loads from L2; or, with embed, the embedding row of the step's
 // token) -> xs; rms_norm(x) * norm weights (nw0..3: this lane's weights of
 // blocks warp + u * kNW); quantized into aq / ad (src/ops_cpu.cpp:128-139,
@@ -277,12 +320,10 @@ __device__ __noinline__ void norm_quant(CtaState* cs, uint8_t* smem, const uint6
       xs[k] = v;
       if (x_out) ll_store(x_out + k, __float_as_uint(v), tag);
     }
+    __syncthreads();
   } else {
-    bool dead = cs->dead != 0;
-    for (int k = tid; k < E; k += kNT) xs[k] = __uint_as_float(ll_wait(xw + k, tag, p.err, dead));
-    if (dead) cs->dead = 1;
+    poll_words(cs, xw, E, tag, 0, xs, nullptr, nullptr);  // ends with a CTA barrier
   }
-  __syncthreads();
   if (tl >= 0 && tid == 0) pstamp(p, tl, tp);
   for (int k = tid; k < E; k += kNT) sq[k] = __fmul_rn(xs[k], xs[k]);
   __syncthreads();
@@ -316,18 +357,8 @@ __device__ __noinline__ void norm_quant(CtaState* cs, uint8_t* smem, const uint6
 
 // Q8_0_ACT blocks as tagged words (word 0 the scale, 1..8 the quants, four
 // to a word) into aq / ad, once every word carries `tag`.
-__device__ __noinline__ void load_act(uint8_t* smem, CtaState* cs, const uint64_t* w, int nb, uint32_t tag) {
-  int8_t* aq = (int8_t*)(smem + cs->L.aq);
-  float* ad = (float*)(smem + cs->L.ad);
-  bool dead = cs->dead != 0;
-  for (int e = threadIdx.x; e < nb * 9; e += kNT) {
-    const uint32_t v = ll_wait(w + e, tag, cs->p.err, dead);
-    const int b = e / 9, k = e - b * 9;
-    if (k == 0) ad[b] = __uint_as_float(v);
-    else ((uint32_t*)(aq + 32 * b))[k - 1] = v;
-  }
-  if (dead) cs->dead = 1;
-  __syncthreads();
+__device__ __forceinline__ void load_act(uint8_t* smem, CtaState* cs, const uint64_t* w, int nb, uint32_t tag) {
+  poll_words(cs, w, nb * 9, tag, 1, nullptr, (int8_t*)(smem + cs->L.aq), (float*)(smem + cs->L.ad));
 }
 
 // One quantized 32-element block held by a warp (lane i: element i, q its
@@ -707,11 +738,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       const uint32_t tag = base + (uint32_t)l + 1u;
       // ---- O projection + residual: x2 = x + W_o . attn ----
       if (tr_gemv) pstamp(p, l, tb + 0);
-      if (l == 0) {
-        bool dead = cs.dead != 0;
-        for (int i = tid; i < rows_o; i += kNT) xloc[i] = __uint_as_float(ll_wait(p.xw + r0 + i, base, p.err, dead));
-        if (dead) cs.dead = 1;
-      }
+      if (l == 0) poll_words(&cs, p.xw + r0, rows_o, base, 0, xloc, nullptr, nullptr);
       load_act(smem, &cs, p.attw, nbE, tag);
       if (tr_gemv) pstamp(p, l, tb + 1);
       const uint8_t* wb = wait_item(3 * l);
