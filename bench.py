@@ -203,25 +203,23 @@ def persist_trace_summary(kv) -> dict:
     """Phase timeline of the last timed persistent step (one kernel): per
     layer, from attention CTA 0 and the first projection CTA, means over the
     layers in microseconds."""
+    t = kv.step_trace().astype(np.int64)
     L = kv.model.hparams.n_layer
-    st = kv.step_trace().astype(np.int64).reshape(-1, 32)
-    a, g, h = st[:L, :16], st[:L, 16:], st[L]
-    us = lambda v: round(float(np.mean(v)) / 1e3, 3)
-    d = lambda m, i, j: us(m[:, j] - m[:, i])
-    att = ["layer_start", "prefetch", "x_received", "sum_squares", "quantized", "weights_ready", "qkv_rows",
-           "bias_rope", "kv_received", "scores", "max", "exp", "softmax_sum", "values", "out_stored", "synced"]
-    prj = ["o_start", "o_input_received", "o_weights", "o_rows", "o_stored", "gu_start", "gu_x2_received",
-           "gu_sum_squares", "gu_quantized", "gu_rows", "gu_silu_quant_stored", "gu_synced", "down_start",
-           "down_input_received", "down_rows", "down_stored"]
+    a, g, h = t[0:2 * L:2], t[1:2 * L:2], t[2 * L]
+    us = lambda v: float(np.mean(v)) / 1e3
     return {
         "schedule": "persistent (one kernel per step)",
         "step_us": float(h[2] - a[0, 0]) / 1e3,
-        "per_layer_us": us(np.diff(a[:, 0])) if L > 1 else None,
-        "attention_cta_us": {att[j]: d(a, j - 1, j) for j in range(1, 16)},
-        "attention_x_after_down_rows_us": us(a[1:, 2] - g[:-1, 14]) if L > 1 else None,
-        "projection_cta_us": {"o_input_after_heads": us(g[:, 1] - a[:, 13]),
-                              **{prj[j]: d(g, j - 1, j) for j in range(1, 16)}},
-        "lm_head_us": {"start": float(h[0] - g[-1, 15]) / 1e3, "norm_quant": float(h[1] - h[0]) / 1e3,
+        "per_layer_us": us(np.diff(a[:, 1])) if L > 1 else None,
+        "attention_cta_us": {"x_wait": us(a[1:, 1] - g[:-1, 6]) if L > 1 else None,
+                             "norm_quant": us(a[:, 2] - a[:, 1]), "qkv_rows": us(a[:, 3] - a[:, 2]),
+                             "kv_handover": us(a[:, 4] - a[:, 3]), "scores_exp": us(a[:, 5] - a[:, 4]),
+                             "softmax_sum": us(a[:, 6] - a[:, 5]), "values_quant_signal": us(a[:, 7] - a[:, 6])},
+        "projection_cta_us": {"o_wait_after_heads": us(g[:, 0] - a[:, 7]), "o": us(g[:, 1] - g[:, 0]),
+                              "gate_up_wait": us(g[:, 2] - g[:, 1]), "gate_up_norm_quant": us(g[:, 3] - g[:, 2]),
+                              "gate_up_rows": us(g[:, 4] - g[:, 3]), "down_wait": us(g[:, 5] - g[:, 4]),
+                              "down": us(g[:, 6] - g[:, 5])},
+        "lm_head_us": {"wait": float(h[0] - g[-1, 6]) / 1e3, "norm_quant": float(h[1] - h[0]) / 1e3,
                        "rows_argmax": float(h[2] - h[1]) / 1e3}}
 
 

@@ -22,13 +22,11 @@
 //    FFN gate/up (rms_norm + quantize prologue, SiLU * up + quantize epilogue)
 //    and the down projection (+ residual), each CTA its own rows; then all of
 //    them share the LM head and its argmax.
-//  * phases hand over through tagged words: every value a phase passes on
-//    (the residual streams, the quantized attention and FFN activations) is
-//    stored as one 8-byte word, value bits | tag << 32, with a single 64-bit
-//    store (single-copy atomic), the tag naming the step and layer; a consumer
-//    polls each word it needs until it carries that tag. No flag, counter or
-//    fence sits between producer and consumer. Every poll is bounded
-//    (kSpinLimit) and records MI_CUDA_ERR_TIMEOUT on expiry.
+//  * phases hand over through monotonic device counters (one per layer and
+//    phase): a producer CTA's threads store their outputs, the CTA
+//    synchronizes, one thread fences and increments; a consumer's thread 0
+//    polls with acquire loads until the count of this step is reached. Every
+//    poll is bounded (kSpinLimit) and records MI_CUDA_ERR_TIMEOUT on expiry.
 //  * every CTA streams the weights of its coming work items, in order, into
 //    a ring in shared memory with bulk async copies (one mbarrier per item),
 //    so weights arrive ahead of the phases that need them.
@@ -61,7 +59,7 @@ __host__ __device__ inline size_t groups_bytes(int G, int64_t K) {
 // [256,512) ring bookkeeping, then the activation region, then the weight
 // ring; query CTAs add the K / V tiles and the scores after their ring.
 struct PSmem {
-  size_t lay, aq, ad, xs, sq, spec, res, xloc, x2loc, ring, total;
+  size_t lay, aq, ad, xs, sq, spec, res, ring, total;
 };
 constexpr int kMaxLayers = 128;
 __host__ __device__ inline PSmem persist_smem(int64_t E, int64_t FF, int n_layer) {
@@ -81,10 +79,6 @@ __host__ __device__ inline PSmem persist_smem(int64_t E, int64_t FF, int n_layer
   L.spec = off;
   off += up16((size_t)spec_sum_scratch_bytes(kNW, 2));
   L.res = off;
-  off += (size_t)kMaxRes * 4;
-  L.xloc = off;  // a projection CTA's own rows of x and x2 (the next residuals)
-  off += (size_t)kMaxRes * 4;
-  L.x2loc = off;
   off += (size_t)kMaxRes * 4;
   L.ring = up128(off);
   L.total = L.ring;
@@ -173,298 +167,17 @@ __device__ inline uint32_t item_bytes(const ItemDesc& d) {
 struct RingState {
   uint32_t head, tail;  // monotonic byte positions (issued / freed)
   int32_t next, freed;  // next item to issue, items freed
-  uint32_t R;           // ring bytes (query CTAs: grows once their tiles are free)
   uint32_t off[kQ], end[kQ];
 };
 
-
-// Step trace: per layer 32 stamps (16 of attention CTA 0, 16 of the first
-// projection CTA), then the LM head's; see persist_trace_points.
-__device__ inline void pstamp(const PersistParams& p, int layer, int point) {
-  if (p.trace) p.trace[(size_t)layer * 32 + point] = globaltimer_ns();
+__device__ inline unsigned long long ld_acquire_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 
-// ---------------------------------------------------------------------------
-// Building blocks, each a separate (not inlined) function: every phase of
-// every layer runs the same few copies of this code, which then stay in the
-// SM's instruction caches (inlined at every call site, the kernel's code was
-// several times the instruction cache, and phases stalled on fetching it).
-// ---------------------------------------------------------------------------
-
-// Per-CTA state in shared memory: the kernel parameters, the CTA's role and
-// the shared-memory map, read by the building blocks.
-struct CtaState {
-  PersistParams p;
-  Role r;
-  PSmem L;
-  int32_t n_past, dead;
-  uint32_t R;
-};
-
-__device__ __forceinline__ const PersistLayer* lay_of(uint8_t* smem, const CtaState* cs) {
-  return (const PersistLayer*)(smem + cs->L.lay);
-}
-
-// Thread 0: issues the next items of the CTA's list, in order, while they
-// fit the ring and fewer than kQ are in flight.
-__device__ __noinline__ void ring_issue(CtaState* cs, uint8_t* smem) {
-  const PersistParams& p = cs->p;
-  const Role& r = cs->r;
-  RingState* rs = (RingState*)(smem + 256);
-  uint64_t* bars = (uint64_t*)smem;
-  uint8_t* ring = smem + cs->L.ring;
-  fence_proxy_async_smem();
-  while (rs->next < r.n_items && rs->next - rs->freed < kQ) {
-    if (rs->next == r.n_main && r.attn) {
-      // the LM head after the last layer: an attention CTA's tiles are free
-      // now; start over with the whole space once its last item is freed
-      if (rs->freed < r.n_main) break;
-      rs->head = rs->tail = 0u;
-      rs->R = (uint32_t)p.ring_gemv;
-    }
-    const uint32_t R = rs->R;
-    const ItemDesc d = item_desc(p, lay_of(smem, cs), r, rs->next);
-    const uint32_t bytes = item_bytes(d);
-    const uint32_t off0 = rs->head % R;
-    const uint32_t pad = off0 + bytes > R ? R - off0 : 0u;
-    if (rs->head + pad + bytes - rs->tail > R) break;
-    rs->head += pad;
-    const uint32_t off = rs->head % R;
-    const int slot = rs->next % kQ;
-    rs->off[slot] = off;
-    rs->end[slot] = rs->head + bytes;
-    uint32_t tx = 0;
-    for (int i = 0; i < d.n; i++) tx += (uint32_t)(d.G[i] * 4 * d.K + d.G[i] * (d.K / 32) * 8);
-    mbar_arrive_expect_tx(&bars[slot], tx);
-    uint32_t o = off;
-    for (int i = 0; i < d.n; i++) {
-      if (d.G[i] > 0) {
-        const uint32_t qb = (uint32_t)(d.G[i] * 4 * d.K), db = (uint32_t)(d.G[i] * (d.K / 32) * 8);
-        bulk_load(ring + o, d.w + (int64_t)d.g0[i] * 4 * d.K, qb, &bars[slot]);
-        bulk_load(ring + o + qb, d.w + d.npad * d.K + (int64_t)d.g0[i] * (d.K / 32) * 8, db, &bars[slot]);
-      }
-      o += (uint32_t)groups_bytes(d.G[i], d.K);
-    }
-    rs->head += bytes;
-    rs->next++;
-  }
-}
-
-// Every thread's words of w[0, n) (indices tid, tid + kNT, ...) once each
-// carries `tag`: the loads of a batch are all issued before any is checked,
-// so an arrival costs one memory round trip, not one per word. act == 0: the
-// values into dst (floats); act == 1: Q8_0_ACT blocks of 9 words (the scale,
-// then the quants four to a word) into aq / ad. Bounded like ll_wait.
-__device__ __noinline__ void poll_words(CtaState* cs, const uint64_t* w, int n, uint32_t tag, int act, float* dst,
-                                        int8_t* aq, float* ad) {
-  constexpr int B = 8;
-  const int tid = threadIdx.x;
-  int dead = cs->dead;
-  for (int e0 = 0; e0 < n; e0 += B * kNT) {
-    uint64_t v[B];
-#pragma unroll
-    for (int u = 0; u < B; u++) {
-      const int e = e0 + tid + u * kNT;
-      v[u] = e < n ? ll_load(w + e) : ((uint64_t)tag << 32);
-    }
-#pragma unroll
-    for (int u = 0; u < B; u++) {
-      const int e = e0 + tid + u * kNT;
-      if (e >= n) continue;
-      uint32_t it = 0;
-      while ((uint32_t)(v[u] >> 32) != tag && !dead) {
-        v[u] = ll_load(w + e);
-        if (++it >= kSpinLimit || ((it & 1023u) == 0 && *(volatile int32_t*)cs->p.err != 0)) {
-          atomicExch(cs->p.err, 5 /* MI_CUDA_ERR_TIMEOUT */);
-          dead = 1;
-        }
-      }
-      const uint32_t x = (uint32_t)v[u];
-      if (!act) {
-        dst[e] = __uint_as_float(x);
-      } else {
-        const int b = e / 9, k = e - b * 9;
-        if (k == 0) ad[b] = __uint_as_float(x);
-        else ((uint32_t*)(aq + 32 * b))[k - 1] = x;
-      }
-    }
-  }
-  if (dead) cs->dead = 1;
-  __syncthreads();
-}
-
-// x (coherent loads from L2; or, with embed, the embedding row of the step's
-// token) -> xs; rms_norm(x) * norm weights (nw0..3: this lane's weights of
-// blocks warp + u * kNW); quantized into aq / ad (src/ops_cpu.cpp:128-139,
-// 154-160, 462-479). tl >= 0: trace stamps tp .. tp + 2 of layer tl.
-__device__ __noinline__ void norm_quant(CtaState* cs, uint8_t* smem, const uint64_t* xw, uint32_t tag, int embed,
-                                        float nw0, float nw1, float nw2, float nw3, uint64_t* x_out, int tl, int tp) {
-  const PersistParams& p = cs->p;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int E = p.E, nbE = E / 32;
-  float* xs = (float*)(smem + cs->L.xs);
-  float* sq = (float*)(smem + cs->L.sq);
-  int8_t* aq = (int8_t*)(smem + cs->L.aq);
-  float* ad = (float*)(smem + cs->L.ad);
-  float* misc = (float*)(smem + 256 + sizeof(RingState));
-  if (embed) {
-    const int n_past = cs->n_past;
-    int tok = n_past < p.tokens_len ? p.tokens[n_past] : -1;
-    if (tok < 0 || tok >= p.V) {
-      if (tid == 0) atomicExch(p.err, 1 /* MI_CUDA_ERR_ARG */);
-      tok = 0;
-    }
-    for (int k = tid; k < E; k += kNT) {
-      const float v = __fmul_rn((float)packed_qs(p.embed, E, tok, k >> 5)[k & 31],
-                                packed_scale(p.embed, E, p.embed_npad, tok, k >> 5));
-      xs[k] = v;
-      if (x_out) ll_store(x_out + k, __float_as_uint(v), tag);
-    }
-    __syncthreads();
-  } else {
-    poll_words(cs, xw, E, tag, 0, xs, nullptr, nullptr);  // ends with a CTA barrier
-  }
-  if (tl >= 0 && tid == 0) pstamp(p, tl, tp);
-  for (int k = tid; k < E; k += kNT) sq[k] = __fmul_rn(xs[k], xs[k]);
-  __syncthreads();
-  const float ss = spec_ordered_sum<kNT, 2>(sq, E, smem + cs->L.spec);
-  if (tid == 0) misc[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)E), p.eps)));
-  __syncthreads();
-  if (tl >= 0 && tid == 0) pstamp(p, tl, tp + 1);
-  const float scale = misc[0];
-  // four blocks per warp at once overlap the quantizer's divisions
-  const float nw[4] = {nw0, nw1, nw2, nw3};
-  float v[4], d[4];
-  int8_t q[4];
-#pragma unroll
-  for (int u = 0; u < 4; u++) {
-    const int b = warp + u * kNW;
-    v[u] = b < nbE ? __fmul_rn(__fmul_rn(xs[b * 32 + lane], scale), nw[u]) : 0.0f;
-  }
-#pragma unroll
-  for (int u = 0; u < 4; u++) q[u] = quantize_lane(v[u], &d[u]);
-#pragma unroll
-  for (int u = 0; u < 4; u++) {
-    const int b = warp + u * kNW;
-    if (b < nbE) {
-      aq[b * 32 + lane] = q[u];
-      if (lane == 0) ad[b] = d[u];
-    }
-  }
-  __syncthreads();
-  if (tl >= 0 && tid == 0) pstamp(p, tl, tp + 2);
-}
-
-// Q8_0_ACT blocks as tagged words (word 0 the scale, 1..8 the quants, four
-// to a word) into aq / ad, once every word carries `tag`.
-__device__ __forceinline__ void load_act(uint8_t* smem, CtaState* cs, const uint64_t* w, int nb, uint32_t tag) {
-  poll_words(cs, w, nb * 9, tag, 1, nullptr, (int8_t*)(smem + cs->L.aq), (float*)(smem + cs->L.ad));
-}
-
-// One quantized 32-element block held by a warp (lane i: element i, q its
-// quant, d the block scale) as 9 tagged words at w.
-__device__ __forceinline__ void put_block(uint64_t* w, int8_t q, float d, uint32_t tag) {
-  const int lane = threadIdx.x & 31;
-  const uint32_t b0 = (uint8_t)q;
-  const uint32_t b1 = __shfl_down_sync(FULL, b0, 1), b2 = __shfl_down_sync(FULL, b0, 2),
-                 b3 = __shfl_down_sync(FULL, b0, 3);
-  if (lane == 0) ll_store(w, __float_as_uint(d), tag);
-  if ((lane & 3) == 0) ll_store(w + 1 + (lane >> 2), b0 | (b1 << 8) | (b2 << 16) | (b3 << 24), tag);
-}
-
-// Rows of a ring item of one or two group ranges (G0 then G1 groups of 4
-// rows, K columns), 2 threads per row: res[4g + r] = dot(row, act), the AVX2
-// lane order (src/quant_avx2.cpp:170-181, hsum order :74-83).
-__device__ __noinline__ void rows_2t(uint8_t* smem, const CtaState* cs, const uint8_t* base, int G0, int G1, int K) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint4* aq16 = (const uint4*)(smem + cs->L.aq);
-  const float* ad = (const float*)(smem + cs->L.ad);
-  float* res = (float*)(smem + cs->L.res);
-  const int nb = K / 32, Gt = G0 + G1;
-  const int gw = lane >> 3, r4 = (lane >> 1) & 3, hh = lane & 1;
-  for (int g0 = warp * 4; g0 < Gt; g0 += kNW * 4) {
-    const int g = g0 + gw;
-    const bool valid = g < Gt;
-    int gc = valid ? g : g0;
-    const uint8_t* rb = base;
-    int Gr = G0;
-    if (gc >= G0) {
-      rb = base + groups_bytes(G0, K);
-      gc -= G0;
-      Gr = G1;
-    }
-    const uint4* gq = (const uint4*)(rb + (size_t)gc * 4 * K);
-    const __half* gd = (const __half*)(rb + (size_t)Gr * 4 * K) + (size_t)gc * nb * 4;
-    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-#pragma unroll 2
-    for (int i = 0; i < nb; i++) {
-      const uint4 w = gq[i * 8 + (lane & 7)];
-      const uint4 a = aq16[i * 2 + hh];
-      const float dxdy = __fmul_rn(__half2float(gd[i * 4 + r4]), ad[i]);
-      a0 = __fmaf_rn(__int2float_rn(__dp4a((int)w.x, (int)a.x, 0)), dxdy, a0);
-      a1 = __fmaf_rn(__int2float_rn(__dp4a((int)w.y, (int)a.y, 0)), dxdy, a1);
-      a2 = __fmaf_rn(__int2float_rn(__dp4a((int)w.z, (int)a.z, 0)), dxdy, a2);
-      a3 = __fmaf_rn(__int2float_rn(__dp4a((int)w.w, (int)a.w, 0)), dxdy, a3);
-    }
-    const float s0 = __fadd_rn(a0, __shfl_xor_sync(FULL, a0, 1));
-    const float s1 = __fadd_rn(a1, __shfl_xor_sync(FULL, a1, 1));
-    const float s2 = __fadd_rn(a2, __shfl_xor_sync(FULL, a2, 1));
-    const float s3 = __fadd_rn(a3, __shfl_xor_sync(FULL, a3, 1));
-    if (valid && hh == 0) res[g * 4 + r4] = __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
-  }
-  __syncthreads();
-}
-
-// Rows of a ring item with long rows (G groups, K columns), 8 threads per
-// row (one AVX2 lane each; a warp per group of 4 rows).
-__device__ __noinline__ void rows_8t(uint8_t* smem, const CtaState* cs, const uint8_t* base, int G, int K) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int* aq4 = (const int*)(smem + cs->L.aq);
-  const float* ad = (const float*)(smem + cs->L.ad);
-  float* res = (float*)(smem + cs->L.res);
-  const int nb = K / 32, rr = lane >> 3, j = lane & 7;
-  for (int g = warp; g < G; g += kNW) {
-    const uint32_t* gq = (const uint32_t*)(base + (size_t)g * 4 * K);
-    const __half* gd = (const __half*)(base + (size_t)G * 4 * K) + (size_t)g * nb * 4;
-    const float acc = lane_chain(0.0f, gq, gd, aq4, ad, nb, lane, j, rr);
-    const float s4 = __fadd_rn(acc, __shfl_xor_sync(FULL, acc, 4));
-    const float s1 = __fadd_rn(s4, __shfl_xor_sync(FULL, s4, 1));
-    const float s2 = __fadd_rn(s1, __shfl_xor_sync(FULL, s1, 2));
-    if (j == 0) res[g * 4 + rr] = s2;
-  }
-  __syncthreads();
-}
-
-// Cached K / V rows [c0, c0 + rows) of one KV head into the tiles (position
-// skip, this step's, comes from the k/v CTA instead).
-__device__ __noinline__ void load_kv(const float* kbase, const float* vbase, int rsd, int c0, int rows, int skip,
-                                     int D, float* Ks, float* Vs, int with_k, int with_v) {
-  const int tid = threadIdx.x, D4 = D / 4, KP = D + 1, total = rows * D4;
-  for (int e0 = tid; e0 < total; e0 += 4 * kNT) {
-    float4 vk[4], vv[4];
-#pragma unroll
-    for (int u = 0; u < 4; u++) {
-      const int e = e0 + u * kNT, rw = e / D4, c = e - rw * D4;
-      if (e < total && c0 + rw != skip) {
-        if (with_k) vk[u] = __ldcg((const float4*)(kbase + (size_t)(c0 + rw) * rsd) + c);
-        if (with_v) vv[u] = __ldcg((const float4*)(vbase + (size_t)(c0 + rw) * rsd) + c);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 4; u++) {
-      const int e = e0 + u * kNT, rw = e / D4, c = e - rw * D4;
-      if (e < total && c0 + rw != skip) {
-        if (with_k) {
-          float* dk = Ks + (size_t)rw * KP + c * 4;
-          dk[0] = vk[u].x;
-          dk[1] = vk[u].y;
-          dk[2] = vk[u].z;
-          dk[3] = vk[u].w;
-        }
-        if (with_v) *(float4*)(Vs + (size_t)rw * D + c * 4) = vv[u];
-      }
-    }
-  }
+__device__ inline void pstamp(const PersistParams& p, int slot, int point) {
+  if (p.trace) p.trace[(size_t)slot * kTracePoints + point] = globaltimer_ns();
 }
 
 __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParams p) {
@@ -472,8 +185,9 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
   __shared__ __align__(16) float qr[128], kr[128], vr[128];
   __shared__ float red_f[kNW];
   __shared__ int32_t red_i[kNW];
+  __shared__ float misc[4];
+  __shared__ int s_dead;
   __shared__ uint32_t s_ticket;
-  __shared__ CtaState cs;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int cta = (int)blockIdx.x, G = (int)gridDim.x;
@@ -484,10 +198,11 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
   uint64_t* bars = (uint64_t*)smem;      // kQ ring barriers
   uint64_t* bar_kv = bars + kQ;          // query CTAs: k / v from the k/v CTA
   RingState* rs = (RingState*)(smem + 256);
-  float* misc = (float*)(smem + 256 + sizeof(RingState));
+  int8_t* aq = (int8_t*)(smem + L.aq);
+  float* ad = (float*)(smem + L.ad);
+  float* xs = (float*)(smem + L.xs);
+  float* sq = (float*)(smem + L.sq);
   float* res = (float*)(smem + L.res);
-  float* xloc = (float*)(smem + L.xloc);
-  float* x2loc = (float*)(smem + L.x2loc);
   uint8_t* ring = smem + L.ring;
   PersistLayer* lay = (PersistLayer*)(smem + L.lay);
   for (int i = tid; i < p.n_layer * (int)(sizeof(PersistLayer) / 8); i += kNT)
@@ -503,23 +218,23 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
     r.kv = c == n_rep;
     r.h = r.kvh * n_rep + c;
     r.n_main = p.n_layer;
+    r.n_items = r.n_main;
   } else {
     const int wi = cta - p.n_attn;
-    const int GO = E / 4;
+    const int GO = E / 4, GV = (int)(p.head_npad / 4);
     r.o_g0 = (int)((int64_t)wi * GO / W);
     r.o_g1 = (int)((int64_t)(wi + 1) * GO / W);
     r.gu_b0 = (int)((int64_t)wi * nbF / W);
     r.gu_b1 = (int)((int64_t)(wi + 1) * nbF / W);
+    r.hd_g0 = (int)((int64_t)wi * GV / W);
+    r.hd_g1 = (int)((int64_t)(wi + 1) * GV / W);
     r.n_main = 3 * p.n_layer;
-  }
-  {
-    // every CTA streams a contiguous share of the LM head's rows
-    const int GV = (int)(p.head_npad / 4);
-    r.hd_g0 = (int)((int64_t)cta * GV / G);
-    r.hd_g1 = (int)((int64_t)(cta + 1) * GV / G);
     r.n_items = r.n_main + (p.with_head ? (r.hd_g1 - r.hd_g0 + kHeadChunkGroups - 1) / kHeadChunkGroups : 0);
   }
   const bool query = r.attn && !r.kv;
+  // ring bytes: the whole space after the activation region, except in query
+  // CTAs, whose K / V tiles and scores follow a ring of ring_attn bytes
+  const uint32_t R = query ? (uint32_t)p.ring_attn : (uint32_t)p.ring_gemv;
   const int KT = p.kv_tile, KP = D + 1;
   float* Ks = (float*)(ring + p.ring_attn);
   float* Vs = Ks + (size_t)KT * KP;
@@ -535,19 +250,11 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
   const int tr_attn = cta == 0 && tid == 0, tr_gemv = cta == p.n_attn && tid == 0;
 
   if (tid == 0) {
-    cs.p = p;
-    cs.r = r;
-    cs.L = L;
-    cs.n_past = n_past;
-    cs.dead = 0;
     for (int i = 0; i <= kQ; i++) mbar_init(&bars[i], 1);
     fence_mbar_init();
     rs->head = rs->tail = 0u;
     rs->next = rs->freed = 0;
-    // ring bytes: the whole space after the activation region, except in
-    // query CTAs, whose K / V tiles and scores follow a ring of ring_attn
-    // bytes until their last layer
-    rs->R = query ? (uint32_t)p.ring_attn : (uint32_t)p.ring_gemv;
+    s_dead = 0;
   }
   __syncthreads();
   // cluster phase: every CTA's barriers are initialized before any k/v CTA
@@ -555,48 +262,219 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
   cluster_arrive_relaxed();
   cluster_wait_acquire();
 
+  // ---- weight ring (thread 0) ----
+  const uint64_t wpol = l2_evict_first_policy();  // weights are read once per step
+  auto issue_more = [&]() {
+    fence_proxy_async_smem();
+    while (rs->next < r.n_items && rs->next - rs->freed < kQ) {
+      const ItemDesc d = item_desc(p, lay, r, rs->next);
+      const uint32_t bytes = item_bytes(d);
+      const uint32_t off0 = rs->head % R;
+      const uint32_t pad = off0 + bytes > R ? R - off0 : 0u;
+      if (rs->head + pad + bytes - rs->tail > R) break;
+      rs->head += pad;
+      const uint32_t off = rs->head % R;
+      const int slot = rs->next % kQ;
+      rs->off[slot] = off;
+      rs->end[slot] = rs->head + bytes;
+      uint32_t tx = 0;
+      for (int i = 0; i < d.n; i++)
+        tx += (uint32_t)(d.G[i] * 4 * d.K + d.G[i] * (d.K / 32) * 8);
+      mbar_arrive_expect_tx(&bars[slot], tx);
+      uint32_t o = off;
+      for (int i = 0; i < d.n; i++) {
+        if (d.G[i] > 0) {
+          const uint32_t qb = (uint32_t)(d.G[i] * 4 * d.K), db = (uint32_t)(d.G[i] * (d.K / 32) * 8);
+          bulk_load_hint(ring + o, d.w + (int64_t)d.g0[i] * 4 * d.K, qb, &bars[slot], wpol);
+          bulk_load_hint(ring + o + qb, d.w + d.npad * d.K + (int64_t)d.g0[i] * (d.K / 32) * 8, db, &bars[slot],
+                         wpol);
+        }
+        o += (uint32_t)groups_bytes(d.G[i], d.K);
+      }
+      rs->head += bytes;
+      rs->next++;
+    }
+  };
   // Waits for item `it` (every thread); returns its ring address.
   auto wait_item = [&](int it) -> const uint8_t* {
     const int slot = it % kQ;
-    if (!cs.dead && !mbar_wait_bounded(&bars[slot], (uint32_t)((it / kQ) & 1), p.err)) cs.dead = 1;
+    if (!s_dead && !mbar_wait_bounded(&bars[slot], (uint32_t)((it / kQ) & 1), p.err)) s_dead = 1;
     return ring + rs->off[slot];
   };
   // After every thread is done with item `it` (the caller has synchronized
-  // the CTA since its last read of it): frees it and issues more. After a
-  // time-out the CTA stops issuing and keeps the item unfreed, so the drain at
-  // the end of the kernel still waits (bounded) for its copies and no
-  // mbarrier is re-armed while a copy counted on it may be in flight.
+  // the CTA since its last read of it): frees it and issues more.
+  // After a time-out the CTA stops issuing and keeps the item unfreed, so the
+  // drain at the end of the kernel still waits (bounded) for its copies and
+  // no mbarrier is re-armed while a copy counted on it may be in flight.
   auto free_item = [&](int it) {
-    if (tid == 0 && !cs.dead) {
+    if (tid == 0 && !s_dead) {
       rs->tail = rs->end[it % kQ];
       rs->freed = it + 1;
-      ring_issue(&cs, smem);
+      issue_more();
     }
   };
-  if (tid == 0) ring_issue(&cs, smem);
+  if (tid == 0) issue_more();
 
-
-  // this lane's norm weights of blocks warp + u * kNW, loaded before a wait
-  auto nwl = [&](const float* norm_w, int u) {
-    return warp + u * kNW < nbE ? norm_w[(warp + u * kNW) * 32 + lane] : 0.0f;
+  // ---- hand-over counters ----
+  auto wait_ctr = [&](const unsigned long long* c, unsigned long long target) {
+    if (tid == 0 && !s_dead) {
+      uint32_t it = 0;
+      while (ld_acquire_u64(c) < target) {
+        if (++it >= kSpinLimit || ((it & 1023u) == 0 && *(volatile int32_t*)p.err != 0)) {
+          atomicExch(p.err, 5 /* MI_CUDA_ERR_TIMEOUT */);
+          s_dead = 1;
+          break;
+        }
+      }
+    }
+    __syncthreads();
+  };
+  auto signal_ctr = [&](unsigned long long* c) {
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      atomicAdd(c, 1ull);
+    }
   };
 
-  // tags: the embedding base, layer l's outputs base + l + 1 (words start
-  // zeroed and base >= 1, so a word never matches before its first store)
-  const uint32_t base = (uint32_t)(epoch * (unsigned long long)(p.n_layer + 1) + 1ull);
+  // ---- building blocks ----
+  // x (coherent loads from L2; or the embedding row) -> xs; rms_norm with
+  // norm_w; quantized into aq / ad (src/ops_cpu.cpp:154-160, 462-479).
+  // nw: this lane's norm weights of blocks warp + u * kNW (load_nw), loaded
+  // before the caller's wait so their latency overlaps it.
+  auto load_nw = [&](const float* norm_w, float (&nw)[4]) {
+#pragma unroll
+    for (int u = 0; u < 4; u++) nw[u] = warp + u * kNW < nbE ? norm_w[(warp + u * kNW) * 32 + lane] : 0.0f;
+  };
+  auto norm_quant = [&](const float* x, bool embed, const float (&nw)[4], float* x_out) {
+    if (embed) {
+      // mi_compute_get_rows on the Q8_0 embedding (ref src/ops_cpu.cpp:128-139)
+      int tok = n_past < p.tokens_len ? p.tokens[n_past] : -1;
+      if (tok < 0 || tok >= p.V) {
+        if (tid == 0) atomicExch(p.err, 1 /* MI_CUDA_ERR_ARG */);
+        tok = 0;
+      }
+      for (int k = tid; k < E; k += kNT) {
+        const float v = __fmul_rn((float)packed_qs(p.embed, E, tok, k >> 5)[k & 31],
+                                  packed_scale(p.embed, E, p.embed_npad, tok, k >> 5));
+        xs[k] = v;
+        if (x_out) x_out[k] = v;
+      }
+    } else {
+      for (int k = tid; k < E / 4; k += kNT) ((float4*)xs)[k] = __ldcg((const float4*)x + k);
+    }
+    __syncthreads();
+    for (int k = tid; k < E; k += kNT) sq[k] = __fmul_rn(xs[k], xs[k]);
+    __syncthreads();
+    const float ss = spec_ordered_sum<kNT, 2>(sq, E, smem + L.spec);
+    if (tid == 0) misc[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)E), p.eps)));
+    __syncthreads();
+    const float scale = misc[0];
+    // four blocks per warp at once overlap the quantizer's divisions
+    float v[4], d[4];
+    int8_t q[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int b = warp + u * kNW;
+      v[u] = b < nbE ? __fmul_rn(__fmul_rn(xs[b * 32 + lane], scale), nw[u]) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) q[u] = quantize_lane(v[u], &d[u]);
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int b = warp + u * kNW;
+      if (b < nbE) {
+        aq[b * 32 + lane] = q[u];
+        if (lane == 0) ad[b] = d[u];
+      }
+    }
+    __syncthreads();
+  };
+  // Q8_0_ACT blocks from global memory (coherent loads) into aq / ad.
+  auto load_act = [&](const uint8_t* g, int nb) {
+    const uint32_t* w = (const uint32_t*)g;
+    for (int e = tid; e < nb * 9; e += kNT) {
+      const uint32_t v = __ldcg(w + e);
+      const int b = e / 9, k = e - b * 9;
+      if (k == 0) ad[b] = __uint_as_float(v);
+      else ((uint32_t*)(aq + 32 * b))[k - 1] = v;
+    }
+    __syncthreads();
+  };
+  // Rows of an item, 2 threads per row (K of the activation region):
+  // res[4g + r] = dot(row, act), the AVX2 lane order.
+  auto rows_2t = [&](const uint8_t* base, const ItemDesc& d) {
+    const int K = (int)d.K, nb = K / 32, Gt = d.G[0] + (d.n > 1 ? d.G[1] : 0);
+    const int gw = lane >> 3, r4 = (lane >> 1) & 3, hh = lane & 1;
+    const uint4* aq16 = (const uint4*)aq;
+    for (int g0 = warp * 4; g0 < Gt; g0 += kNW * 4) {
+      const int g = g0 + gw;
+      const bool valid = g < Gt;
+      int gc = valid ? g : g0;
+      const uint8_t* rb = base;
+      int Gr = d.G[0];
+      if (gc >= d.G[0]) {
+        rb = base + groups_bytes(d.G[0], d.K);
+        gc -= d.G[0];
+        Gr = d.G[1];
+      }
+      const uint4* gq = (const uint4*)(rb + (size_t)gc * 4 * K);
+      const __half* gd = (const __half*)(rb + (size_t)Gr * 4 * K) + (size_t)gc * nb * 4;
+      float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll 2
+      for (int i = 0; i < nb; i++) {
+        const uint4 w = gq[i * 8 + (lane & 7)];
+        const uint4 a = aq16[i * 2 + hh];
+        const float dxdy = __fmul_rn(__half2float(gd[i * 4 + r4]), ad[i]);
+        a0 = __fmaf_rn(__int2float_rn(__dp4a((int)w.x, (int)a.x, 0)), dxdy, a0);
+        a1 = __fmaf_rn(__int2float_rn(__dp4a((int)w.y, (int)a.y, 0)), dxdy, a1);
+        a2 = __fmaf_rn(__int2float_rn(__dp4a((int)w.z, (int)a.z, 0)), dxdy, a2);
+        a3 = __fmaf_rn(__int2float_rn(__dp4a((int)w.w, (int)a.w, 0)), dxdy, a3);
+      }
+      // hsum ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7))
+      const float s0 = __fadd_rn(a0, __shfl_xor_sync(FULL, a0, 1));
+      const float s1 = __fadd_rn(a1, __shfl_xor_sync(FULL, a1, 1));
+      const float s2 = __fadd_rn(a2, __shfl_xor_sync(FULL, a2, 1));
+      const float s3 = __fadd_rn(a3, __shfl_xor_sync(FULL, a3, 1));
+      if (valid && hh == 0) res[g * 4 + r4] = __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+    }
+    __syncthreads();
+  };
+  // Rows of an item with long rows, 8 threads per row (one AVX2 lane each; a
+  // warp per group of 4 rows).
+  auto rows_8t = [&](const uint8_t* base, const ItemDesc& d) {
+    const int K = (int)d.K, nb = K / 32, Gt = d.G[0];
+    const int rr = lane >> 3, j = lane & 7;
+    for (int g = warp; g < Gt; g += kNW) {
+      const uint32_t* gq = (const uint32_t*)(base + (size_t)g * 4 * K);
+      const __half* gd = (const __half*)(base + (size_t)Gt * 4 * K) + (size_t)g * nb * 4;
+      const float acc = lane_chain(0.0f, gq, gd, (const int*)aq, ad, nb, lane, j, rr);
+      const float s4 = __fadd_rn(acc, __shfl_xor_sync(FULL, acc, 4));
+      const float s1 = __fadd_rn(s4, __shfl_xor_sync(FULL, s4, 1));
+      const float s2 = __fadd_rn(s1, __shfl_xor_sync(FULL, s1, 2));
+      if (j == 0) res[g * 4 + rr] = s2;
+    }
+    __syncthreads();
+  };
+
+  unsigned long long* const ctr = p.ctr;
+  const unsigned long long tH = (epoch + 1ull) * (unsigned long long)p.H;
+  const unsigned long long tW = (epoch + 1ull) * (unsigned long long)W;
 
   if (r.attn) {
     // ===================== attention CTAs =====================
-    const int half = D / 2;
+    const float* bias_base = nullptr;
     for (int l = 0; l < p.n_layer; l++) {
       const PersistLayer& Ly = lay[l];
       float* cache_k = p.cache + (size_t)l * 2 * p.n_ctx * HKV * D;
       float* cache_v = cache_k + (size_t)p.n_ctx * HKV * D;
       const float* kbase = cache_k + (size_t)r.kvh * D;
       const float* vbase = cache_v + (size_t)r.kvh * D;
-      if (tr_attn) pstamp(p, l, 0);
+      const size_t rsd = (size_t)HKV * D;
+      if (tr_attn) pstamp(p, 2 * l, 0);
       // operands that do not depend on this step's previous phases
-      const float* bias_base = Ly.bqkv + (r.kv ? E + r.kvh * D : r.h * D);
+      bias_base = Ly.bqkv + (r.kv ? E + r.kvh * D : r.h * D);
+      const int half = D / 2;
       float2 rc = make_float2(0.0f, 0.0f);
       float b_lo = 0.0f, b_hi = 0.0f, b_v = 0.0f;
       if (tid < half) {
@@ -605,23 +483,54 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         b_hi = bias_base[tid + half];
       }
       if (r.kv && tid < D) b_v = Ly.bqkv[E + HKV * D + r.kvh * D + tid];
+      // cached K / V rows [c0, c0 + rows) into the tiles (position n_past,
+      // this step's, comes from kr / vr)
+      // (with_k / with_v: which of the two tiles to fill)
+      auto load_kv = [&](int c0, int rows, bool with_k, bool with_v) {
+        const int D4 = D / 4, total = rows * D4;
+        for (int e0 = tid; e0 < total; e0 += 4 * kNT) {
+          float4 vk[4], vv[4];
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            const int e = e0 + u * kNT, rw = e / D4, c = e - rw * D4;
+            if (e < total && c0 + rw != n_past) {
+              if (with_k) vk[u] = __ldcg((const float4*)(kbase + (size_t)(c0 + rw) * rsd) + c);
+              if (with_v) vv[u] = __ldcg((const float4*)(vbase + (size_t)(c0 + rw) * rsd) + c);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            const int e = e0 + u * kNT, rw = e / D4, c = e - rw * D4;
+            if (e < total && c0 + rw != n_past) {
+              if (with_k) {
+                float* dk = Ks + (size_t)rw * KP + c * 4;
+                dk[0] = vk[u].x;
+                dk[1] = vk[u].y;
+                dk[2] = vk[u].z;
+                dk[3] = vk[u].w;
+              }
+              if (with_v) *(float4*)(Vs + (size_t)rw * D + c * 4) = vv[u];
+            }
+          }
+        }
+      };
       if (query) {
         if (tid == 0) mbar_arrive_expect_tx(bar_kv, (uint32_t)(2 * D * 4));
-        load_kv(kbase, vbase, HKV * D, 0, min(KT, n_kv), n_past, D, Ks, Vs, 1, 1);
+        load_kv(0, min(KT, n_kv), true, true);
       }
-      const float n0 = nwl(Ly.attn_norm, 0), n1 = nwl(Ly.attn_norm, 1), n2 = nwl(Ly.attn_norm, 2),
-                  n3 = nwl(Ly.attn_norm, 3);
+      float nw[4];
+      load_nw(Ly.attn_norm, nw);
       // ---- x of this layer: the embedding (layer 0) or the down output ----
-      if (tr_attn) pstamp(p, l, 1);
-      norm_quant(&cs, smem, p.xw, base + (uint32_t)l, l == 0, n0, n1, n2, n3, l == 0 && cta == 0 ? p.xw : nullptr,
-                 tr_attn ? l : -1, 2);
+      if (l > 0) wait_ctr(&ctr[(size_t)(l - 1) * 4 + 3], tW);
+      if (tr_attn) pstamp(p, 2 * l, 1);
+      norm_quant(p.x, l == 0, nw, l == 0 && cta == 0 ? p.x : nullptr);
+      if (tr_attn) pstamp(p, 2 * l, 2);
       // ---- the CTA's q rows, or k and v rows ----
       const ItemDesc d = item_desc(p, lay, r, l);
       const uint8_t* wbase = wait_item(l);
-      if (tr_attn) pstamp(p, l, 5);
-      rows_2t(smem, &cs, wbase, d.G[0], d.n > 1 ? d.G[1] : 0, E);  // ends with a CTA barrier
+      rows_2t(wbase, d);  // ends with a CTA barrier: the item may be reused
       free_item(l);
-      if (tr_attn) pstamp(p, l, 6);
+      if (tr_attn) pstamp(p, 2 * l, 3);
       // ---- bias, RoPE (ref src/ops_cpu.cpp:286-297), v ----
       if (tid < half) {
         const float a0 = __fadd_rn(res[tid], b_lo), a1 = __fadd_rn(res[tid + half], b_hi);
@@ -631,11 +540,10 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       }
       if (r.kv && tid < D) vr[tid] = __fadd_rn(res[D + tid], b_v);
       __syncthreads();
-      if (tr_attn) pstamp(p, l, 7);
       if (r.kv) {
         // k / v into every query CTA of the cluster (st.async, counted on the
         // receiver's bar_kv), then the KV-cache append
-        if (!cs.dead) {
+        if (!s_dead) {
           const int per = D >> 1;
           for (int e = tid; e < n_rep * per; e += kNT) {
             const int c = e / per, i4 = e - c * per;
@@ -651,13 +559,13 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         continue;
       }
       // ---- query CTA: the decode attention of head h ----
-      if (!cs.dead && !mbar_wait_bounded(bar_kv, (uint32_t)(l & 1), p.err)) cs.dead = 1;
+      if (!s_dead && !mbar_wait_bounded(bar_kv, (uint32_t)(l & 1), p.err)) s_dead = 1;
       if (n_past < KT && tid < D) {
         Ks[(size_t)n_past * KP + tid] = kr[tid];
         Vs[(size_t)n_past * D + tid] = vr[tid];
       }
       __syncthreads();
-      if (tr_attn) pstamp(p, l, 8);
+      if (tr_attn) pstamp(p, 2 * l, 4);
       float* sc = p.scores_in_smem ? scs : p.scores + (size_t)r.h * p.n_ctx;
       const int n_chunks = (n_kv + KT - 1) / KT;
       float lmax = -INFINITY;
@@ -665,7 +573,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         const int c0 = c * KT, rows = min(KT, n_kv - c0);
         if (c > 0) {
           __syncthreads();
-          load_kv(kbase, vbase, HKV * D, c0, rows, n_past, D, Ks, Vs, 1, 0);  // V keeps chunk 0
+          load_kv(c0, rows, true, false);  // the V tile keeps chunk 0 for the value sums
           if (n_past >= c0 && n_past < c0 + rows)
             for (int i = tid; i < D; i += kNT) Ks[(size_t)(n_past - c0) * KP + i] = kr[i];
           __syncthreads();
@@ -677,173 +585,167 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
           lmax = fmaxf(lmax, v);
         }
       }
-      if (tr_attn) pstamp(p, l, 9);
       lmax = warp_max(lmax);
       if (lane == 0) red_f[warp] = lmax;
       __syncthreads();
       float mx = red_f[0];
       for (int w = 1; w < kNW; w++) mx = fmaxf(mx, red_f[w]);
-      if (tr_attn) pstamp(p, l, 10);
       for (int i = tid; i < n_kv; i += kNT) sc[i] = expf_exact(__fsub_rn(sc[i], mx), p.et);
       __syncthreads();
-      if (tr_attn) pstamp(p, l, 11);
+      if (tr_attn) pstamp(p, 2 * l, 5);
       // the softmax denominator: one ordered chain (src/ops_cpu.cpp:331-336)
       if (tid == 0) {
         float sum = 0.0f;
         if (p.scores_in_smem) {
           sum = ordered_sum_smem(sc, n_kv);
         } else {
+#pragma unroll 8
           for (int i = 0; i < n_kv; i++) sum = __fadd_rn(sum, sc[i]);
         }
         misc[1] = __fdiv_rn(1.0f, sum);
       }
       __syncthreads();
       const float inv = misc[1];
-      if (tr_attn) pstamp(p, l, 12);
-      // out[o] = sum_t V[o, kvh, t] * P[t], t ascending (src/ops_cpu.cpp:402-406)
+      if (tr_attn) pstamp(p, 2 * l, 6);
+      // out[o] = sum_t V[o, kvh, t] * P[t], t ascending (src/ops_cpu.cpp:402-406);
+      // the K / V tiles of the next layer replace these only after this loop
       float acc = 0.0f;
       for (int c = 0; c < n_chunks; c++) {
         const int c0 = c * KT, rows = min(KT, n_kv - c0);
         if (c > 0) {
           __syncthreads();
-          load_kv(kbase, vbase, HKV * D, c0, rows, n_past, D, Ks, Vs, 0, 1);
+          load_kv(c0, rows, false, true);
           if (n_past >= c0 && n_past < c0 + rows)
             for (int i = tid; i < D; i += kNT) Vs[(size_t)(n_past - c0) * D + i] = vr[i];
           __syncthreads();
         }
         if (tid < D) acc = ordered_dot_scaled(acc, Vs + tid, D, sc + c0, inv, rows);
       }
-      if (tr_attn) pstamp(p, l, 13);
       // the O projection's quantize node (src/ops_cpu.cpp:462-479) for this
       // head's outputs: warp w holds block h*D/32 + w
       if (tid < D) {
         float dq;
         const int8_t q = quantize_lane(acc, &dq);
-        put_block(p.attw + ((size_t)r.h * (D / 32) + (tid >> 5)) * 9, q, dq, base + (uint32_t)l + 1u);
+        uint8_t* blk = p.attn_q + ((size_t)r.h * (D / 32) + (tid >> 5)) * 36;
+        ((int8_t*)blk)[4 + lane] = q;
+        if (lane == 0) *(float*)blk = dq;
       }
-      if (tr_attn) pstamp(p, l, 14);
-      __syncthreads();  // the tiles and scores are reused by the next layer
-      if (tr_attn) pstamp(p, l, 15);
+      signal_ctr(&ctr[(size_t)l * 4 + 0]);
+      if (tr_attn) pstamp(p, 2 * l, 7);
     }
   } else {
     // ===================== projection CTAs =====================
-    // Rows [4 o_g0, 4 o_g1) of the O and down projections are this CTA's in
-    // every layer, so the residual each of them adds is the row this CTA
-    // stored one phase earlier (kept in xloc / x2loc), except the embedding
-    // rows that layer 0's O adds.
-    const int rows_o = 4 * (r.o_g1 - r.o_g0), r0 = 4 * r.o_g0;
-    constexpr int tb = 16;  // projection stamps are points 16..31 of a layer
     for (int l = 0; l < p.n_layer; l++) {
       const PersistLayer& Ly = lay[l];
-      const uint32_t tag = base + (uint32_t)l + 1u;
       // ---- O projection + residual: x2 = x + W_o . attn ----
-      if (tr_gemv) pstamp(p, l, tb + 0);
-      if (l == 0) poll_words(&cs, p.xw + r0, rows_o, base, 0, xloc, nullptr, nullptr);
-      load_act(smem, &cs, p.attw, nbE, tag);
-      if (tr_gemv) pstamp(p, l, tb + 1);
-      const uint8_t* wb = wait_item(3 * l);
-      if (tr_gemv) pstamp(p, l, tb + 2);
-      if (rows_o > 0) rows_2t(smem, &cs, wb, rows_o / 4, 0, E);
-      if (tr_gemv) pstamp(p, l, tb + 3);
-      for (int i = tid; i < rows_o; i += kNT) {
-        const float v = __fadd_rn(xloc[i], res[i]);
-        x2loc[i] = v;
-        ll_store(p.x2w + r0 + i, __float_as_uint(v), tag);
-      }
-      free_item(3 * l);  // rows_2t ended with a CTA barrier
-      if (tr_gemv) pstamp(p, l, tb + 4);
-      // ---- gate/up: rms_norm(x2) * ffn_norm, quantize; silu(gate) * up, quantize ----
-      const int nblk = r.gu_b1 - r.gu_b0;
       {
-        const float n0 = nwl(Ly.ffn_norm, 0), n1 = nwl(Ly.ffn_norm, 1), n2 = nwl(Ly.ffn_norm, 2),
-                    n3 = nwl(Ly.ffn_norm, 3);
-        if (tr_gemv) pstamp(p, l, tb + 5);
-        norm_quant(&cs, smem, p.x2w, tag, 0, n0, n1, n2, n3, nullptr, tr_gemv ? l : -1, tb + 6);
+        const ItemDesc d = item_desc(p, lay, r, 3 * l);
+        const int rows = 4 * d.G[0], r0 = 4 * d.g0[0];
+        wait_ctr(&ctr[(size_t)l * 4 + 0], tH);
+        if (tr_gemv) pstamp(p, 2 * l + 1, 0);
+        load_act(p.attn_q, nbE);
+        const uint8_t* wb = wait_item(3 * l);
+        if (rows > 0) rows_2t(wb, d);
+        for (int i = tid; i < rows; i += kNT) p.x2[r0 + i] = __fadd_rn(__ldcg(p.x + r0 + i), res[i]);
+        signal_ctr(&ctr[(size_t)l * 4 + 1]);
+        free_item(3 * l);
+        if (tr_gemv) pstamp(p, 2 * l + 1, 1);
       }
-      wb = wait_item(3 * l + 1);
-      if (nblk > 0) rows_2t(smem, &cs, wb, 16 * nblk, 0, E);
-      if (tr_gemv) pstamp(p, l, tb + 9);
-      // each 64 packed rows are the gate / up rows of one 32-element block:
-      // act[a] = silu(gate) * up, then the down projection's quantize node
-      for (int j = warp; j < nblk; j += kNW) {
-        const int a = 32 * j + lane;                  // element of the CTA's blocks
-        const int lr = (a >> 2) * 8 + (a & 3);        // its gate row, local
-        const float v = __fmul_rn(silu_exact(res[lr], p.et), res[lr + 4]);
-        float dq;
-        const int8_t q = quantize_lane(v, &dq);
-        put_block(p.actw + (size_t)(r.gu_b0 + j) * 9, q, dq, tag);
+      // ---- gate/up: rms_norm(x2) * ffn_norm, quantize; silu(gate) * up, quantize ----
+      {
+        const ItemDesc d = item_desc(p, lay, r, 3 * l + 1);
+        float nw[4];
+        load_nw(Ly.ffn_norm, nw);
+        wait_ctr(&ctr[(size_t)l * 4 + 1], tW);
+        if (tr_gemv) pstamp(p, 2 * l + 1, 2);
+        norm_quant(p.x2, false, nw, nullptr);
+        if (tr_gemv) pstamp(p, 2 * l + 1, 3);
+        const uint8_t* wb = wait_item(3 * l + 1);
+        if (d.G[0] > 0) rows_2t(wb, d);
+        // each 64 packed rows are the gate / up rows of one 32-element block:
+        // act[a] = silu(gate) * up, then the down projection's quantize node
+        for (int j = warp; j < r.gu_b1 - r.gu_b0; j += kNW) {
+          const int a = 32 * j + lane;                  // element of the CTA's blocks
+          const int lr = (a >> 2) * 8 + (a & 3);        // its gate row, local
+          const float v = __fmul_rn(silu_exact(res[lr], p.et), res[lr + 4]);
+          float dq;
+          const int8_t q = quantize_lane(v, &dq);
+          uint8_t* blk = p.act_q + (size_t)(r.gu_b0 + j) * 36;
+          ((int8_t*)blk)[4 + lane] = q;
+          if (lane == 0) *(float*)blk = dq;
+        }
+        signal_ctr(&ctr[(size_t)l * 4 + 2]);
+        free_item(3 * l + 1);
+        if (tr_gemv) pstamp(p, 2 * l + 1, 4);
       }
-      if (tr_gemv) pstamp(p, l, tb + 10);
-      __syncthreads();  // res is rewritten by the down rows
-      free_item(3 * l + 1);
-      if (tr_gemv) pstamp(p, l, tb + 11);
       // ---- down projection + residual: x = x2 + W_down . act ----
-      if (tr_gemv) pstamp(p, l, tb + 12);
-      load_act(smem, &cs, p.actw, nbF, tag);
-      wb = wait_item(3 * l + 2);
-      if (tr_gemv) pstamp(p, l, tb + 13);
-      if (rows_o > 0) rows_8t(smem, &cs, wb, rows_o / 4, FF);
-      if (tr_gemv) pstamp(p, l, tb + 14);
-      for (int i = tid; i < rows_o; i += kNT) {
-        const float v = __fadd_rn(x2loc[i], res[i]);
-        xloc[i] = v;
-        ll_store(p.xw + r0 + i, __float_as_uint(v), tag);
+      {
+        const ItemDesc d = item_desc(p, lay, r, 3 * l + 2);
+        const int rows = 4 * d.G[0], r0 = 4 * d.g0[0];
+        wait_ctr(&ctr[(size_t)l * 4 + 2], tW);
+        if (tr_gemv) pstamp(p, 2 * l + 1, 5);
+        load_act(p.act_q, nbF);
+        const uint8_t* wb = wait_item(3 * l + 2);
+        if (rows > 0) rows_8t(wb, d);
+        for (int i = tid; i < rows; i += kNT) p.x[r0 + i] = __fadd_rn(__ldcg(p.x2 + r0 + i), res[i]);
+        signal_ctr(&ctr[(size_t)l * 4 + 3]);
+        free_item(3 * l + 2);
+        if (tr_gemv) pstamp(p, 2 * l + 1, 6);
       }
-      free_item(3 * l + 2);  // rows_8t ended with a CTA barrier
-      if (tr_gemv) pstamp(p, l, tb + 15);
     }
-  }
-  // ---- LM head (every CTA, its own rows): rms_norm(x) * output_norm,
-  // quantize; logits; the CTA's first maximum ----
-  if (p.with_head) {
-    const float n0 = nwl(p.out_norm, 0), n1 = nwl(p.out_norm, 1), n2 = nwl(p.out_norm, 2), n3 = nwl(p.out_norm, 3);
-    if (tr_gemv) pstamp(p, p.n_layer, 0);
-    norm_quant(&cs, smem, p.xw, base + (uint32_t)p.n_layer, 0, n0, n1, n2, n3, nullptr, -1, 0);
-    if (tr_gemv) pstamp(p, p.n_layer, 1);
-    float bv = -INFINITY;
-    int32_t bi = 0x7fffffff;
-    for (int it = r.n_main; it < r.n_items; it++) {
-      const ItemDesc d = item_desc(p, lay, r, it);
-      const uint8_t* wb = wait_item(it);
-      rows_2t(smem, &cs, wb, d.G[0], 0, E);  // ends with a CTA barrier: the item may be reused
-      free_item(it);
-      const int hr0 = 4 * d.g0[0];
-      for (int i = tid; i < 4 * d.G[0]; i += kNT) {
-        const int row = hr0 + i;
-        if (row >= p.V) continue;
-        const float v = res[i];
-        p.logits[row] = v;
-        if (v > bv || bi == 0x7fffffff) {  // rows ascend per thread: first maximum
-          bv = v;
-          bi = row;
+    // ---- LM head: rms_norm(x) * output_norm, quantize; logits; argmax ----
+    if (p.with_head) {
+      float nw[4];
+      load_nw(p.out_norm, nw);
+      wait_ctr(&ctr[(size_t)(p.n_layer - 1) * 4 + 3], tW);
+      if (tr_gemv) pstamp(p, 2 * p.n_layer, 0);
+      norm_quant(p.x, false, nw, nullptr);
+      if (tr_gemv) pstamp(p, 2 * p.n_layer, 1);
+      float bv = -INFINITY;
+      int32_t bi = 0x7fffffff;
+      for (int it = r.n_main; it < r.n_items; it++) {
+        const ItemDesc d = item_desc(p, lay, r, it);
+        const uint8_t* wb = wait_item(it);
+        rows_2t(wb, d);  // ends with a CTA barrier: the item may be reused
+        free_item(it);
+        const int r0 = 4 * d.g0[0];
+        for (int i = tid; i < 4 * d.G[0]; i += kNT) {
+          const int row = r0 + i;
+          if (row >= p.V) continue;
+          const float v = res[i];
+          p.logits[row] = v;
+          if (v > bv || bi == 0x7fffffff) {  // rows ascend per thread: first maximum
+            bv = v;
+            bi = row;
+          }
         }
+        __syncthreads();  // res is rewritten by the next chunk
       }
-      __syncthreads();  // res is rewritten by the next chunk
-    }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(FULL, bv, o);
-      const int32_t oi = __shfl_xor_sync(FULL, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    if (lane == 0) {
-      red_f[warp] = bv;
-      red_i[warp] = bi;
-    }
-    __syncthreads();
-    if (tid == 0) {
-      for (int w = 1; w < kNW; w++)
-        if (red_f[w] > bv || (red_f[w] == bv && red_i[w] < bi)) {
-          bv = red_f[w];
-          bi = red_i[w];
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(FULL, bv, o);
+        const int32_t oi = __shfl_xor_sync(FULL, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+          bv = ov;
+          bi = oi;
         }
-      p.part_val[cta] = bv;
-      p.part_idx[cta] = bi;
+      }
+      if (lane == 0) {
+        red_f[warp] = bv;
+        red_i[warp] = bi;
+      }
+      __syncthreads();
+      if (tid == 0) {
+        for (int w = 1; w < kNW; w++)
+          if (red_f[w] > bv || (red_f[w] == bv && red_i[w] < bi)) {
+            bv = red_f[w];
+            bi = red_i[w];
+          }
+        p.part_val[cta - p.n_attn] = bv;
+        p.part_idx[cta - p.n_attn] = bi;
+      }
+      if (tr_gemv) pstamp(p, 2 * p.n_layer, 2);
     }
-    if (tr_gemv) pstamp(p, p.n_layer, 2);
   }
 
   // ---- close the step: the last CTA to finish advances the state ----
@@ -860,10 +762,10 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
   if (s_ticket == (uint32_t)G - 1 && tid == 0) {
     __threadfence();
     if (p.with_head) {
-      // the first maximum over the CTAs, whose row ranges ascend
+      // the first maximum over the projection CTAs, whose row ranges ascend
       float best = __ldcg(&p.part_val[0]);
       int32_t besti = __ldcg(&p.part_idx[0]);
-      for (int c = 1; c < G; c++) {
+      for (int c = 1; c < W; c++) {
         const float v = __ldcg(&p.part_val[c]);
         const int32_t i = __ldcg(&p.part_idx[c]);
         if (v > best || (v == best && i < besti)) {
@@ -877,7 +779,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
     *p.pos = n_past + 1;
     *p.epoch = epoch + 1ull;
     *p.ticket = 0u;
-    if (tr_gemv || tr_attn) pstamp(p, p.n_layer, 3);
+    if (tr_gemv || tr_attn) pstamp(p, 2 * p.n_layer, 3);
   }
   // peers may still store into this CTA's shared memory (k / v hand-over)
   // until every CTA of the cluster is here

@@ -101,6 +101,7 @@ __global__ void __launch_bounds__(NT, 2) gemv_q8_kernel(const GemvParams p) {
   const uint8_t* wq = p.w;
   const uint8_t* wd = p.w + p.n_pad * K;
 
+  const uint64_t wpol = l2_evict_first_policy();  // weights are read once per step
   auto issue = [&](int t) {
     const int s = t % p.n_stages;
     const int pass = n_chunks == 1 ? t : t / n_chunks, ch = t - pass * n_chunks;
@@ -110,8 +111,8 @@ __global__ void __launch_bounds__(NT, 2) gemv_q8_kernel(const GemvParams p) {
     if (n_chunks == 1) {
       const uint32_t qb = (uint32_t)(rows * K), db = (uint32_t)(rows * nb * 2);
       mbar_arrive_expect_tx(&bars[s], qb + db);
-      bulk_load(st, wq + tr0 * K, qb, &bars[s]);
-      bulk_load(st + (size_t)p.stage_rows * K, wd + tr0 * nb * 2, db, &bars[s]);
+      bulk_load_hint(st, wq + tr0 * K, qb, &bars[s], wpol);
+      bulk_load_hint(st + (size_t)p.stage_rows * K, wd + tr0 * nb * 2, db, &bars[s], wpol);
     } else {
       // blocks [c0, c0 + kcb) of each 4-row group: 128 B of quants and 8 B of
       // scales per block, contiguous in the packed layout (nb and kc even keep
@@ -122,8 +123,8 @@ __global__ void __launch_bounds__(NT, 2) gemv_q8_kernel(const GemvParams p) {
       const int64_t g0 = tr0 >> 2;
       uint8_t* sdst = st + (size_t)p.stage_rows * 32 * kc;
       for (int g = 0; g < ng; g++) {
-        bulk_load(st + (size_t)g * 128 * kc, wq + (g0 + g) * 4 * K + (int64_t)c0 * 128, qb, &bars[s]);
-        bulk_load(sdst + (size_t)g * 8 * kc, wd + ((g0 + g) * nb + c0) * 8, db, &bars[s]);
+        bulk_load_hint(st + (size_t)g * 128 * kc, wq + (g0 + g) * 4 * K + (int64_t)c0 * 128, qb, &bars[s], wpol);
+        bulk_load_hint(sdst + (size_t)g * 8 * kc, wd + ((g0 + g) * nb + c0) * 8, db, &bars[s], wpol);
       }
     }
   };
@@ -145,8 +146,8 @@ __global__ void __launch_bounds__(NT, 2) gemv_q8_kernel(const GemvParams p) {
     const int c0 = ch * kc, kcb = min(kc, nb - c0);
     uint8_t* st = wring + (size_t)s * L.stage_bytes;
     mbar_arrive_expect_tx(&wbars[s], 136u * (uint32_t)kcb);
-    bulk_load(st, wq + G * 4 * K + (int64_t)c0 * 128, 128u * (uint32_t)kcb, &wbars[s]);
-    bulk_load(st + (size_t)128 * kc, wd + (G * nb + c0) * 8, 8u * (uint32_t)kcb, &wbars[s]);
+    bulk_load_hint(st, wq + G * 4 * K + (int64_t)c0 * 128, 128u * (uint32_t)kcb, &wbars[s], wpol);
+    bulk_load_hint(st + (size_t)128 * kc, wd + (G * nb + c0) * 8, 8u * (uint32_t)kcb, &wbars[s], wpol);
   };
 
   trace_mark(p.trace, p.trace_slot, 0);

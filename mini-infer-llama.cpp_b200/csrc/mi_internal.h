@@ -212,8 +212,8 @@ cudaError_t prepare_qkv_attn_kernel(int optin);
 // ---------------------------------------------------------------------------
 // Persistent decode step (decode_persist.cu): one launch per decode step on
 // one GPU. CTAs stay resident for the whole step; phases hand over through
-// tagged words in device memory instead of kernel boundaries, and every CTA
-// streams the weights of its coming work items into a shared-memory ring.
+// device counters instead of kernel boundaries, and every CTA streams the
+// weights of its coming work items into a shared-memory ring a layer ahead.
 // ---------------------------------------------------------------------------
 struct PersistLayer {
   const uint8_t* qkv;     // packed Q | K | V rows, n_pad qkv_npad
@@ -236,13 +236,10 @@ struct PersistParams {
   const float* out_norm;
   float* cache;                // [layer][k|v][n_ctx][HKV][D]
   const float2* rope;          // [pos][D/2]
-  // Hand-over buffers of 8-byte words, value bits | tag << 32, each written
-  // with one 64-bit store; a consumer polls a word until it carries the tag
-  // of the current step and layer (no separate flag or fence).
-  uint64_t* xw;                // residual stream x (E words: embedding, down outputs)
-  uint64_t* x2w;               // residual stream after attention (E words)
-  uint64_t* attw;              // the O projection's Q8_0_ACT input, 9 words a block
-  uint64_t* actw;              // the down projection's Q8_0_ACT input, 9 words a block
+  float* x;                    // residual stream (layer input / down output)
+  float* x2;                   // residual stream after attention
+  uint8_t* attn_q;             // Q8_0_ACT: the O projection's input
+  uint8_t* act_q;              // Q8_0_ACT: the down projection's input
   float* logits;
   float* scores;               // [H][n_ctx] when the scores do not fit on chip
   float* part_val;             // per-CTA LM-head winners
@@ -255,7 +252,8 @@ struct PersistParams {
   const int32_t* feedback;
   int32_t* err;
   uint32_t* ticket;            // CTAs finished with the step (the last one closes it)
-  unsigned long long* epoch;   // steps completed since the hand-over words were zeroed
+  unsigned long long* epoch;   // steps completed since the counters were zeroed
+  unsigned long long* ctr;     // [n_layer][4] hand-over counters
   // schedule: CTAs [0, n_attn) run the attention of one head (clusters of
   // n_rep + 1: n_rep query heads and one k/v CTA), the other n_gemv CTAs the
   // O, gate/up and down projections; all of them share the LM head

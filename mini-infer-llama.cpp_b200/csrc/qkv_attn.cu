@@ -144,14 +144,15 @@ __global__ void __launch_bounds__(kNT, 1) qkv_attn_kernel(const QkvAttnParams p)
     // r * nb * 2 bytes into the scale plane
     const uint32_t qb = (uint32_t)((int64_t)D * K), db = (uint32_t)(D * nb * 2);
     const uint8_t* wd = p.w + p.n_pad * K;
+    const uint64_t wpol = l2_evict_first_policy();  // weights are read once per step
     mbar_arrive_expect_tx(bar, (kv_cta ? 2u : 1u) * (qb + db));
     const int64_t ra = kv_cta ? E + (int64_t)kvh * D : (int64_t)h * D;
-    bulk_load(smem + L.wa, p.w + ra * K, qb, bar);
-    bulk_load(smem + L.wa + (size_t)D * K, wd + ra * nb * 2, db, bar);
+    bulk_load_hint(smem + L.wa, p.w + ra * K, qb, bar, wpol);
+    bulk_load_hint(smem + L.wa + (size_t)D * K, wd + ra * nb * 2, db, bar, wpol);
     if (kv_cta) {
       const int64_t rb = E + (int64_t)HKV * D + (int64_t)kvh * D;
-      bulk_load(smem + L.wb, p.w + rb * K, qb, bar);
-      bulk_load(smem + L.wb + (size_t)D * K, wd + rb * nb * 2, db, bar);
+      bulk_load_hint(smem + L.wb, p.w + rb * K, qb, bar, wpol);
+      bulk_load_hint(smem + L.wb + (size_t)D * K, wd + rb * nb * 2, db, bar, wpol);
     }
   }
   // The weights' other operands, into registers: rms_norm weights of this

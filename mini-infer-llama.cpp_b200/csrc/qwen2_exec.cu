@@ -149,8 +149,7 @@ struct mi_cuda_kv_cache {
   // layers' weight pointers.
   PersistPlan plan_persist{};
   bool persist = false;
-  unsigned long long* pctr = nullptr;  // epoch | ticket, then the hand-over words
-  size_t pctr_words = 0;
+  unsigned long long* pctr = nullptr;  // [n_layer][4] | epoch | ticket
   PersistLayer* d_layers = nullptr;
   cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
   // Batched-prefill workspace, allocated on first use and grown to the largest
@@ -522,10 +521,10 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     q.out_norm = m->output_norm;
     q.cache = kv->cache;
     q.rope = kv->rope;
-    q.xw = (uint64_t*)kv->pctr + 2;
-    q.x2w = q.xw + E;
-    q.attw = q.x2w + E;
-    q.actw = q.attw + (E / 32) * 9;
+    q.x = kv->x;
+    q.x2 = kv->x2;
+    q.attn_q = kv->attn_q;
+    q.act_q = kv->act_q;
     q.logits = kv->logits;
     q.scores = kv->scores;
     q.part_val = kv->part_val;
@@ -537,8 +536,9 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     q.next_token = &kv->state->next_token;
     q.feedback = &kv->state->feedback;
     q.err = err;
-    q.epoch = kv->pctr;
-    q.ticket = (uint32_t*)(kv->pctr + 1);
+    q.ctr = kv->pctr;
+    q.epoch = kv->pctr + (size_t)hp.n_layer * 4;
+    q.ticket = (uint32_t*)(kv->pctr + (size_t)hp.n_layer * 4 + 1);
     q.et = et;
     q.trace = kv->trace;
     CK(launch_persist(q, kv->plan_persist, kv->stream));
@@ -1104,11 +1104,11 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
     }
   }
 
-  // The persistent one-kernel step where the shape fits it (one GPU), with
-  // MI_CUDA_PERSIST=1; otherwise the kernel-per-phase graph.
+  // The persistent one-kernel step where the shape fits it (one GPU);
+  // MI_CUDA_PERSIST=0 keeps the kernel-per-phase graph (for comparisons).
   if (m->world == 1) {
     const char* pe = std::getenv("MI_CUDA_PERSIST");
-    if (pe && std::atoi(pe) != 0) {
+    if (!(pe && std::atoi(pe) == 0)) {
       kv->plan_persist = plan_persist(E, (int32_t)D, hp.n_head, hp.n_head_kv, FF, hp.n_vocab, hp.n_layer, n_ctx,
                                       sms);
       kv->persist = kv->plan_persist.ok;
@@ -1130,9 +1130,8 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
                o_pi = slot(1024 * 4), o_tok = slot((size_t)(n_ctx + 1) * 4),
                o_state = slot(sizeof(StepState)), o_attnq = slot(E / 32 * 36),
                o_actq = slot(FF / 32 * 36),
-               o_trace = slot((size_t)std::max(6 * hp.n_layer + 1, 4 * hp.n_layer + 4) * kTraceStamps * 8),
-               o_epoch = slot(4),
-               o_pctr = slot((2 + 2 * (size_t)E + (size_t)(E / 32 + FF / 32) * 9) * 8),
+               o_trace = slot((size_t)(6 * hp.n_layer + 1) * kTraceStamps * 8), o_epoch = slot(4),
+               o_pctr = slot(((size_t)hp.n_layer * 4 + 2) * 8),
                o_play = slot((size_t)hp.n_layer * sizeof(PersistLayer));
   CK(cudaMalloc(&kv->buf, off));
   CK(cudaMemset(kv->buf, 0, off));
@@ -1154,10 +1153,9 @@ int mi_cuda_kv_cache_init(mi_cuda_model* m, int32_t n_ctx, mi_cuda_kv_cache** ou
   kv->trace = (uint64_t*)(kv->buf + o_trace);
   // one slot per kernel of a step; the fused QKV + attention kernel adds two
   // detail slots per layer after the step's slots
-  kv->trace_slots = kv->persist ? 4 * hp.n_layer + 4 : 6 * hp.n_layer + 1;
+  kv->trace_slots = kv->persist ? 2 * hp.n_layer + 1 : 6 * hp.n_layer + 1;
   kv->epoch = (uint32_t*)(kv->buf + o_epoch);
   kv->pctr = (unsigned long long*)(kv->buf + o_pctr);
-  kv->pctr_words = 2 + 2 * (size_t)E + (size_t)(E / 32 + FF / 32) * 9;
   kv->d_layers = (PersistLayer*)(kv->buf + o_play);
   {
     std::vector<PersistLayer> pl((size_t)hp.n_layer);
@@ -1303,9 +1301,9 @@ int mi_cuda_qwen2_set_position(mi_cuda_kv_cache* kv, const int32_t* h_tokens, in
   kv->h_state->pos = pos;
   kv->h_state->feedback = 1;
   CK(cudaMemcpyAsync(kv->state, kv->h_state, sizeof(StepState), cudaMemcpyHostToDevice, kv->stream));
-  // a fresh start for the persistent step: epoch 0, and no hand-over word
-  // carrying a tag the restarted epochs will use again
-  CK(cudaMemsetAsync(kv->pctr, 0, kv->pctr_words * 8, kv->stream));
+  // a fresh start for the persistent step's hand-over counters (a step that
+  // gave up part-way leaves them behind their targets)
+  CK(cudaMemsetAsync(kv->pctr, 0, ((size_t)kv->model->hp.n_layer * 4 + 2) * 8, kv->stream));
   return MI_CUDA_OK;
 }
 

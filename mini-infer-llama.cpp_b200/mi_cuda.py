@@ -436,15 +436,12 @@ class KVCache:
         step: one slot per kernel (first CTA): entry, predecessor done,
         prologue done, epilogue start, then the kernel's own phase marks
         (attention: scores, exp, sum, KV done). Persistent step (one kernel):
-        32 stamps (four slots) per layer -- 0-15 from attention CTA 0 (layer
-        start, x ready, x loaded, sum of squares, quantized, weights ready,
-        rows, bias + RoPE, k/v received, scores, max, exp, sum, values,
-        quantized, signalled), 16-31 from the first projection CTA (O: wait
-        done, input loaded, weights ready, rows, signalled; gate/up: wait done,
-        x2 loaded, sum of squares, quantized, rows, SiLU + quantize,
-        signalled; down: wait done, input + weights ready, rows, signalled) --
-        then the LM head's (wait done, prologue done, rows done, step closed)."""
-        n = max(6 * self.model.hparams.n_layer + 1, 4 * self.model.hparams.n_layer + 4)
+        two slots per layer -- attention CTA 0 (layer start, x ready, prologue
+        done, rows done, k/v received, exp done, sum done, head signalled) and
+        the first projection CTA (O wait done, O signalled, gate/up wait done,
+        its prologue done, gate/up signalled, down wait done, down signalled)
+        -- then the LM head (wait done, prologue done, rows done, step closed)."""
+        n = 6 * self.model.hparams.n_layer + 1
         out = np.zeros((n, 8), dtype=np.uint64)
         got = C.c_int32()
         check(lib().mi_cuda_qwen2_step_trace(self.h, out.ctypes.data, n, C.byref(got)))

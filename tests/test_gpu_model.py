@@ -123,17 +123,16 @@ def test_step_trace(mc, model_path, qkv_attn_path):
     per = qkv_attn_path
     L = model.hparams.n_layer
     if per == 0:
-        # persistent step: per layer 16 stamps of attention CTA 0 and 16 of the
-        # first projection CTA, in phase order; then the LM head's
+        # persistent step: per layer the attention CTA's and the first
+        # projection CTA's phase stamps, then the LM head's
         assert kv.kernels_per_step == 1
-        assert t.shape == (4 * L + 4, 8)
-        st = t.reshape(L + 1, 32)
-        attn, proj, head = st[:L, :16], st[:L, 16:], st[L, :3]
-        assert np.all(attn > 0) and np.all(proj > 0) and np.all(head > 0)
-        assert np.all(np.diff(attn, axis=1) >= 0) and np.all(np.diff(proj, axis=1) >= 0)
-        assert np.all(proj[:, 1] >= attn[:, 13] - 2000)   # O's input arrives after the heads are done
-        assert np.all(attn[1:, 2] >= proj[:-1, 14] - 2000)  # x arrives after the previous layer's down rows
-        assert head[2] - attn[0, 0] < 10_000_000
+        assert t.shape == (2 * L + 1, 8)
+        attn, proj = t[0:2 * L:2], t[1:2 * L:2]
+        assert np.all(attn > 0) and np.all(proj[:, :7] > 0) and np.all(t[-1, :3] > 0)
+        assert np.all(np.diff(attn, axis=1) >= 0) and np.all(np.diff(proj[:, :7], axis=1) >= 0)
+        assert np.all(proj[:, 0] >= attn[:, 7] - 2000)   # O starts after the heads are done
+        assert np.all(attn[1:, 1] >= proj[:-1, 6] - 2000)  # a layer starts after the previous down
+        assert t[-1, 2] - attn[0, 0] < 10_000_000
     else:
         assert t.shape == (kv.kernels_per_step, 8) == (per * 4 + 1, 8)
         assert np.all(t[:, :4] > 0)
