@@ -441,7 +441,7 @@ class KVCache:
         the first projection CTA (O wait done, O signalled, gate/up wait done,
         its prologue done, gate/up signalled, down wait done, down signalled)
         -- then the LM head (wait done, prologue done, rows done, step closed)."""
-        n = 6 * self.model.hparams.n_layer + 1
+        n = self.kernels_per_step if self.kernels_per_step > 1 else 2 * self.model.hparams.n_layer + 1
         out = np.zeros((n, 8), dtype=np.uint64)
         got = C.c_int32()
         check(lib().mi_cuda_qwen2_step_trace(self.h, out.ctypes.data, n, C.byref(got)))
