@@ -24,7 +24,7 @@
 //    them share the LM head and its argmax.
 //  * phases hand over through monotonic device counters (one per layer and
 //    phase): a producer CTA's threads store their outputs, the CTA
-//    synchronizes, one thread fences and increments; a consumer's thread 0
+//    synchronizes, one thread increments with release semantics; a consumer's thread 0
 //    polls with acquire loads until the count of this step is reached. Every
 //    poll is bounded (kSpinLimit) and records MI_CUDA_ERR_TIMEOUT on expiry.
 //  * every CTA streams the weights of its coming work items, in order, into
@@ -187,6 +187,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
   __shared__ int32_t red_i[kNW];
   __shared__ float misc[4];
   __shared__ int s_dead;
+  __shared__ float xl[kMaxRes], x2l[kMaxRes];  // this CTA's rows of x and x2 (the next residuals)
   __shared__ uint32_t s_ticket;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -329,11 +330,12 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
     }
     __syncthreads();
   };
+  // After the CTA barrier, one release add publishes every thread's stores
+  // made before it (the barrier orders them before thread 0's release).
   auto signal_ctr = [&](unsigned long long* c) {
     __syncthreads();
     if (tid == 0) {
-      __threadfence();
-      atomicAdd(c, 1ull);
+      asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(c), "l"(1ull) : "memory");
     }
   };
 
@@ -646,7 +648,11 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         load_act(p.attn_q, nbE);
         const uint8_t* wb = wait_item(3 * l);
         if (rows > 0) rows_2t(wb, d);
-        for (int i = tid; i < rows; i += kNT) p.x2[r0 + i] = __fadd_rn(__ldcg(p.x + r0 + i), res[i]);
+        for (int i = tid; i < rows; i += kNT) {
+          const float v = __fadd_rn(l == 0 ? __ldcg(p.x + r0 + i) : xl[i], res[i]);
+          x2l[i] = v;
+          p.x2[r0 + i] = v;
+        }
         signal_ctr(&ctr[(size_t)l * 4 + 1]);
         free_item(3 * l);
         if (tr_gemv) pstamp(p, 2 * l + 1, 1);
@@ -687,7 +693,11 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         load_act(p.act_q, nbF);
         const uint8_t* wb = wait_item(3 * l + 2);
         if (rows > 0) rows_8t(wb, d);
-        for (int i = tid; i < rows; i += kNT) p.x[r0 + i] = __fadd_rn(__ldcg(p.x2 + r0 + i), res[i]);
+        for (int i = tid; i < rows; i += kNT) {
+          const float v = __fadd_rn(x2l[i], res[i]);
+          xl[i] = v;
+          p.x[r0 + i] = v;
+        }
         signal_ctr(&ctr[(size_t)l * 4 + 3]);
         free_item(3 * l + 2);
         if (tr_gemv) pstamp(p, 2 * l + 1, 6);
