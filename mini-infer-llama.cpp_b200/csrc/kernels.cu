@@ -714,6 +714,7 @@ cudaError_t prepare_kernels() {
   if (e == cudaSuccess) e = set_gemv_smem<0, true>(optin);
   if (e == cudaSuccess) e = prepare_attn_kernels(optin);
   if (e == cudaSuccess) e = prepare_gemm_kernel();
+  if (e == cudaSuccess) e = prepare_gemm_tc_kernel();
   if (e == cudaSuccess) e = prepare_qkv_attn_kernel(optin);
   if (e == cudaSuccess) e = prepare_persist_kernel(optin);
   return e;

@@ -300,9 +300,25 @@ struct GemmParams {
   float* d_out;
   int64_t q_stride;
   ExpTab et;
+  // The tensor-core path (prefill_tc.cu): the weights' prefill copy made by
+  // launch_pack_tc (nullptr: the CUDA-core kernel of prefill.cu), and the
+  // error word for its bounded waits.
+  const uint8_t* wt;
+  const float* st;
+  int32_t* err;
 };
 cudaError_t prepare_gemm_kernel();
 cudaError_t launch_gemm(const GemmParams& p, cudaStream_t s);
+// Tensor-core exact GEMM (prefill_tc.cu). tc_rows(npad) is the row count of
+// the prefill copy (a multiple of 128); launch_pack_tc fills it
+// (tc_weight_bytes of fp16 quants at wt, n_tc * K / 32 floats at st) from a
+// packed matrix.
+int64_t tc_rows(int64_t npad);
+size_t tc_weight_bytes(int64_t n_tc, int64_t K);
+cudaError_t launch_pack_tc(const uint8_t* w, int64_t K, int64_t npad, int64_t n_tc, uint8_t* wt, float* st,
+                           cudaStream_t s);
+cudaError_t prepare_gemm_tc_kernel();
+cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t s);
 
 // Per token: [embedding lookup (x_out),] [rms_norm * norm_w,] Q8_0_ACT quantize
 // into the split layout (q_out [t][K], d_out [t][K/32]).

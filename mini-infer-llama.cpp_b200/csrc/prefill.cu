@@ -230,6 +230,7 @@ cudaError_t prepare_gemm_kernel() {
 
 cudaError_t launch_gemm(const GemmParams& p, cudaStream_t s) {
   if (p.M <= 0) return cudaSuccess;
+  if (p.wt) return launch_gemm_tc(p, s);
   if (p.K % 32 != 0 || (p.epi == EPI_SILU_GATEUP_Q && p.n_pad % kGemmBN != 0)) return cudaErrorInvalidValue;
   dim3 grid((unsigned)((p.n_pad + kGemmBN - 1) / kGemmBN), (unsigned)((p.M + kGemmBM - 1) / kGemmBM));
   gemm_q8_kernel<<<grid, 256, GemmSmem::total, s>>>(p);

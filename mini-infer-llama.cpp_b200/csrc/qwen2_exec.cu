@@ -36,6 +36,9 @@ namespace {
 struct Mat {
   uint8_t* w = nullptr;
   int64_t K = 0, N = 0, npad = 0;
+  // the prefill copy for the tensor-core GEMM (launch_pack_tc), or nullptr
+  uint8_t* wt = nullptr;
+  float* st = nullptr;
 };
 
 struct Layer {
@@ -97,6 +100,8 @@ struct mi_cuda_model {
   bool tied = true;
   uint8_t* buf = nullptr;
   size_t bytes = 0;
+  uint8_t* tc_buf = nullptr;  // prefill copies of the GEMM weights (tensor-core layout)
+  size_t tc_bytes = 0;
   Mat embed, lm_head;
   float* output_norm = nullptr;
   std::vector<Layer> layers;
@@ -216,6 +221,41 @@ void shard_range(int64_t units, int rank, int world, int64_t* first, int64_t* co
 }  // namespace
 
 namespace {
+
+// The batched prefill's GEMMs run on the tensor cores from a second copy of
+// each weight matrix in their tile layout (fp16 quants and float scales,
+// about 2.13 bytes per weight);
+// MI_CUDA_TC_GEMM=0 skips it and the prefill uses the CUDA-core GEMM.
+int pack_prefill_copies(mi_cuda_model* m, cudaStream_t s) {
+  const char* env = std::getenv("MI_CUDA_TC_GEMM");
+  if (env && std::strcmp(env, "0") == 0) return MI_CUDA_OK;
+  std::vector<Mat*> mats;
+  for (auto& L : m->layers) {
+    mats.push_back(&L.qkv);
+    mats.push_back(&L.o);
+    mats.push_back(&L.gateup);
+    mats.push_back(&L.down);
+  }
+  mats.push_back(&m->lm_head);
+  auto bytes_of = [](const Mat& x) {
+    const size_t n = (size_t)tc_rows(x.npad);
+    return a256(tc_weight_bytes((int64_t)n, x.K)) + a256(n * (size_t)(x.K / 32) * 4);
+  };
+  size_t total = 0;
+  for (const Mat* x : mats) total += bytes_of(*x);
+  CK(cudaMalloc(&m->tc_buf, total));
+  m->tc_bytes = total;
+  size_t off = 0;
+  for (Mat* x : mats) {
+    const int64_t n = tc_rows(x->npad);
+    x->wt = m->tc_buf + off;
+    x->st = (float*)(m->tc_buf + off + a256(tc_weight_bytes(n, x->K)));
+    off += bytes_of(*x);
+    CK(launch_pack_tc(x->w, x->K, x->npad, n, x->wt, x->st, s));
+  }
+  CK(cudaStreamSynchronize(s));
+  return MI_CUDA_OK;
+}
 
 struct ModelDeleter {
   void operator()(mi_cuda_model* m) const { mi_cuda_qwen2_model_free(m); }
@@ -431,6 +471,7 @@ int load_model(const char* gguf_path, int device, int rank, int world, mi_cuda_m
     rc = upload_f32_range(bv, va, vb, L.bqkv + (E + kvd + va - q0), s);
     if (rc) break;
   }
+  if (!rc) rc = pack_prefill_copies(m.get(), s);
   cleanup();
   if (!rc && cudaGetLastError() != cudaSuccess) rc = fail(MI_CUDA_ERR_CUDA, "weight upload failed");
   if (rc) return rc;
@@ -462,6 +503,7 @@ void mi_cuda_qwen2_model_free(mi_cuda_model* model) {
   if (!model) return;
   cudaSetDevice(model->device);
   cudaFree(model->buf);
+  if (model->tc_buf) cudaFree(model->tc_buf);
   delete model;
 }
 
@@ -864,6 +906,9 @@ int enqueue_prefill(mi_cuda_kv_cache* kv, int32_t n, int32_t n_past, bool all_lo
     g.out = kv->pQKV;
     g.out_stride = row_qkv;
     g.et = et;
+    g.wt = L.qkv.wt;
+    g.st = L.qkv.st;
+    g.err = err;
     CK(launch_gemm(g, s));
 
     float* ck = kv->cache + (size_t)l * layer_floats;
@@ -937,6 +982,8 @@ int enqueue_prefill(mi_cuda_kv_cache* kv, int32_t n, int32_t n_past, bool all_lo
     o.resid = kv->pX;
     o.out = kv->pX2;
     o.out_stride = E;
+    o.wt = L.o.wt;
+    o.st = L.o.st;
     CK(launch_gemm(o, s));
 
     nq = NormQuantParams{};
@@ -959,6 +1006,8 @@ int enqueue_prefill(mi_cuda_kv_cache* kv, int32_t n, int32_t n_past, bool all_lo
     gu.q_out = kv->pAqF;
     gu.d_out = kv->pAdF;
     gu.q_stride = FF;
+    gu.wt = L.gateup.wt;
+    gu.st = L.gateup.st;
     CK(launch_gemm(gu, s));
 
     GemmParams dn{};
@@ -975,6 +1024,9 @@ int enqueue_prefill(mi_cuda_kv_cache* kv, int32_t n, int32_t n_past, bool all_lo
     dn.out = kv->pX;
     dn.out_stride = E;
     dn.et = et;
+    dn.wt = L.down.wt;
+    dn.st = L.down.st;
+    dn.err = err;
     CK(launch_gemm(dn, s));
   }
   if (all_logits && n > 1) {
@@ -1000,6 +1052,9 @@ int enqueue_prefill(mi_cuda_kv_cache* kv, int32_t n, int32_t n_past, bool all_lo
     h.out = kv->pLogits;
     h.out_stride = hp.n_vocab;
     h.et = et;
+    h.wt = m->lm_head.wt;
+    h.st = m->lm_head.st;
+    h.err = err;
     CK(launch_gemm(h, s));
   }
   // LM head + greedy argmax of the last token (the decode kernel, on row n-1).
