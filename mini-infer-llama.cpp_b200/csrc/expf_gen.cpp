@@ -132,6 +132,15 @@ int main(int argc, char** argv) {
   h.mul1 = mul1;
   h.mul2 = mul2;
   h.n_entries = (uint32_t)all.size();
+  // The device may skip the table for results far from a rounding boundary
+  // only if no exception lies far from one.
+  size_t far = 0;
+  for (const entry& e : all) {
+    const float x = mi_u2f(e.key);
+    if (!(x >= -110.0f && x <= 100.0f)) continue;  // these always probe
+    if (!mi_expf_near_tie(mi_expf_core_wide(x), MI_EXPF_TIE_VERIFIED)) far++;
+  }
+  if (far == 0) h.flags |= MI_EXPF_FLAG_TIE_FILTER;
   mi_expf_fingerprints(&h.core_checksum, &h.libm_checksum);
   std::string tmp = std::string(argv[1]) + ".tmp";
   FILE* f = std::fopen(tmp.c_str(), "wb");
@@ -146,6 +155,7 @@ int main(int argc, char** argv) {
     std::fprintf(stderr, "mi_expf_gen: write failed\n");
     return 1;
   }
-  std::printf("mi_expf_gen: %zu exceptions, 2^%u buckets\n", all.size(), log2b);
+  std::printf("mi_expf_gen: %zu exceptions, 2^%u buckets, %zu far from a rounding boundary\n", all.size(), log2b,
+              far);
   return 0;
 }

@@ -218,15 +218,37 @@ __device__ __forceinline__ void trace_mark(uint64_t* trace, int32_t slot, int po
 // libm-exact expf: the double-precision core plus one probe of the exception
 // hash (two buckets of four (key, value) pairs, loaded as four independent
 // 16-byte reads).
+// Read-only 16-byte load whose line L2 keeps in preference to others
+// (evict_last): the expf exception table is probed at random and would
+// otherwise be evicted by the weight streams between uses.
+__device__ __forceinline__ uint4 ldg_keep(const uint4* p) {
+  uint64_t pol;
+  asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  uint4 v;
+  asm("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p), "l"(pol));
+  return v;
+}
+
 __device__ __forceinline__ float expf_exact(float x, const ExpTab& t) {
-  float y = mi_expf_core(x);
+  float y;
+  if (x >= -110.0f && x <= 100.0f) {
+    const double yd = mi_expf_core_wide(x);
+    y = (float)yd;
+    // results far from a rounding boundary are never exceptions (when the
+    // table generator has verified that for this libm)
+    if (t.filter && !mi_expf_near_tie(yd, MI_EXPF_TIE_PROBE)) return y;
+  } else {
+    y = mi_expf_core(x);
+  }
   if (x == x) {
     uint32_t key = __float_as_uint(x);
     uint32_t b1 = mi_expf_bucket(key, t.mul1, t.log2b);
     uint32_t b2 = mi_expf_bucket(key, t.mul2, t.log2b);
     const uint4* p1 = t.buckets + 2 * (size_t)b1;
     const uint4* p2 = t.buckets + 2 * (size_t)b2;
-    uint4 a0 = __ldg(p1), a1 = __ldg(p1 + 1), c0 = __ldg(p2), c1 = __ldg(p2 + 1);
+    uint4 a0 = ldg_keep(p1), a1 = ldg_keep(p1 + 1), c0 = ldg_keep(p2), c1 = ldg_keep(p2 + 1);
     if (a0.x == key) y = __uint_as_float(a0.y);
     if (a0.z == key) y = __uint_as_float(a0.w);
     if (a1.x == key) y = __uint_as_float(a1.y);

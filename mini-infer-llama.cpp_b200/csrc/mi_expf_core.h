@@ -96,12 +96,8 @@ MI_HD float mi_u2f(uint32_t u) {
 #endif
 }
 
-// exp(x) in double, rounded once to float. NaN propagates; results beyond the
-// float range saturate to inf / 0 the way the final conversion rounds them.
-MI_HD float mi_expf_core(float x) {
-  if (!(x == x)) return x;
-  if (x > 100.0f) return mi_u2f(0x7f800000u);
-  if (x < -110.0f) return 0.0f;
+// exp(x) in double, before the final rounding; for -110 <= x <= 100.
+MI_HD double mi_expf_core_wide(float x) {
   const double inv_ln2_64 = 0x1.71547652b82fep+6;  // 64 / ln 2
   const double shift = 0x1.8p52;                    // round-to-int by addition
   const double ln2_64_hi = 0x1.62e42fefa39efp-7;    // ln 2 / 64, leading part
@@ -124,7 +120,40 @@ MI_HD float mi_expf_core(float x) {
   double tj = mi_exp2_tab(j);
   double y = MI_FMA(tj, p, tj);
   double s = mi_asdouble((uint64_t)(1023 + m) << 52);
-  return (float)MI_MUL(y, s);
+  return MI_MUL(y, s);
+}
+
+// exp(x) in double, rounded once to float. NaN propagates; results beyond the
+// float range saturate to inf / 0 the way the final conversion rounds them.
+MI_HD float mi_expf_core(float x) {
+  if (!(x == x)) return x;
+  if (x > 100.0f) return mi_u2f(0x7f800000u);
+  if (x < -110.0f) return 0.0f;
+  return (float)mi_expf_core_wide(x);
+}
+
+// Whether the double value yd lies within `thresh_bits` / 2^29 of a float
+// spacing from a rounding boundary of the float grid (always true for results
+// below the normal range or at the top of it). For a normal float result the
+// 29 mantissa bits of yd below float precision place it within the spacing;
+// the boundary is at 2^28. A libm expf whose error stays within 0.5 + eps ulp
+// can only round differently from the correctly rounded result where the exact
+// value lies within about eps ulp of a boundary, so the exception table needs
+// probing only near one; mi_expf_gen checks that every exception it finds is
+// within MI_EXPF_TIE_VERIFIED of a boundary before it marks the table for that
+// shortcut, and the device probes within the wider MI_EXPF_TIE_PROBE.
+#define MI_EXPF_TIE_PROBE (1u << 23)     // 2^-6 of the spacing
+#define MI_EXPF_TIE_VERIFIED (1u << 22)  // 2^-7 of the spacing
+MI_HD int mi_expf_near_tie(double yd, uint32_t thresh_bits) {
+  if (!(yd >= 0x1p-126 && yd < 0x1.fffffep127)) return 1;
+  uint64_t u;
+#ifdef __CUDA_ARCH__
+  u = (uint64_t)__double_as_longlong(yd);
+#else
+  memcpy(&u, &yd, 8);
+#endif
+  const int32_t low = (int32_t)((uint32_t)u & 0x1fffffffu) - (int32_t)0x10000000;
+  return (uint32_t)(low < 0 ? -low : low) < thresh_bits;
 }
 
 // Exception-table file / device layout: header, then n_buckets buckets of
@@ -134,6 +163,7 @@ MI_HD float mi_expf_core(float x) {
 #define MI_EXPF_MAGIC 0x4658454du  // "MEXF"
 #define MI_EXPF_SLOTS 4
 #define MI_EXPF_EMPTY 0xffffffffu
+#define MI_EXPF_FLAG_TIE_FILTER 1u
 
 typedef struct {
   uint32_t magic;
@@ -142,7 +172,7 @@ typedef struct {
   uint32_t n_entries;
   uint32_t core_checksum;  // fingerprint of mi_expf_core over a fixed sample
   uint32_t libm_checksum;  // fingerprint of the host expf over the same sample
-  uint32_t reserved;
+  uint32_t flags;          // MI_EXPF_FLAG_TIE_FILTER: every exception is near a boundary (mi_expf_near_tie)
 } mi_expf_table_header;
 
 MI_HD uint32_t mi_expf_bucket(uint32_t key, uint32_t mul, uint32_t log2_buckets) {

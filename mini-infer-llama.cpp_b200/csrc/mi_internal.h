@@ -12,6 +12,7 @@ namespace mi {
 struct ExpTab {
   const uint4* buckets;
   uint32_t log2b, mul1, mul2;
+  uint32_t filter;  // the table holds only results near a rounding boundary (mi_expf_near_tie)
 };
 
 // ---------------------------------------------------------------------------

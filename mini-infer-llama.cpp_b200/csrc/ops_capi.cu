@@ -70,6 +70,7 @@ bool load_expf_table(DeviceCtx* c, std::string* err) {
   c->et.log2b = h.log2_buckets;
   c->et.mul1 = h.mul1;
   c->et.mul2 = h.mul2;
+  c->et.filter = (h.flags & MI_EXPF_FLAG_TIE_FILTER) ? 1u : 0u;
   return true;
 }
 

@@ -346,49 +346,90 @@ cudaError_t launch_rope_kv(const float* qkv, int64_t row, int32_t head_dim, int3
 //   softmax max, e = expf(s - max), the denominator as one ordered chain,
 //           p = e * (1 / sum),
 //   out[r][o] = sum over k, in order, of V[k][o] * p[r][k].
-// The K / V tiles are shared by the n_rep heads; each chain is one thread's.
+// Register-blocked: in the score phase a thread owns one key of the tile and
+// the chains of up to 8 heads (q in shared memory as [d][8], read as two
+// broadcast float4 per d; the K row as float4); in the value phase a thread
+// owns 2 outputs of one head, reading four probabilities as a float4 and the
+// four V row pieces as float2 per step. Every chain keeps the reference's order (multiply, then
+// add, each rounded).
 // ---------------------------------------------------------------------------
-constexpr int kPfKT = 64;  // keys per K / V tile
+struct PfAttnShape {
+  int kt, rg;  // keys per tile, threads per key (each owning 8 / rg heads)
+  size_t smem(int D, int R, int64_t cap) const {
+    return ((size_t)8 * D + (size_t)kt * (D + 4) + (size_t)R * cap) * 4 + kChainSlackBytes;
+  }
+};
+__host__ __device__ inline PfAttnShape pf_attn_shape(int D) {
+  return D <= 64 ? PfAttnShape{256, 1} : (D <= 128 ? PfAttnShape{128, 2} : PfAttnShape{64, 4});
+}
+
+// A product then a sum, two lanes at a time, each rounded on its own. (Two
+// scalar operations per lane: ptxas may fuse an f32x2 multiply and the f32x2
+// add that consumes it into one FMA, which rounds once.)
+__device__ __forceinline__ float2 mul2s(float2 a, float2 b) {
+  return make_float2(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y));
+}
+__device__ __forceinline__ float2 add2s(float2 a, float2 b) {
+  return make_float2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y));
+}
 
 __global__ void __launch_bounds__(256) attn_prefill_kernel(const PrefillAttnParams p) {
   extern __shared__ __align__(16) float sm[];
   __shared__ float mx[8], inv[8];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kvh = blockIdx.x, t = blockIdx.y;
-  const int D = p.head_dim, R = p.n_rep, HKV = p.n_head_kv, KP = D + 1;
+  const int D = p.head_dim, R = p.n_rep, HKV = p.n_head_kv, KP = D + 4;
+  const PfAttnShape shp = pf_attn_shape(D);
+  const int KT = shp.kt, RG = shp.rg;
   const int n_kv = p.n_past + t + 1;
   const int cap = p.sc_stride;  // score row stride (>= n_kv, a multiple of 4)
-  float* qs = sm;                          // [R][D]
-  float* Ks = qs + R * D;                  // [kPfKT][D + 1]
-  float* Vs = Ks + kPfKT * KP;             // [kPfKT][D]
-  float* sc = Vs + kPfKT * D;              // [R][cap] (+ slack)
+  float* qs = sm;            // [D][8]: q[r][d] at d*8 + r (r >= R: zero)
+  float* Ts = qs + 8 * D;    // K tile [KT][D + 4], then V tile [KT][D], then the outputs [R][D]
+  float* sc = Ts + KT * KP;  // [R][cap]
   const size_t rs = (size_t)HKV * D;
   const float* kb = p.cache_k + (size_t)kvh * D;
   const float* vb = p.cache_v + (size_t)kvh * D;
   const int h0 = kvh * R;
-  for (int e = tid; e < R * D; e += 256) qs[e] = p.q_rot[((size_t)t * p.n_head + h0) * D + e];
-  const int n_chunks = (n_kv + kPfKT - 1) / kPfKT;
+  for (int e = tid; e < 8 * D; e += 256) {
+    const int d = e >> 3, r = e & 7;
+    qs[e] = r < R ? p.q_rot[((size_t)t * p.n_head + h0 + r) * D + d] : 0.0f;
+  }
+  const int n_chunks = (n_kv + KT - 1) / KT;
+  // ---- scores ----
+  const int kk = tid % KT, rgi = tid / KT, npair = 4 / RG;  // head pairs rgi*npair ..
   for (int c = 0; c < n_chunks; c++) {
-    const int c0 = c * kPfKT, rows = min(kPfKT, n_kv - c0);
+    const int c0 = c * KT, rows = min(KT, n_kv - c0);
     __syncthreads();
     for (int e = tid; e < rows * (D >> 2); e += 256) {
       const int r = e / (D >> 2), q4 = e - r * (D >> 2);
-      const float4 v = *(const float4*)(kb + (size_t)(c0 + r) * rs + q4 * 4);
-      float* d = Ks + r * KP + q4 * 4;  // padded rows: the per-key dot reads conflict-free
-      d[0] = v.x;
-      d[1] = v.y;
-      d[2] = v.z;
-      d[3] = v.w;
+      *(float4*)(Ts + r * KP + q4 * 4) = *(const float4*)(kb + (size_t)(c0 + r) * rs + q4 * 4);
     }
     __syncthreads();
-    for (int e = tid; e < R * rows; e += 256) {
-      const int r = e / rows, k = e - r * rows;
-      const float acc = ordered_dot(0.0f, Ks + k * KP, 1, qs + r * D, D);
-      sc[r * cap + c0 + k] = __fmul_rn(acc, p.scale);
+    if (kk < rows) {
+      const float* kr = Ts + kk * KP;
+      float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      for (int d4 = 0; d4 < (D >> 2); d4++) {
+        const float4 kv = *(const float4*)(kr + 4 * d4);
+        const float kd[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const float2 k2 = make_float2(kd[i], kd[i]);
+          const float2* q2 = (const float2*)(qs + (4 * d4 + i) * 8) + rgi * npair;
+#pragma unroll
+          for (int j = 0; j < 4; j++)
+            if (j < npair) acc[j] = add2s(acc[j], mul2s(k2, q2[j]));
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int r = 2 * (rgi * npair + j);
+        if (j < npair && r < R) sc[r * cap + c0 + kk] = __fmul_rn(acc[j].x, p.scale);
+        if (j < npair && r + 1 < R) sc[(r + 1) * cap + c0 + kk] = __fmul_rn(acc[j].y, p.scale);
+      }
     }
   }
   __syncthreads();
-  // softmax: the maximum per head (order-free), expf, the ordered denominator
+  // ---- softmax: the maximum per head (order-free), expf, the ordered denominator ----
   if (warp < R) {
     float m = -INFINITY;
     for (int k = lane; k < n_kv; k += 32) m = fmaxf(m, sc[warp * cap + k]);
@@ -396,55 +437,90 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const PrefillAttnPara
     if (lane == 0) mx[warp] = m;
   }
   __syncthreads();
-  for (int e = tid; e < R * n_kv; e += 256) {
-    const int r = e / n_kv, k = e - r * n_kv;
-    sc[r * cap + k] = expf_exact(__fsub_rn(sc[r * cap + k], mx[r]), p.et);
-  }
-  __syncthreads();
-  if (warp < R && lane == 0) inv[warp] = __fdiv_rn(1.0f, ordered_sum_smem(sc + warp * cap, n_kv));
-  // (the normalization p = e * inv is applied inside the value chains)
-  // out[r][o]: thread chains (r, o) = (e / D, e % D) for e = tid + 256 c
-  constexpr int kMaxChains = 4;  // R * D <= 1024
-  float acc[kMaxChains] = {0.0f, 0.0f, 0.0f, 0.0f};
-  for (int c = 0; c < n_chunks; c++) {
-    const int c0 = c * kPfKT, rows = min(kPfKT, n_kv - c0);
-    __syncthreads();
-    for (int e = tid; e < rows * (D >> 2); e += 256) {
-      const int r = e / (D >> 2), q4 = e - r * (D >> 2);
-      *(float4*)(Vs + r * D + q4 * 4) = *(const float4*)(vb + (size_t)(c0 + r) * rs + q4 * 4);
-    }
-    __syncthreads();
-#pragma unroll
-    for (int j = 0; j < kMaxChains; j++) {
-      const int e = tid + 256 * j;
-      if (e < R * D) {
-        const int r = e / D, o = e - r * D;
-        acc[j] = ordered_dot_scaled(acc[j], Vs + o, D, sc + r * cap + c0, inv[r], rows);
+  {
+    // element e = r * n_kv + k, stepping by the CTA size without a division
+    int r = tid / n_kv, k = tid - r * n_kv;
+    for (; r < R;) {
+      float* a = sc + r * cap + k;
+      *a = expf_exact(__fsub_rn(*a, mx[r]), p.et);
+      k += 256;
+      while (k >= n_kv) {
+        k -= n_kv;
+        r++;
       }
     }
   }
+  __syncthreads();
+  if (warp < R && lane == 0) inv[warp] = __fdiv_rn(1.0f, ordered_sum_smem(sc + warp * cap, n_kv));
+  __syncthreads();
+  for (int e = tid; e < R * n_kv; e += 256) {
+    const int r = e / n_kv, k = e - r * n_kv;
+    sc[r * cap + k] = __fmul_rn(sc[r * cap + k], inv[r]);  // p = e * (1 / sum)
+  }
+  // ---- values: unit u = (head r, outputs 2*o2, 2*o2 + 1) ----
+  const int D2 = D >> 1, n_units = R * D2;
+  constexpr int kMaxUnits = 4;  // R * D / 2 <= 1024
+  float2 acc[kMaxUnits];
 #pragma unroll
-  for (int j = 0; j < kMaxChains; j++) {
-    const int e = tid + 256 * j;
-    if (e >= R * D) break;  // warp-uniform: R * D is a multiple of 32
+  for (int j = 0; j < kMaxUnits; j++) acc[j] = make_float2(0.f, 0.f);
+  for (int c = 0; c < n_chunks; c++) {
+    const int c0 = c * KT, rows = min(KT, n_kv - c0);
+    __syncthreads();
+    for (int e = tid; e < rows * (D >> 2); e += 256) {
+      const int r = e / (D >> 2), q4 = e - r * (D >> 2);
+      *(float4*)(Ts + r * D + q4 * 4) = *(const float4*)(vb + (size_t)(c0 + r) * rs + q4 * 4);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kMaxUnits; j++) {
+      const int u = tid + 256 * j;
+      if (u >= n_units) break;
+      const int r = u / D2, o2 = u - r * D2;
+      const float* pr = sc + r * cap + c0;
+      const float* vr = Ts + 2 * o2;
+      float2 a = acc[j];
+      int k = 0;
+      for (; k + 4 <= rows; k += 4) {
+        const float4 p4 = *(const float4*)(pr + k);
+        const float pk[4] = {p4.x, p4.y, p4.z, p4.w};
+        float2 v[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) v[i] = *(const float2*)(vr + (k + i) * D);
+#pragma unroll
+        for (int i = 0; i < 4; i++) a = add2s(a, mul2s(v[i], make_float2(pk[i], pk[i])));
+      }
+      for (; k < rows; k++) a = add2s(a, mul2s(*(const float2*)(vr + k * D), make_float2(pr[k], pr[k])));
+      acc[j] = a;
+    }
+  }
+  __syncthreads();
+  float* outs = Ts;  // [R][D], the concatenated heads' outputs
+#pragma unroll
+  for (int j = 0; j < kMaxUnits; j++) {
+    const int u = tid + 256 * j;
+    if (u >= n_units) break;
+    *(float2*)(outs + 2 * u) = acc[j];
+  }
+  __syncthreads();
+  for (int e = tid; e < R * D; e += 256) {
     const size_t col = (size_t)h0 * D + e;  // element of the concatenated heads
     if (p.act_qs) {
       // the O projection's quantize node, one 32-element block per warp
+      // (R * D is a multiple of 32, so the loop bound is warp-uniform)
       float d;
-      const int8_t q = quantize_lane(acc[j], &d);
+      const int8_t q = quantize_lane(outs[e], &d);
       p.act_qs[(size_t)t * p.row + col] = q;
       if (lane == 0) p.act_d[((size_t)t * p.row + col) >> 5] = d;
     } else {
-      p.out[(size_t)t * p.row + col] = acc[j];
+      p.out[(size_t)t * p.row + col] = outs[e];
     }
   }
 }
 
 bool prefill_attn_fits(int32_t head_dim, int32_t n_rep, int64_t max_kv) {
   const int64_t cap = (max_kv + 3) / 4 * 4;
-  const int64_t smem = ((int64_t)n_rep * head_dim + kPfKT * (head_dim + 1) + kPfKT * head_dim + n_rep * cap) * 4 +
-                       kChainSlackBytes;
-  return n_rep <= 8 && n_rep * head_dim <= 1024 && head_dim % 4 == 0 && smem <= 200 * 1024;
+  return n_rep <= 8 && head_dim <= 256 && n_rep * head_dim <= 2048 && head_dim % 4 == 0 &&
+         pf_attn_shape(head_dim).smem(head_dim, n_rep, cap) <= 200 * 1024;
 }
 
 cudaError_t launch_attn_prefill(const PrefillAttnParams& p, int64_t n_tokens, cudaStream_t s) {
@@ -454,8 +530,7 @@ cudaError_t launch_attn_prefill(const PrefillAttnParams& p, int64_t n_tokens, cu
   if (!prefill_attn_fits(p.head_dim, p.n_rep, max_kv)) return cudaErrorInvalidValue;
   if (p.act_qs && (p.n_rep * p.head_dim) % 32 != 0) return cudaErrorInvalidValue;
   q.sc_stride = (int32_t)((max_kv + 3) / 4 * 4);
-  const size_t smem = (size_t)((int64_t)p.n_rep * p.head_dim + kPfKT * (p.head_dim + 1) + kPfKT * p.head_dim +
-                               (int64_t)p.n_rep * q.sc_stride) * 4 + kChainSlackBytes;
+  const size_t smem = pf_attn_shape(p.head_dim).smem(p.head_dim, p.n_rep, q.sc_stride);
   cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   attn_prefill_kernel<<<dim3((unsigned)p.n_head_kv, (unsigned)n_tokens), 256, smem, s>>>(q);
