@@ -359,8 +359,12 @@ struct PfAttnShape {
     return ((size_t)8 * D + (size_t)kt * (D + 4) + (size_t)R * cap) * 4 + kChainSlackBytes;
   }
 };
+// 128-key tiles (two threads per key up to head_dim 128) keep the shared
+// memory of a CTA near 66 KB at 1024 positions (0.5B shape), so three CTAs
+// share an SM; 256-key tiles (two CTAs per SM) measured 10% slower for the
+// whole prefill, 64-key tiles 5% slower.
 __host__ __device__ inline PfAttnShape pf_attn_shape(int D) {
-  return D <= 64 ? PfAttnShape{256, 1} : (D <= 128 ? PfAttnShape{128, 2} : PfAttnShape{64, 4});
+  return D <= 128 ? PfAttnShape{128, 2} : PfAttnShape{64, 4};
 }
 
 // A product then a sum, two lanes at a time, each rounded on its own. (Two
