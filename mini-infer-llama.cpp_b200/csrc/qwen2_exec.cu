@@ -102,6 +102,7 @@ struct mi_cuda_model {
   size_t bytes = 0;
   uint8_t* tc_buf = nullptr;  // prefill copies of the GEMM weights (tensor-core layout)
   size_t tc_bytes = 0;
+  bool tc_tried = false;      // pack_prefill_copies ran (once per model)
   Mat embed, lm_head;
   float* output_norm = nullptr;
   std::vector<Layer> layers;
@@ -224,9 +225,12 @@ namespace {
 
 // The batched prefill's GEMMs run on the tensor cores from a second copy of
 // each weight matrix in their tile layout (fp16 quants and float scales,
-// about 2.13 bytes per weight);
-// MI_CUDA_TC_GEMM=0 skips it and the prefill uses the CUDA-core GEMM.
+// about 2.13 bytes per weight), made on the first batched prefill of the
+// model (a decode-only user never pays for it). MI_CUDA_TC_GEMM=0 skips it,
+// as does a failed allocation, and the prefill then uses the CUDA-core GEMM.
 int pack_prefill_copies(mi_cuda_model* m, cudaStream_t s) {
+  if (m->tc_tried) return MI_CUDA_OK;
+  m->tc_tried = true;
   const char* env = std::getenv("MI_CUDA_TC_GEMM");
   if (env && std::strcmp(env, "0") == 0) return MI_CUDA_OK;
   std::vector<Mat*> mats;
@@ -243,7 +247,11 @@ int pack_prefill_copies(mi_cuda_model* m, cudaStream_t s) {
   };
   size_t total = 0;
   for (const Mat* x : mats) total += bytes_of(*x);
-  CK(cudaMalloc(&m->tc_buf, total));
+  if (cudaMalloc(&m->tc_buf, total) != cudaSuccess) {
+    cudaGetLastError();  // (clears the allocation error; the CUDA-core GEMM serves)
+    m->tc_buf = nullptr;
+    return MI_CUDA_OK;
+  }
   m->tc_bytes = total;
   size_t off = 0;
   for (Mat* x : mats) {
@@ -471,7 +479,6 @@ int load_model(const char* gguf_path, int device, int rank, int world, mi_cuda_m
     rc = upload_f32_range(bv, va, vb, L.bqkv + (E + kvd + va - q0), s);
     if (rc) break;
   }
-  if (!rc) rc = pack_prefill_copies(m.get(), s);
   cleanup();
   if (!rc && cudaGetLastError() != cudaSuccess) rc = fail(MI_CUDA_ERR_CUDA, "weight upload failed");
   if (rc) return rc;
@@ -1426,6 +1433,7 @@ int mi_cuda_qwen2_forward(mi_cuda_model* m, mi_cuda_kv_cache* kv, const int32_t*
   kv->h_state->feedback = 0;
   const size_t V = (size_t)m->hp.n_vocab;
   if (use_batched_prefill(kv, n_tokens)) {
+    if (int rc = pack_prefill_copies(m, kv->stream)) return rc;
     kv->h_state->pos = n_past + n_tokens - 1;
     CK(cudaMemcpyAsync(kv->state, kv->h_state, sizeof(StepState), cudaMemcpyHostToDevice, kv->stream));
     const bool all = !last_logits_only && h_logits_out;
@@ -1491,6 +1499,8 @@ int mi_cuda_qwen2_generate(mi_cuda_model* m, mi_cuda_kv_cache* kv, const int32_t
   if (rc) return rc;
   // The reference loop stops once n_past reaches n_ctx (src/main.cpp:409-423).
   const int32_t n_decode = std::min<int32_t>(n_predict - 1, kv->n_ctx - n_prompt);
+  if (use_batched_prefill(kv, n_prompt))
+    if (int rc2 = pack_prefill_copies(kv->model, kv->stream)) return rc2;
   CK(cudaEventRecord(kv->ev[0], kv->stream));
   if (use_batched_prefill(kv, n_prompt)) {
     // the prompt in one batch; its LM head feeds the first token back
