@@ -602,6 +602,9 @@ def prefill_measure(path: str, model, kv, steps: int, warmup: int, with_cpu: boo
         "roofline": {"bound": "tensor", "achieved": ops, "peak": peak_tops, "unit": "TOPS",
                      "frac": ops / peak_tops, "traffic": None,
                      "peak_kind": "2 x measured bf16 TF/s (the int8 tensor rate)",
+                     "achieved_counts": "useful int8 multiply-adds of the projections (x2); the GEMMs run them "
+                                        "as lane-expanded fp16 tcgen05 MMAs (4x the useful MACs on the tensor "
+                                        "pipe) feeding the exact FMA chains on the CUDA cores",
                      "kernel": "prefill (24 layers x (norm, QKV GEMM, RoPE/KV, attention, O GEMM, norm, "
                                "gate/up GEMM, down GEMM) + LM head)",
                      "ops_per_step": 2 * prefill_macs(hp, N_PREFILL)},

@@ -357,20 +357,41 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     } else if (lane == 0) {
       // ---------------- MMA issue ----------------
+      // This thread's loop is on the critical path of every block, so it does
+      // as little as possible: the descriptors are the first stage's plus the
+      // operand's offset in 16-byte units (shared addresses stay below 2^18,
+      // so the 14-bit address field never carries).
+      const uint64_t a0 = umma_desc(smem_addr(smem + TcSmem::wa), 128, 512);
+      const uint64_t b0 = umma_desc(smem_addr(smem + TcSmem::bx0), 128, 256);
+      int s = 0, g = 0, c = 0;
+      uint32_t pf = 0, pb = 0, pt = 0;  // phases of full[s], bready[c], tempty[d] to wait for
       for (int b = 0; b < nb; b++) {
-        const int i = b / kTcG, s = i % kTcStages, g = b % kTcG, c = b % kTcBx, d = b & 1;
-        if (g == 0 && !tc_wait1(&full[s], (i / kTcStages) & 1, abort_flag, p.err)) break;
-        if (!tc_wait1(&bready[c], (b / kTcBx) & 1, abort_flag, p.err)) break;
-        if (b >= 2 && !tc_wait1(&tempty[d], ((b >> 1) + 1) & 1, abort_flag, p.err)) break;
+        const int d = b & 1;
+        if (g == 0 && !tc_wait1(&full[s], pf, abort_flag, p.err)) break;
+        if (!tc_wait1(&bready[c], pb, abort_flag, p.err)) break;
+        if (b >= 2 && !tc_wait1(&tempty[d], pt, abort_flag, p.err)) break;
         tc_fence_after();
-        const uint32_t wa = smem_addr(smem + s * TcSmem::stage + TcSmem::wa + g * 8192);
-        const uint32_t ba = smem_addr(smem + TcSmem::bx0 + c * 8192);
+        const uint64_t ad = a0 + (uint64_t)((s * TcSmem::stage + g * 8192) >> 4);
+        const uint64_t bd = b0 + (uint64_t)((c * 8192) >> 4);
         const uint32_t dt = tmem + (uint32_t)d * 256;
-        umma_f16(dt, umma_desc(wa, 128, 512), umma_desc(ba, 128, 256));
-        umma_f16(dt + 128, umma_desc(wa + 256, 128, 512), umma_desc(ba + 4096, 128, 256));
+        umma_f16(dt, ad, bd);
+        umma_f16(dt + 128, ad + (256 >> 4), bd + (4096 >> 4));
         umma_commit(&tfull[d]);
         umma_commit(&bfree[c]);
         n_issued[1] = b + 1;
+        // advance the ring positions and the phases they wait for
+        if (d == 1 && b >= 2) pt ^= 1u;
+        if (++c == kTcBx) {
+          c = 0;
+          pb ^= 1u;
+        }
+        if (++g == kTcG) {
+          g = 0;
+          if (++s == kTcStages) {
+            s = 0;
+            pf ^= 1u;
+          }
+        }
       }
     }
   } else {
