@@ -377,14 +377,16 @@ __device__ __forceinline__ float2 add2s(float2 a, float2 b) {
   return make_float2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y));
 }
 
+// RG threads per key in the score phase (each owning 8 / RG heads), a
+// compile-time constant so the head-pair loops carry no predicated-off work.
+template <int RG>
 __global__ void __launch_bounds__(256) attn_prefill_kernel(const PrefillAttnParams p) {
   extern __shared__ __align__(16) float sm[];
   __shared__ float mx[8], inv[8];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kvh = blockIdx.x, t = blockIdx.y;
   const int D = p.head_dim, R = p.n_rep, HKV = p.n_head_kv, KP = D + 4;
-  const PfAttnShape shp = pf_attn_shape(D);
-  const int KT = shp.kt, RG = shp.rg;
+  constexpr int KT = 256 / RG;
   const int n_kv = p.n_past + t + 1;
   const int cap = p.sc_stride;  // score row stride (>= n_kv, a multiple of 4)
   float* qs = sm;            // [D][8]: q[r][d] at d*8 + r (r >= R: zero)
@@ -399,13 +401,15 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const PrefillAttnPara
     qs[e] = r < R ? p.q_rot[((size_t)t * p.n_head + h0 + r) * D + d] : 0.0f;
   }
   const int n_chunks = (n_kv + KT - 1) / KT;
+  const int sh4 = __ffs(D >> 2) - 1;  // log2(D / 4): head_dim is a power of two here
   // ---- scores ----
-  const int kk = tid % KT, rgi = tid / KT, npair = 4 / RG;  // head pairs rgi*npair ..
+  constexpr int npair = 4 / RG;
+  const int kk = tid % KT, rgi = tid / KT;  // head pairs rgi*npair ..
   for (int c = 0; c < n_chunks; c++) {
     const int c0 = c * KT, rows = min(KT, n_kv - c0);
     __syncthreads();
     for (int e = tid; e < rows * (D >> 2); e += 256) {
-      const int r = e / (D >> 2), q4 = e - r * (D >> 2);
+      const int r = e >> sh4, q4 = e & ((D >> 2) - 1);
       *(float4*)(Ts + r * KP + q4 * 4) = *(const float4*)(kb + (size_t)(c0 + r) * rs + q4 * 4);
     }
     __syncthreads();
@@ -457,10 +461,18 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const PrefillAttnPara
   __syncthreads();
   if (warp < R && lane == 0) inv[warp] = __fdiv_rn(1.0f, ordered_sum_smem(sc + warp * cap, n_kv));
   __syncthreads();
-  for (int e = tid; e < R * n_kv; e += 256) {
-    const int r = e / n_kv, k = e - r * n_kv;
-    sc[r * cap + k] = __fmul_rn(sc[r * cap + k], inv[r]);  // p = e * (1 / sum)
-  }
+  // p = e * (1 / sum), four at a time (entries past n_kv are never read)
+  for (int r = 0; r < R; r++)
+    for (int k4 = tid; 4 * k4 < n_kv; k4 += 256) {
+      float4* a = (float4*)(sc + r * cap) + k4;
+      const float iv = inv[r];
+      float4 v = *a;
+      v.x = __fmul_rn(v.x, iv);
+      v.y = __fmul_rn(v.y, iv);
+      v.z = __fmul_rn(v.z, iv);
+      v.w = __fmul_rn(v.w, iv);
+      *a = v;
+    }
   // ---- values: unit u = (head r, outputs 2*o2, 2*o2 + 1) ----
   const int D2 = D >> 1, n_units = R * D2;
   constexpr int kMaxUnits = 4;  // R * D / 2 <= 1024
@@ -471,7 +483,7 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const PrefillAttnPara
     const int c0 = c * KT, rows = min(KT, n_kv - c0);
     __syncthreads();
     for (int e = tid; e < rows * (D >> 2); e += 256) {
-      const int r = e / (D >> 2), q4 = e - r * (D >> 2);
+      const int r = e >> sh4, q4 = e & ((D >> 2) - 1);
       *(float4*)(Ts + r * D + q4 * 4) = *(const float4*)(vb + (size_t)(c0 + r) * rs + q4 * 4);
     }
     __syncthreads();
@@ -523,7 +535,8 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const PrefillAttnPara
 
 bool prefill_attn_fits(int32_t head_dim, int32_t n_rep, int64_t max_kv) {
   const int64_t cap = (max_kv + 3) / 4 * 4;
-  return n_rep <= 8 && head_dim <= 256 && n_rep * head_dim <= 2048 && head_dim % 4 == 0 &&
+  return n_rep <= 8 && head_dim >= 4 && head_dim <= 256 && (head_dim & (head_dim - 1)) == 0 &&
+         n_rep * head_dim <= 2048 &&
          pf_attn_shape(head_dim).smem(head_dim, n_rep, cap) <= 200 * 1024;
 }
 
@@ -535,9 +548,11 @@ cudaError_t launch_attn_prefill(const PrefillAttnParams& p, int64_t n_tokens, cu
   if (p.act_qs && (p.n_rep * p.head_dim) % 32 != 0) return cudaErrorInvalidValue;
   q.sc_stride = (int32_t)((max_kv + 3) / 4 * 4);
   const size_t smem = pf_attn_shape(p.head_dim).smem(p.head_dim, p.n_rep, q.sc_stride);
-  cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int rg = pf_attn_shape(p.head_dim).rg;
+  auto kern = rg == 2 ? attn_prefill_kernel<2> : (rg == 4 ? attn_prefill_kernel<4> : attn_prefill_kernel<1>);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  attn_prefill_kernel<<<dim3((unsigned)p.n_head_kv, (unsigned)n_tokens), 256, smem, s>>>(q);
+  kern<<<dim3((unsigned)p.n_head_kv, (unsigned)n_tokens), 256, smem, s>>>(q);
   return cudaGetLastError();
 }
 
