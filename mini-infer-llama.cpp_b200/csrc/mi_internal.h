@@ -149,7 +149,7 @@ bool attn_split_fits(int64_t head_dim, int64_t n_head, int64_t n_head_kv);
 void attn_split_shape(int64_t n_kv, int64_t n_head_kv, int32_t* n_splits, int32_t* per_split);
 size_t attn_split_scratch_bytes(int64_t n_head, int64_t n_kv, int64_t n_head_kv, int64_t head_dim);
 cudaError_t launch_attn_split(const float* q, const float* ck, const float* cv, int64_t D, int64_t H, int64_t HKV,
-                              int64_t n_kv, float scale, const ExpTab& et, float* part, float* out,
+                              int64_t n_kv, float scale, const ExpTab& et, int32_t* err, float* part, float* out,
                               cudaStream_t s);
 
 // ---------------------------------------------------------------------------

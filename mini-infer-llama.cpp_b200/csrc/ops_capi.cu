@@ -437,10 +437,11 @@ int mi_cuda_attention_decode_split(const float* d_q, const float* d_cache_k, con
                                    float scale, void* d_scratch, float* d_dst, mi_cuda_stream s) {
   MI_CTX(c);
   MI_REQUIRE(d_q && d_cache_k && d_cache_v && d_scratch && d_dst && n_kv > 0 && n_kv < (1ll << 31) &&
-                 attn_split_fits(head_dim, n_head, n_head_kv),
-             "mi_cuda_attention_decode_split: bad arguments");
+                 attn_split_fits(head_dim, n_head, n_head_kv) && (uintptr_t)d_cache_k % 16 == 0 &&
+                 (uintptr_t)d_cache_v % 16 == 0 && (uintptr_t)d_scratch % 16 == 0,
+             "mi_cuda_attention_decode_split: bad arguments (16-byte aligned caches and scratch)");
   return cuda_status(launch_attn_split(d_q, d_cache_k, d_cache_v, head_dim, n_head, n_head_kv, n_kv, scale,
-                                       c->et, (float*)d_scratch, d_dst, S(s)),
+                                       c->et, c->err, (float*)d_scratch, d_dst, S(s)),
                      "attention_decode_split");
 }
 
