@@ -257,6 +257,80 @@ def step_trace_summary(kv) -> dict:
 
 
 
+def fast_mode_measure(args, kv, seed_tokens, exact_gen, stream, dist, local: int, world: int, hp,
+                      peak: float, peak_kind: str) -> dict:
+    """The labelled fast mode of the decode step (mi_cuda_qwen2_set_fast_mode:
+    regrouped sums, CUDA expf; never the parity result): the same timed decode
+    steps, then its accuracy -- teacher-forced on the exact run's 128 tokens,
+    the argmax at every position against the exact step's, with the exact
+    top-two gap wherever they differ (a disagreement is expected only where
+    that gap is within the fast mode's logit error), and the length of the
+    identical prefix of a free-running fast greedy generation."""
+    import torch
+    kv.set_fast_mode(True)
+    kv.set_position(seed_tokens, N_PROMPT)
+    kv.decode_steps(args.warmup, N_PROMPT, PERIOD)
+    torch.cuda.synchronize()
+    kv.set_position(seed_tokens, N_PROMPT)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    kv.decode_steps(args.steps, N_PROMPT, PERIOD)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if dist:
+        dist.barrier()
+        t = torch.tensor([ms], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    trace = step_trace_summary(kv) if args.trace else None
+    kv.set_position(seed_tokens, N_PROMPT)
+    kv.decode_steps(PERIOD)
+    free_run = kv.read_tokens(N_PROMPT, N_PREDICT)
+    same = free_run == exact_gen
+    prefix = int(np.argmin(same)) if not np.all(same) else int(same.size)
+
+    seq = np.concatenate([seed_tokens[:N_PROMPT], exact_gen]).astype(np.int32)
+
+    def teacher_forced():
+        return np.stack([kv.forward(seq[N_PROMPT + t:N_PROMPT + t + 1], N_PROMPT + t, last_logits_only=True)[0]
+                         for t in range(PERIOD)])
+
+    fast = teacher_forced()
+    kv.set_fast_mode(False)
+    exact = teacher_forced()
+    fa, ea = np.argmax(fast, axis=1), np.argmax(exact, axis=1)
+    rows = np.arange(PERIOD)
+    mad = float(np.max(np.abs(fast.astype(np.float64) - exact)))
+    a, b = fast.astype(np.float64).ravel(), exact.astype(np.float64).ravel()
+    cos = float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
+    gaps = (exact[rows, ea] - exact[rows, fa])[fa != ea]
+    n_kvs = [N_PROMPT + (i % PERIOD) + 1 for i in range(args.steps)]
+    achieved = sum(step_bytes(hp, n) for n in n_kvs) / (ms / 1e3) / 1e9
+    out = {
+        "label": "fast mode: tree-reduced rms_norm and softmax sums, split value sums and down-projection "
+                 "dots, CUDA expf; NOT bit-identical, not the parity result",
+        "value": args.steps * world / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms / args.steps,
+        "steps": args.steps,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": peak_kind},
+        "argmax_agreement": {
+            "teacher_forced": float(np.mean(fa == ea)), "n_positions": PERIOD, "disagreements": int(gaps.size),
+            "max_abs_logit_diff": mad, "cos": cos,
+            "disagree_max_exact_gap": float(gaps.max()) if gaps.size else None,
+            "gap_check": bool(np.all(gaps <= 2 * mad)),
+            "run": "exact run's tokens fed back (positions 32..158), fast vs exact step argmax"},
+        "free_run": {"tokens_identical_prefix": prefix, "n_tokens": int(exact_gen.size)},
+    }
+    if trace is not None:
+        out["trace"] = trace
+    return out
+
+
 def decode_config() -> dict:
     """The decode workload, the same dict on both arms."""
     return {"workload": "qwen2.5-0.5b-shape Q8_0 greedy decode, ctx 2048, prompt 32, positions 32..158",
@@ -874,6 +948,9 @@ def decode_measure(args, dist, rank: int, world: int, local: int) -> dict:
 
     e2e_tps = e2e_run(False)
     e2e_logits_tps = e2e_run(True)
+    fast = None
+    if not args.no_fast_mode and kv.kernels_per_step == 1:
+        fast = fast_mode_measure(args, kv, seed_tokens, gen, stream, dist, local, world, hp, peak, peak_kind)
     clk.__exit__(None, None, None)
     kernels = kv.kernels_per_step
 
@@ -913,12 +990,14 @@ def decode_measure(args, dist, rank: int, world: int, local: int) -> dict:
                        "d2h_bytes_per_step": hp.n_vocab * 4 + 4,
                        "api": "mi_cuda_qwen2_forward (logits row out) + host greedy, as the reference loop"},
         "gpu_launches": args.steps * kernels + (args.steps - 1) // PERIOD,
-        "clocks": {**clk.summary(), "span": "warm-up, timed steps, parity pass and e2e runs"},
+        "clocks": {**clk.summary(), "span": "warm-up, timed steps, parity pass, e2e runs and the fast-mode run"},
         "cpu_baseline": cpu,
         "parity": parity,
     }
     if trace is not None:
         line["trace"] = trace
+    if fast is not None:
+        line["fast_mode"] = fast
     if sweeps is not None:
         line["sweeps"] = sweeps
     return line
@@ -934,6 +1013,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tp7b", action="store_true", help="decode: skip the 7B tensor-parallel object")
     ap.add_argument("--no-sweeps", action="store_true", help="decode: skip the configs 1-3 sweeps")
+    ap.add_argument("--no-fast-mode", action="store_true", help="decode: skip the labelled fast-mode object")
     ap.add_argument("--config", choices=["decode", "gemv", "attention", "prefill", "tp7b"], default="decode",
                     help="decode: config 0 (default); gemv: config-1 GEMV sweep; attention: config 2; "
                          "prefill: config 3, 1024-token prompt; tp7b: config 4, 7B shape tensor-parallel over the "

@@ -303,6 +303,20 @@ int mi_cuda_qwen2_step_trace(mi_cuda_kv_cache* kv, uint64_t* h_out, int32_t max_
 mi_cuda_stream mi_cuda_qwen2_stream(mi_cuda_kv_cache* kv);
 int32_t mi_cuda_qwen2_kernels_per_step(mi_cuda_kv_cache* kv);
 
+/* No counterpart in the reference: a labelled FAST MODE of the decode step
+ * (on = 1), for measuring how close the step's design comes to the bandwidth
+ * roofline without the reference's sequential sums. Same schedule and
+ * kernel as the persistent step, but rms_norm's sum of squares and the
+ * softmax denominator are block trees, the attention value sums and the
+ * down projection's dot products are split over thread groups, and the
+ * softmax uses CUDA's expf. Results are NOT bit-identical to the reference
+ * (greedy tokens can differ where the top two logits are close); on = 0
+ * restores the exact step. Applies to decode steps only (a batched prompt
+ * stays exact). MI_CUDA_ERR_STATE where the persistent step is not in use
+ * (tensor parallelism, shapes it does not support, MI_CUDA_PERSIST=0). */
+int mi_cuda_qwen2_set_fast_mode(mi_cuda_kv_cache* kv, int32_t on);
+int32_t mi_cuda_qwen2_fast_mode(mi_cuda_kv_cache* kv);
+
 #ifdef __cplusplus
 }
 #endif

@@ -30,6 +30,14 @@
 //  * every CTA streams the weights of its coming work items, in order, into
 //    a ring in shared memory with bulk async copies (one mbarrier per item),
 //    so weights arrive ahead of the phases that need them.
+//
+// FAST = true is a labelled fast mode (not bit-identical to the reference,
+// never reported as parity): the same schedule and hand-overs, but the sums
+// the reference computes as sequential chains are regrouped -- rms_norm's sum
+// of squares and the softmax denominator as block trees, the attention value
+// sums split over thread groups, the QK dots as four interleaved chains, the
+// down projection's 152-block lane chains split over the CTA's warps -- and
+// the softmax uses CUDA's expf.
 #include <algorithm>
 #include <cstdlib>
 
@@ -180,10 +188,11 @@ __device__ inline void pstamp(const PersistParams& p, int slot, int point) {
   if (p.trace) p.trace[(size_t)slot * kTracePoints + point] = globaltimer_ns();
 }
 
+template <bool FAST>
 __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(16) float qr[128], kr[128], vr[128];
-  __shared__ float red_f[kNW];
+  __shared__ float red_f[kNW], red_s[kNW];
   __shared__ int32_t red_i[kNW];
   __shared__ float misc[4];
   __shared__ int s_dead;
@@ -366,12 +375,26 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       for (int k = tid; k < E / 4; k += kNT) ((float4*)xs)[k] = __ldcg((const float4*)x + k);
     }
     __syncthreads();
-    for (int k = tid; k < E; k += kNT) sq[k] = __fmul_rn(xs[k], xs[k]);
-    __syncthreads();
-    const float ss = spec_ordered_sum<kNT, 2>(sq, E, smem + L.spec);
-    if (tid == 0) misc[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)E), p.eps)));
-    __syncthreads();
-    const float scale = misc[0];
+    float scale;
+    if constexpr (FAST) {
+      // fast mode: the sum of squares as a block tree
+      float part = 0.0f;
+      for (int k = tid; k < E; k += kNT) part = fmaf(xs[k], xs[k], part);
+      part = warp_sum_tree(part);
+      if (lane == 0) red_s[warp] = part;
+      __syncthreads();
+      float ss = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kNW; w++) ss += red_s[w];
+      scale = rsqrtf(ss / (float)E + p.eps);
+    } else {
+      for (int k = tid; k < E; k += kNT) sq[k] = __fmul_rn(xs[k], xs[k]);
+      __syncthreads();
+      const float ss = spec_ordered_sum<kNT, 2>(sq, E, smem + L.spec);
+      if (tid == 0) misc[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)E), p.eps)));
+      __syncthreads();
+      scale = misc[0];
+    }
     // four blocks per warp at once overlap the quantizer's divisions
     float v[4], d[4];
     int8_t q[4];
@@ -389,6 +412,32 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         aq[b * 32 + lane] = q[u];
         if (lane == 0) ad[b] = d[u];
       }
+    }
+    __syncthreads();
+  };
+  // Fast mode: the down projection's rows with each row's blocks split over
+  // the CTA's warps (warp w takes blocks [w nb / kNW, (w+1) nb / kNW) of every
+  // group; lanes as rows_8t), partials summed through shared memory (sq).
+  // Needs Gt * 4 * kNW <= E floats of scratch: rows_8t otherwise.
+  auto rows_8t_split = [&](const uint8_t* base, const ItemDesc& d) {
+    const int K = (int)d.K, nb = K / 32, Gt = d.G[0];
+    const int rr = lane >> 3, j = lane & 7;
+    const int b0 = warp * nb / kNW, b1 = (warp + 1) * nb / kNW;
+    for (int g = 0; g < Gt; g++) {
+      const uint32_t* gq = (const uint32_t*)(base + (size_t)g * 4 * K) + (size_t)b0 * 32;
+      const __half* gd = (const __half*)(base + (size_t)Gt * 4 * K) + (size_t)g * nb * 4 + (size_t)b0 * 4;
+      float acc = lane_chain(0.0f, gq, gd, (const int*)aq + b0 * 8, ad + b0, b1 - b0, lane, j, rr);
+      acc += __shfl_xor_sync(FULL, acc, 4);
+      acc += __shfl_xor_sync(FULL, acc, 1);
+      acc += __shfl_xor_sync(FULL, acc, 2);
+      if (j == 0) sq[warp * Gt * 4 + g * 4 + rr] = acc;
+    }
+    __syncthreads();
+    for (int i = tid; i < Gt * 4; i += kNT) {
+      float s = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kNW; w++) s += sq[w * Gt * 4 + i];
+      res[i] = s;
     }
     __syncthreads();
   };
@@ -582,7 +631,22 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         }
         // scores[i] * scale, d ascending with separate roundings (src/ops_cpu.cpp:373-376)
         for (int i = tid; i < rows; i += kNT) {
-          const float v = __fmul_rn(ordered_dot(0.0f, Ks + (size_t)i * KP, 1, qr, D), p.scale);
+          float dot;
+          if constexpr (FAST) {
+            // fast mode: four interleaved chains
+            const float* kr_ = Ks + (size_t)i * KP;
+            float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+            for (int e = 0; e < D; e += 4) {
+              s0 = fmaf(kr_[e], qr[e], s0);
+              s1 = fmaf(kr_[e + 1], qr[e + 1], s1);
+              s2 = fmaf(kr_[e + 2], qr[e + 2], s2);
+              s3 = fmaf(kr_[e + 3], qr[e + 3], s3);
+            }
+            dot = (s0 + s1) + (s2 + s3);
+          } else {
+            dot = ordered_dot(0.0f, Ks + (size_t)i * KP, 1, qr, D);
+          }
+          const float v = __fmul_rn(dot, p.scale);
           sc[c0 + i] = v;
           lmax = fmaxf(lmax, v);
         }
@@ -592,25 +656,47 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       __syncthreads();
       float mx = red_f[0];
       for (int w = 1; w < kNW; w++) mx = fmaxf(mx, red_f[w]);
-      for (int i = tid; i < n_kv; i += kNT) sc[i] = expf_exact(__fsub_rn(sc[i], mx), p.et);
-      __syncthreads();
-      if (tr_attn) pstamp(p, 2 * l, 5);
-      // the softmax denominator: one ordered chain (src/ops_cpu.cpp:331-336)
-      if (tid == 0) {
-        float sum = 0.0f;
-        if (p.scores_in_smem) {
-          sum = ordered_sum_smem(sc, n_kv);
-        } else {
-#pragma unroll 8
-          for (int i = 0; i < n_kv; i++) sum = __fadd_rn(sum, sc[i]);
+      float inv;
+      if constexpr (FAST) {
+        // fast mode: exp and the denominator's block tree in one pass
+        float ls = 0.0f;
+        for (int i = tid; i < n_kv; i += kNT) {
+          const float e = expf(sc[i] - mx);
+          sc[i] = e;
+          ls += e;
         }
-        misc[1] = __fdiv_rn(1.0f, sum);
+        ls = warp_sum_tree(ls);
+        if (lane == 0) red_s[warp] = ls;
+        __syncthreads();
+        if (tr_attn) pstamp(p, 2 * l, 5);
+        float sum = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kNW; w++) sum += red_s[w];
+        inv = 1.0f / sum;
+      } else {
+        for (int i = tid; i < n_kv; i += kNT) sc[i] = expf_exact(__fsub_rn(sc[i], mx), p.et);
+        __syncthreads();
+        if (tr_attn) pstamp(p, 2 * l, 5);
+        // the softmax denominator: one ordered chain (src/ops_cpu.cpp:331-336)
+        if (tid == 0) {
+          float sum = 0.0f;
+          if (p.scores_in_smem) {
+            sum = ordered_sum_smem(sc, n_kv);
+          } else {
+#pragma unroll 8
+            for (int i = 0; i < n_kv; i++) sum = __fadd_rn(sum, sc[i]);
+          }
+          misc[1] = __fdiv_rn(1.0f, sum);
+        }
+        __syncthreads();
+        inv = misc[1];
       }
-      __syncthreads();
-      const float inv = misc[1];
       if (tr_attn) pstamp(p, 2 * l, 6);
       // out[o] = sum_t V[o, kvh, t] * P[t], t ascending (src/ops_cpu.cpp:402-406);
-      // the K / V tiles of the next layer replace these only after this loop
+      // the K / V tiles of the next layer replace these only after this loop.
+      // Fast mode: NG = kNT / D thread groups each take every NG-th position,
+      // their partials meet in shared memory (res), normalized at the end.
+      const int NG = FAST ? kNT / D : 1, grp = tid / D, o_el = tid - grp * D;
       float acc = 0.0f;
       for (int c = 0; c < n_chunks; c++) {
         const int c0 = c * KT, rows = min(KT, n_kv - c0);
@@ -621,7 +707,21 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
             for (int i = tid; i < D; i += kNT) Vs[(size_t)(n_past - c0) * D + i] = vr[i];
           __syncthreads();
         }
-        if (tid < D) acc = ordered_dot_scaled(acc, Vs + tid, D, sc + c0, inv, rows);
+        if constexpr (FAST) {
+          if (grp < NG)
+            for (int i = grp; i < rows; i += NG) acc = fmaf(Vs[(size_t)i * D + o_el], sc[c0 + i], acc);
+        } else {
+          if (tid < D) acc = ordered_dot_scaled(acc, Vs + tid, D, sc + c0, inv, rows);
+        }
+      }
+      if constexpr (FAST) {
+        if (grp < NG) res[tid] = acc;
+        __syncthreads();
+        if (tid < D) {
+          float s = 0.0f;
+          for (int g2 = 0; g2 < NG; g2++) s += res[g2 * D + tid];
+          acc = s * inv;
+        }
       }
       // the O projection's quantize node (src/ops_cpu.cpp:462-479) for this
       // head's outputs: warp w holds block h*D/32 + w
@@ -692,7 +792,10 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         if (tr_gemv) pstamp(p, 2 * l + 1, 5);
         load_act(p.act_q, nbF);
         const uint8_t* wb = wait_item(3 * l + 2);
-        if (rows > 0) rows_8t(wb, d);
+        if (rows > 0) {
+          if (FAST && rows * kNW <= E) rows_8t_split(wb, d);
+          else rows_8t(wb, d);
+        }
         for (int i = tid; i < rows; i += kNT) {
           const float v = __fadd_rn(x2l[i], res[i]);
           xl[i] = v;
@@ -802,13 +905,20 @@ int g_optin = 0;
 }  // namespace
 
 cudaError_t prepare_persist_kernel(int optin) {
-  cudaFuncAttributes f{};
-  cudaError_t e = cudaFuncGetAttributes(&f, persist_step_kernel);
+  // both instantiations (exact and fast mode) get the same dynamic budget
+  cudaFuncAttributes f0{}, f1{};
+  cudaError_t e = cudaFuncGetAttributes(&f0, persist_step_kernel<false>);
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&f1, persist_step_kernel<true>);
+  const int dyn = optin - (int)std::max(f0.sharedSizeBytes, f1.sharedSizeBytes);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(persist_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             optin - (int)f.sharedSizeBytes);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(persist_step_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-  if (e == cudaSuccess) g_optin = optin - (int)f.sharedSizeBytes;
+    e = cudaFuncSetAttribute(persist_step_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(persist_step_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(persist_step_kernel<false>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(persist_step_kernel<true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess) g_optin = dyn;
   return e;
 }
 
@@ -849,11 +959,14 @@ PersistPlan plan_persist(int64_t E, int32_t D, int32_t H, int32_t HKV, int64_t F
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cfg.gridDim = dim3((unsigned)(C * (num_sms / C)));
-  int n_clusters = 0;
-  if (cudaOccupancyMaxActiveClusters(&n_clusters, persist_step_kernel, &cfg) != cudaSuccess) {
+  // the grid must be resident at once in both modes (exact and fast)
+  int n_clusters = 0, n_fast = 0;
+  if (cudaOccupancyMaxActiveClusters(&n_clusters, persist_step_kernel<false>, &cfg) != cudaSuccess ||
+      cudaOccupancyMaxActiveClusters(&n_fast, persist_step_kernel<true>, &cfg) != cudaSuccess) {
     cudaGetLastError();
     return pl;
   }
+  n_clusters = std::min(n_clusters, n_fast);
   n_clusters = std::min(n_clusters, num_sms / C);
   const int32_t n_attn = HKV * C;
   const int32_t grid = C * n_clusters;
@@ -900,7 +1013,8 @@ cudaError_t launch_persist(const PersistParams& p, const PersistPlan& plan, cuda
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, persist_step_kernel, q);
+  return q.fast ? cudaLaunchKernelEx(&cfg, persist_step_kernel<true>, q)
+                : cudaLaunchKernelEx(&cfg, persist_step_kernel<false>, q);
 }
 
 }  // namespace mi

@@ -385,6 +385,14 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Butterfly sum over a warp (tree order: only for the labelled fast mode,
+// never on a path that must match the reference's sequential sums).
+__device__ __forceinline__ float warp_sum_tree(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
 // C independent ordered chains over the same terms: s[c] = fl(s[c] + a[i]) for
 // i in order. The chains interleave, so C of them cost about one chain's
 // latency. `a` is 16-byte aligned shared memory that stays readable 8 floats

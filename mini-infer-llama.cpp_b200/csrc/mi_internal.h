@@ -263,6 +263,7 @@ struct PersistParams {
   int32_t ring_gemv, ring_attn;  // weight-ring bytes of the two roles
   ExpTab et;
   uint64_t* trace;             // optional: 8 stamps per slot, 2 slots per layer + 1
+  int32_t fast;                // 1: the labelled fast mode (regrouped sums, not bit-exact)
 };
 
 struct PersistPlan {

@@ -132,6 +132,10 @@ struct mi_cuda_kv_cache {
   bool seen_valid = false;
   int32_t* h_tokens = nullptr;   // pinned staging, n_ctx + 1
   cudaGraphExec_t g_head = nullptr, g_nohead = nullptr;
+  // the labelled fast mode's step graphs (persistent step only), captured by
+  // the first mi_cuda_qwen2_set_fast_mode(kv, 1); `fast` selects them
+  cudaGraphExec_t g_fast_head = nullptr, g_fast_nohead = nullptr;
+  bool fast = false;
   int32_t kernels_per_step = 0;
   uint64_t* trace = nullptr;  // [slot][4] globaltimer stamps of the last step
   int32_t trace_slots = 0;
@@ -590,6 +594,7 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     q.ticket = (uint32_t*)(kv->pctr + (size_t)hp.n_layer * 4 + 1);
     q.et = et;
     q.trace = kv->trace;
+    q.fast = kv->fast ? 1 : 0;
     CK(launch_persist(q, kv->plan_persist, kv->stream));
     if (n_kernels) *n_kernels = 1;
     return MI_CUDA_OK;
@@ -1105,6 +1110,10 @@ int graphs_ready(mi_cuda_kv_cache* kv) {
   return MI_CUDA_OK;
 }
 
+// The step graphs of the current mode (exact, or the labelled fast mode).
+cudaGraphExec_t head_graph(const mi_cuda_kv_cache* kv) { return kv->fast ? kv->g_fast_head : kv->g_head; }
+cudaGraphExec_t nohead_graph(const mi_cuda_kv_cache* kv) { return kv->fast ? kv->g_fast_nohead : kv->g_nohead; }
+
 int check_state_error(mi_cuda_kv_cache* kv) {
   // The step state (error word, next token) into pinned memory behind the
   // stream's work: one host round trip per call, and mi_cuda_qwen2_last_token
@@ -1338,6 +1347,8 @@ void mi_cuda_kv_cache_free(mi_cuda_kv_cache* kv) {
   if (kv->pLogits) cudaFree(kv->pLogits);
   if (kv->g_head) cudaGraphExecDestroy(kv->g_head);
   if (kv->g_nohead) cudaGraphExecDestroy(kv->g_nohead);
+  if (kv->g_fast_head) cudaGraphExecDestroy(kv->g_fast_head);
+  if (kv->g_fast_nohead) cudaGraphExecDestroy(kv->g_fast_nohead);
   for (auto& e : kv->ev)
     if (e) cudaEventDestroy(e);
   if (kv->stream) cudaStreamDestroy(kv->stream);
@@ -1378,7 +1389,7 @@ int mi_cuda_qwen2_decode_steps(mi_cuda_kv_cache* kv, int32_t n_steps, int32_t po
   CK(cudaSetDevice(kv->model->device));
   for (int32_t i = 0; i < n_steps; i++) {
     if (period > 0 && i > 0 && i % period == 0) CK(launch_set_pos(&kv->state->pos, pos0, kv->stream));
-    CK(cudaGraphLaunch(kv->g_head, kv->stream));
+    CK(cudaGraphLaunch(head_graph(kv), kv->stream));
   }
   return MI_CUDA_OK;
 }
@@ -1398,6 +1409,32 @@ int mi_cuda_qwen2_read_tokens(mi_cuda_kv_cache* kv, int32_t first, int32_t n, in
 mi_cuda_stream mi_cuda_qwen2_stream(mi_cuda_kv_cache* kv) { return kv ? (mi_cuda_stream)kv->stream : nullptr; }
 
 int32_t mi_cuda_qwen2_kernels_per_step(mi_cuda_kv_cache* kv) { return kv ? kv->kernels_per_step : 0; }
+
+int mi_cuda_qwen2_set_fast_mode(mi_cuda_kv_cache* kv, int32_t on) {
+  if (!kv || (on != 0 && on != 1)) return fail(MI_CUDA_ERR_ARG, "mi_cuda_qwen2_set_fast_mode: bad arguments");
+  if (on && !kv->persist)
+    return fail(MI_CUDA_ERR_STATE, "fast mode needs the persistent one-kernel step (one GPU, a supported shape)");
+  if ((on != 0) == kv->fast) return MI_CUDA_OK;
+  kv->seen_valid = false;
+  CK(cudaSetDevice(kv->model->device));
+  CK(cudaStreamSynchronize(kv->stream));
+  if (on && !kv->g_fast_head) {
+    kv->fast = true;
+    int rc = capture(kv, true, &kv->g_fast_head, nullptr);
+    if (!rc) rc = capture(kv, false, &kv->g_fast_nohead, nullptr);
+    kv->fast = false;
+    if (rc) {
+      if (kv->g_fast_head) cudaGraphExecDestroy(kv->g_fast_head);
+      kv->g_fast_head = nullptr;
+      cudaGetLastError();
+      return rc;
+    }
+  }
+  kv->fast = on != 0;
+  return MI_CUDA_OK;
+}
+
+int32_t mi_cuda_qwen2_fast_mode(mi_cuda_kv_cache* kv) { return kv && kv->fast ? 1 : 0; }
 
 int mi_cuda_qwen2_step_trace(mi_cuda_kv_cache* kv, uint64_t* h_out, int32_t max_slots,
                              int32_t* n_slots) {
@@ -1450,7 +1487,7 @@ int mi_cuda_qwen2_forward(mi_cuda_model* m, mi_cuda_kv_cache* kv, const int32_t*
   CK(cudaMemcpyAsync(kv->state, kv->h_state, sizeof(StepState), cudaMemcpyHostToDevice, kv->stream));
   for (int32_t t = 0; t < n_tokens; t++) {
     const bool head = !last_logits_only || t == n_tokens - 1;
-    CK(cudaGraphLaunch(head ? kv->g_head : kv->g_nohead, kv->stream));
+    CK(cudaGraphLaunch(head ? head_graph(kv) : nohead_graph(kv), kv->stream));
     if (head && h_logits_out) {
       // a sharded model fills its rows [v0, v0 + nv) of each logits row
       float* dst = h_logits_out + (last_logits_only ? 0 : (size_t)t * V) + m->sh.v0;
@@ -1508,11 +1545,11 @@ int mi_cuda_qwen2_generate(mi_cuda_model* m, mi_cuda_kv_cache* kv, const int32_t
     CK(cudaMemcpyAsync(kv->state, kv->h_state, sizeof(StepState), cudaMemcpyHostToDevice, kv->stream));
     if (int rc2 = enqueue_prefill(kv, n_prompt, 0, false)) return rc2;
   } else {
-    for (int32_t t = 0; t + 1 < n_prompt; t++) CK(cudaGraphLaunch(kv->g_nohead, kv->stream));
-    CK(cudaGraphLaunch(kv->g_head, kv->stream));
+    for (int32_t t = 0; t + 1 < n_prompt; t++) CK(cudaGraphLaunch(nohead_graph(kv), kv->stream));
+    CK(cudaGraphLaunch(head_graph(kv), kv->stream));
   }
   CK(cudaEventRecord(kv->ev[1], kv->stream));
-  for (int32_t i = 0; i < n_decode; i++) CK(cudaGraphLaunch(kv->g_head, kv->stream));
+  for (int32_t i = 0; i < n_decode; i++) CK(cudaGraphLaunch(head_graph(kv), kv->stream));
   CK(cudaEventRecord(kv->ev[2], kv->stream));
   const int32_t produced = 1 + n_decode;
   CK(cudaMemcpyAsync(kv->h_tokens, kv->tokens + n_prompt, (size_t)produced * 4,

@@ -88,6 +88,8 @@ _SIGS = {
     "mi_cuda_qwen2_read_tokens": (I32, [P, I32, I32, P]),
     "mi_cuda_qwen2_stream": (P, [P]),
     "mi_cuda_qwen2_kernels_per_step": (I32, [P]),
+    "mi_cuda_qwen2_set_fast_mode": (I32, [P, I32]),
+    "mi_cuda_qwen2_fast_mode": (I32, [P]),
     "mi_cuda_qwen2_step_trace": (I32, [P, P, I32, P]),
     "mi_cuda_qwen2_model_load_shard": (I32, [C.c_char_p, I32, I32, I32, P]),
     "mi_cuda_tp_shard_range": (I32, [I64, I32, I32, P, P]),
@@ -430,6 +432,16 @@ class KVCache:
     @property
     def kernels_per_step(self) -> int:
         return int(lib().mi_cuda_qwen2_kernels_per_step(self.h))
+
+    @property
+    def fast_mode(self) -> bool:
+        return bool(lib().mi_cuda_qwen2_fast_mode(self.h))
+
+    def set_fast_mode(self, on: bool):
+        """Labelled fast mode of the decode step (regrouped sums; NOT
+        bit-identical to the reference): on / off. Raises where the
+        persistent step is not in use."""
+        check(lib().mi_cuda_qwen2_set_fast_mode(self.h, int(bool(on))))
 
     def step_trace(self) -> np.ndarray:
         """[slots, 8] globaltimer stamps (ns) of the last step. Kernel-per-phase

@@ -149,6 +149,69 @@ def test_step_trace(mc, model_path, qkv_attn_path):
     model.free()
 
 
+def teacher_forced_logits(kv, seq, n_prompt, n_steps):
+    """Logits of decode steps at positions n_prompt .. n_prompt + n_steps - 1
+    fed the given token sequence (teacher forcing), one step per call."""
+    return np.stack([kv.forward(seq[n_prompt + t:n_prompt + t + 1], n_prompt + t, last_logits_only=True)[0]
+                     for t in range(n_steps)])
+
+
+@pytest.mark.parametrize("kv_tile", [None, "32"])
+def test_fast_mode_close_and_switchable(mc, model_path, monkeypatch, kv_tile):
+    """The labelled fast mode (regrouped sums, CUDA expf) is not bit-exact;
+    teacher-forced on the exact run's tokens its logits stay within the
+    north-star tolerance (max-abs 1e-2, cosine >= 0.9999), its greedy argmax
+    agrees with the exact one wherever the exact top-two gap exceeds the
+    measured logit error, and switching it off restores bit-identical logits.
+    kv_tile 32: attention walks several K / V tiles."""
+    monkeypatch.setenv("MI_CUDA_PERSIST", "1")
+    if kv_tile:
+        monkeypatch.setenv("MI_CUDA_PERSIST_KV_TILE", kv_tile)
+    path = model_path("SMALL", 4)
+    model = mc.Qwen2Model(path)
+    kv = mc.KVCache(model, 256)
+    assert kv.kernels_per_step == 1
+    n_prompt, n_steps = 32, 80
+    prompt = np.random.default_rng(11).integers(0, model.n_vocab, n_prompt).astype(np.int32)
+    toks, _, _ = kv.generate(prompt, n_steps + 1)
+    seq = np.concatenate([prompt, toks]).astype(np.int32)
+    kv.forward(prompt, 0, last_logits_only=True, want_logits=False)
+    exact = teacher_forced_logits(kv, seq, n_prompt, n_steps)
+    assert np.array_equal(np.argmax(exact, axis=1), toks[1:n_steps + 1])
+    assert not kv.fast_mode
+    kv.set_fast_mode(True)
+    assert kv.fast_mode
+    fast = teacher_forced_logits(kv, seq, n_prompt, n_steps)
+    mad, cos = logits_close(fast, exact)
+    assert mad <= 1e-2 and cos >= 0.9999
+    assert not np.array_equal(bits(fast), bits(exact))  # regrouped sums: not the exact path
+    fa, ea = np.argmax(fast, axis=1), np.argmax(exact, axis=1)
+    rows = np.arange(n_steps)
+    gap = exact[rows, ea] - exact[rows, fa]
+    assert np.all(gap[fa != ea] <= 2 * mad)
+    assert np.mean(fa == ea) >= 0.9
+    # the device-resident stepping path runs the fast graph too
+    kv.set_position(seq[:n_prompt + 1], n_prompt)
+    kv.decode_steps(8)
+    assert kv.read_tokens(n_prompt, 9).size == 9
+    kv.set_fast_mode(False)
+    again = teacher_forced_logits(kv, seq, n_prompt, n_steps)
+    assert np.array_equal(bits(again), bits(exact))
+    kv.free()
+    model.free()
+
+
+def test_fast_mode_refused_without_persistent_step(mc, model_path, monkeypatch):
+    monkeypatch.setenv("MI_CUDA_PERSIST", "0")
+    model = mc.Qwen2Model(model_path("SMALL", 4))
+    kv = mc.KVCache(model, 64)
+    with pytest.raises(mc.MiCudaError):
+        kv.set_fast_mode(True)
+    assert not kv.fast_mode
+    kv.free()
+    model.free()
+
+
 def test_context_limit_matches_reference(mc, model_path):
     # The reference stops decoding once n_past reaches n_ctx (src/main.cpp:409-423).
     path = model_path("TINY", 1)
