@@ -220,7 +220,9 @@ def persist_trace_summary(kv) -> dict:
                               "gate_up_rows": us(g[:, 4] - g[:, 3]), "down_wait": us(g[:, 5] - g[:, 4]),
                               "down": us(g[:, 6] - g[:, 5])},
         "lm_head_us": {"wait": float(h[0] - g[-1, 6]) / 1e3, "norm_quant": float(h[1] - h[0]) / 1e3,
-                       "rows_argmax": float(h[2] - h[1]) / 1e3}}
+                       "rows_argmax": float(h[2] - h[1]) / 1e3, "of_which_ring_wait": float(h[4]) / 1e3,
+                       "of_which_rows": float(h[5]) / 1e3, "of_which_free_issue": float(h[6]) / 1e3,
+                       "ring_items": int(h[7])}}
 
 
 def step_trace_summary(kv) -> dict:

@@ -53,6 +53,13 @@ constexpr int kQ = 16;               // ring items in flight per CTA (one mbarri
 constexpr int kHeadChunkGroups = 16;  // LM-head rows per ring item: 16 groups of 4
 constexpr int kMaxRes = 256;          // rows of one work item
 constexpr int kScoresOnChipMax = 8192;
+// The thread that owns the weight ring (issues its bulk copies). Issuing a
+// bulk copy holds the thread while the SM's copy engine is busy with earlier
+// copies (~0.5 us per 64 KB item in the LM head); moving the issue to a thread
+// of another warp only moved that time into the ring waits and slowed the
+// layers by ~2 us each on B200, so thread 0 issues, after the CTA's signal.
+constexpr int kIssuer = 0;
+
 
 __host__ __device__ inline size_t up16(size_t v) { return (v + 15) / 16 * 16; }
 __host__ __device__ inline size_t up128(size_t v) { return (v + 127) / 128 * 128; }
@@ -170,7 +177,7 @@ __device__ inline uint32_t item_bytes(const ItemDesc& d) {
   return b;
 }
 
-// Ring bookkeeping in shared memory (thread 0 writes, every thread reads the
+// Ring bookkeeping in shared memory (kIssuer writes, every thread reads the
 // offsets after the item's mbarrier completes).
 struct RingState {
   uint32_t head, tail;  // monotonic byte positions (issued / freed)
@@ -317,13 +324,13 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
   // drain at the end of the kernel still waits (bounded) for its copies and
   // no mbarrier is re-armed while a copy counted on it may be in flight.
   auto free_item = [&](int it) {
-    if (tid == 0 && !s_dead) {
+    if (tid == kIssuer && !s_dead) {
       rs->tail = rs->end[it % kQ];
       rs->freed = it + 1;
       issue_more();
     }
   };
-  if (tid == 0) issue_more();
+  if (tid == kIssuer) issue_more();
 
   // ---- hand-over counters ----
   auto wait_ctr = [&](const unsigned long long* c, unsigned long long target) {
@@ -472,7 +479,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       const uint4* gq = (const uint4*)(rb + (size_t)gc * 4 * K);
       const __half* gd = (const __half*)(rb + (size_t)Gr * 4 * K) + (size_t)gc * nb * 4;
       float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-#pragma unroll 2
+#pragma unroll 4
       for (int i = 0; i < nb; i++) {
         const uint4 w = gq[i * 8 + (lane & 7)];
         const uint4 a = aq16[i * 2 + hh];
@@ -816,11 +823,28 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       if (tr_gemv) pstamp(p, 2 * p.n_layer, 1);
       float bv = -INFINITY;
       int32_t bi = 0x7fffffff;
+      // trace: thread 0's time waiting for LM-head ring items, and the rest
+      uint64_t t_wait = 0, t_rows = 0, t_free = 0, t_mark = tr_gemv ? globaltimer_ns() : 0;
       for (int it = r.n_main; it < r.n_items; it++) {
         const ItemDesc d = item_desc(p, lay, r, it);
         const uint8_t* wb = wait_item(it);
+        if (tr_gemv) {
+          const uint64_t now = globaltimer_ns();
+          t_wait += now - t_mark;
+          t_mark = now;
+        }
         rows_2t(wb, d);  // ends with a CTA barrier: the item may be reused
+        if (tr_gemv) {
+          const uint64_t now = globaltimer_ns();
+          t_rows += now - t_mark;
+          t_mark = now;
+        }
         free_item(it);
+        if (tr_gemv) {
+          const uint64_t now = globaltimer_ns();
+          t_free += now - t_mark;
+          t_mark = now;
+        }
         const int r0 = 4 * d.g0[0];
         for (int i = tid; i < 4 * d.G[0]; i += kNT) {
           const int row = r0 + i;
@@ -833,6 +857,13 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
           }
         }
         __syncthreads();  // res is rewritten by the next chunk
+        if (tr_gemv) t_mark = globaltimer_ns();
+      }
+      if (tr_gemv && p.trace) {
+        p.trace[(size_t)(2 * p.n_layer) * kTracePoints + 4] = t_wait;
+        p.trace[(size_t)(2 * p.n_layer) * kTracePoints + 5] = t_rows;
+        p.trace[(size_t)(2 * p.n_layer) * kTracePoints + 6] = t_free;
+        p.trace[(size_t)(2 * p.n_layer) * kTracePoints + 7] = (uint64_t)(r.n_items - r.n_main);
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {

@@ -452,7 +452,9 @@ class KVCache:
         done, rows done, k/v received, exp done, sum done, head signalled) and
         the first projection CTA (O wait done, O signalled, gate/up wait done,
         its prologue done, gate/up signalled, down wait done, down signalled)
-        -- then the LM head (wait done, prologue done, rows done, step closed)."""
+        -- then the LM head (wait done, prologue done, rows done, step closed,
+        then the first projection CTA's totals over its LM-head items: ns
+        waiting for ring items, ns in the rows, ns issuing copies, items)."""
         n = self.kernels_per_step if self.kernels_per_step > 1 else 2 * self.model.hparams.n_layer + 1
         out = np.zeros((n, 8), dtype=np.uint64)
         got = C.c_int32()
