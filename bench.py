@@ -201,22 +201,24 @@ def reference_decode(path: str, steps: int, warmup: int, threads: int):
 
 def persist_trace_summary(kv) -> dict:
     """Phase timeline of the last timed persistent step (one kernel): per
-    layer, from attention CTA 0 and the first projection CTA, means over the
-    layers in microseconds."""
+    layer, from attention CTA 0 (the attention cluster also runs the O
+    projection) and the first projection CTA, means over the layers in
+    microseconds."""
     t = kv.step_trace().astype(np.int64)
     L = kv.model.hparams.n_layer
     a, g, h = t[0:2 * L:2], t[1:2 * L:2], t[2 * L]
     us = lambda v: float(np.mean(v)) / 1e3
     return {
-        "schedule": "persistent (one kernel per step)",
+        "schedule": "persistent (one kernel per step; attention + O on one cluster)",
         "step_us": float(h[2] - a[0, 0]) / 1e3,
         "per_layer_us": us(np.diff(a[:, 1])) if L > 1 else None,
         "attention_cta_us": {"x_wait": us(a[1:, 1] - g[:-1, 6]) if L > 1 else None,
                              "norm_quant": us(a[:, 2] - a[:, 1]), "qkv_rows": us(a[:, 3] - a[:, 2]),
                              "kv_handover": us(a[:, 4] - a[:, 3]), "scores_exp": us(a[:, 5] - a[:, 4]),
-                             "softmax_sum": us(a[:, 6] - a[:, 5]), "values_quant_signal": us(a[:, 7] - a[:, 6])},
-        "projection_cta_us": {"o_wait_after_heads": us(g[:, 0] - a[:, 7]), "o": us(g[:, 1] - g[:, 0]),
-                              "gate_up_wait": us(g[:, 2] - g[:, 1]), "gate_up_norm_quant": us(g[:, 3] - g[:, 2]),
+                             "softmax_sum": us(a[:, 6] - a[:, 5]),
+                             "values_exchange_o": us(a[:, 7] - a[:, 6])},
+        "projection_cta_us": {"gate_up_wait_after_o": us(g[:, 2] - a[:, 7]),
+                              "gate_up_norm_quant": us(g[:, 3] - g[:, 2]),
                               "gate_up_rows": us(g[:, 4] - g[:, 3]), "down_wait": us(g[:, 5] - g[:, 4]),
                               "down": us(g[:, 6] - g[:, 5])},
         "lm_head_us": {"wait": float(h[0] - g[-1, 6]) / 1e3, "norm_quant": float(h[1] - h[0]) / 1e3,

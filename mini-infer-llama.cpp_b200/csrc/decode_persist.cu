@@ -13,15 +13,20 @@
 // What changes is the schedule. A step of the 0.5B shape is ~100 dependent
 // phases of a few microseconds each; as separate kernels every phase pays a
 // launch hand-off, and code that runs once per launch is fetched cold. Here:
-//  * CTAs [0, n_attn) are the attention CTAs, one thread-block cluster of
-//    n_rep + 1 per KV head (n_rep query CTAs + one k/v CTA, as qkv_attn.cu):
-//    per layer rms_norm + quantize, their Q|K|V rows, RoPE, the k/v hand-over
-//    through distributed shared memory, the KV append, the decode attention of
-//    one head and the O projection's quantize.
-//  * the other n_gemv CTAs run, per layer, the O projection (+ residual), the
-//    FFN gate/up (rms_norm + quantize prologue, SiLU * up + quantize epilogue)
-//    and the down projection (+ residual), each CTA its own rows; then all of
-//    them share the LM head and its argmax.
+//  * CTAs [0, n_attn) are the attention CTAs, ONE thread-block cluster of
+//    n_kv_head * (n_rep + 1) CTAs (per KV head n_rep query CTAs + one k/v CTA;
+//    16 for the 0.5B shape, a non-portable cluster size): per layer rms_norm
+//    + quantize, their Q|K|V rows, RoPE, the k/v hand-over through
+//    distributed shared memory, the KV append, the decode attention of one
+//    head and its quantize (the O projection's input node). Each head's
+//    Q8_0_ACT blocks go into every cluster CTA's shared memory (st.async,
+//    counted on an mbarrier), so the whole cluster then runs the O
+//    projection (+ residual) on its own, each CTA its rows, with no grid-wide
+//    hand-over between attention and O.
+//  * the other n_gemv CTAs run, per layer, the FFN gate/up (rms_norm +
+//    quantize prologue, SiLU * up + quantize epilogue) and the down
+//    projection (+ residual), each CTA its own rows; then the LM head and its
+//    argmax.
 //  * phases hand over through monotonic device counters (one per layer and
 //    phase): a producer CTA's threads store their outputs, the CTA
 //    synchronizes, one thread increments with release semantics; a consumer's thread 0
@@ -74,7 +79,7 @@ __host__ __device__ inline size_t groups_bytes(int G, int64_t K) {
 // [256,512) ring bookkeeping, then the activation region, then the weight
 // ring; query CTAs add the K / V tiles and the scores after their ring.
 struct PSmem {
-  size_t lay, aq, ad, xs, sq, spec, res, ring, total;
+  size_t lay, aq, ad, xs, sq, spec, res, oq, od, ring, total;
 };
 constexpr int kMaxLayers = 128;
 __host__ __device__ inline PSmem persist_smem(int64_t E, int64_t FF, int n_layer) {
@@ -95,6 +100,10 @@ __host__ __device__ inline PSmem persist_smem(int64_t E, int64_t FF, int n_layer
   off += up16((size_t)spec_sum_scratch_bytes(kNW, 2));
   L.res = off;
   off += (size_t)kMaxRes * 4;
+  L.oq = off;  // attention CTAs: the O projection's Q8_0_ACT input, from every head
+  off += up16((size_t)E);
+  L.od = off;
+  off += up16((size_t)(E / 32) * 4);
   L.ring = up128(off);
   L.total = L.ring;
   return L;
@@ -103,7 +112,7 @@ __host__ __device__ inline PSmem persist_smem(int64_t E, int64_t FF, int n_layer
 struct Role {
   bool attn, kv;
   int h, kvh;
-  int o_g0, o_g1;    // O and down rows, in groups of 4
+  int o_g0, o_g1;    // O rows (attention CTAs) or down rows (projection CTAs), in groups of 4
   int gu_b0, gu_b1;  // FFN activation blocks (64 packed gate/up rows each)
   int hd_g0, hd_g1;  // LM-head row groups
   int n_main;        // items before the LM head
@@ -121,8 +130,15 @@ __device__ inline ItemDesc item_desc(const PersistParams& p, const PersistLayer*
   ItemDesc d{};
   d.n = 1;
   if (it < r.n_main) {
-    if (r.attn) {
-      const PersistLayer& L = lay[it];
+    const int l = it >> 1, kind = it & 1;  // two items a layer
+    const PersistLayer& L = lay[l];
+    if (r.attn && kind == 1) {
+      d.w = L.o;
+      d.K = p.E;
+      d.npad = p.E;
+      d.g0[0] = r.o_g0;
+      d.G[0] = r.o_g1 - r.o_g0;
+    } else if (r.attn) {
       d.w = L.qkv;
       d.K = p.E;
       d.npad = p.qkv_npad;
@@ -138,15 +154,7 @@ __device__ inline ItemDesc item_desc(const PersistParams& p, const PersistLayer*
         d.G[0] = gd;
       }
     } else {
-      const int l = it / 3, kind = it - 3 * l;
-      const PersistLayer& L = lay[l];
       if (kind == 0) {
-        d.w = L.o;
-        d.K = p.E;
-        d.npad = p.E;
-        d.g0[0] = r.o_g0;
-        d.G[0] = r.o_g1 - r.o_g0;
-      } else if (kind == 1) {
         d.w = L.gateup;
         d.K = p.E;
         d.npad = p.gu_npad;
@@ -203,23 +211,27 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
   __shared__ int32_t red_i[kNW];
   __shared__ float misc[4];
   __shared__ int s_dead;
-  __shared__ float xl[kMaxRes], x2l[kMaxRes];  // this CTA's rows of x and x2 (the next residuals)
   __shared__ uint32_t s_ticket;
+  __shared__ __align__(16) int8_t ostage_q[128];  // a query CTA's head output, quantized
+  __shared__ float ostage_d[4];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int cta = (int)blockIdx.x, G = (int)gridDim.x;
   const int E = p.E, D = p.D, HKV = p.HKV, FF = p.FF;
-  const int n_rep = p.H / HKV, C = n_rep + 1;
+  const int n_rep = p.H / HKV, CK = n_rep + 1;  // CTAs per KV head
   const int nbE = E / 32, nbF = FF / 32;
   const PSmem L = persist_smem(E, FF, p.n_layer);
   uint64_t* bars = (uint64_t*)smem;      // kQ ring barriers
   uint64_t* bar_kv = bars + kQ;          // query CTAs: k / v from the k/v CTA
+  uint64_t* bar_o = bars + kQ + 1;       // attention CTAs: every head's output (the O input)
   RingState* rs = (RingState*)(smem + 256);
   int8_t* aq = (int8_t*)(smem + L.aq);
   float* ad = (float*)(smem + L.ad);
   float* xs = (float*)(smem + L.xs);
   float* sq = (float*)(smem + L.sq);
   float* res = (float*)(smem + L.res);
+  int8_t* oq = (int8_t*)(smem + L.oq);
+  float* od = (float*)(smem + L.od);
   uint8_t* ring = smem + L.ring;
   PersistLayer* lay = (PersistLayer*)(smem + L.lay);
   for (int i = tid; i < p.n_layer * (int)(sizeof(PersistLayer) / 8); i += kNT)
@@ -230,11 +242,14 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
   r.attn = cta < p.n_attn;
   const int W = p.n_gemv;
   if (r.attn) {
-    r.kvh = cta / C;
-    const int c = cta - r.kvh * C;
+    r.kvh = cta / CK;
+    const int c = cta - r.kvh * CK;
     r.kv = c == n_rep;
     r.h = r.kvh * n_rep + c;
-    r.n_main = p.n_layer;
+    const int GO = E / 4;
+    r.o_g0 = (int)((int64_t)cta * GO / p.n_attn);
+    r.o_g1 = (int)((int64_t)(cta + 1) * GO / p.n_attn);
+    r.n_main = 2 * p.n_layer;
     r.n_items = r.n_main;
   } else {
     const int wi = cta - p.n_attn;
@@ -245,7 +260,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
     r.gu_b1 = (int)((int64_t)(wi + 1) * nbF / W);
     r.hd_g0 = (int)((int64_t)wi * GV / W);
     r.hd_g1 = (int)((int64_t)(wi + 1) * GV / W);
-    r.n_main = 3 * p.n_layer;
+    r.n_main = 2 * p.n_layer;
     r.n_items = r.n_main + (p.with_head ? (r.hd_g1 - r.hd_g0 + kHeadChunkGroups - 1) / kHeadChunkGroups : 0);
   }
   const bool query = r.attn && !r.kv;
@@ -267,7 +282,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
   const int tr_attn = cta == 0 && tid == 0, tr_gemv = cta == p.n_attn && tid == 0;
 
   if (tid == 0) {
-    for (int i = 0; i <= kQ; i++) mbar_init(&bars[i], 1);
+    for (int i = 0; i <= kQ + 1; i++) mbar_init(&bars[i], 1);
     fence_mbar_init();
     rs->head = rs->tail = 0u;
     rs->next = rs->freed = 0;
@@ -364,7 +379,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
 #pragma unroll
     for (int u = 0; u < 4; u++) nw[u] = warp + u * kNW < nbE ? norm_w[(warp + u * kNW) * 32 + lane] : 0.0f;
   };
-  auto norm_quant = [&](const float* x, bool embed, const float (&nw)[4], float* x_out) {
+  auto norm_quant = [&](const float* x, bool embed, const float (&nw)[4]) {
     if (embed) {
       // mi_compute_get_rows on the Q8_0 embedding (ref src/ops_cpu.cpp:128-139)
       int tok = n_past < p.tokens_len ? p.tokens[n_past] : -1;
@@ -376,7 +391,6 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         const float v = __fmul_rn((float)packed_qs(p.embed, E, tok, k >> 5)[k & 31],
                                   packed_scale(p.embed, E, p.embed_npad, tok, k >> 5));
         xs[k] = v;
-        if (x_out) x_out[k] = v;
       }
     } else {
       for (int k = tid; k < E / 4; k += kNT) ((float4*)xs)[k] = __ldcg((const float4*)x + k);
@@ -459,12 +473,12 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
     }
     __syncthreads();
   };
-  // Rows of an item, 2 threads per row (K of the activation region):
-  // res[4g + r] = dot(row, act), the AVX2 lane order.
-  auto rows_2t = [&](const uint8_t* base, const ItemDesc& d) {
+  // Rows of an item, 2 threads per row, against the Q8_0_ACT vector a_q / a_d
+  // (K elements): res[4g + r] = dot(row, act), the AVX2 lane order.
+  auto rows_2t = [&](const uint8_t* base, const ItemDesc& d, const int8_t* a_q, const float* a_d) {
     const int K = (int)d.K, nb = K / 32, Gt = d.G[0] + (d.n > 1 ? d.G[1] : 0);
     const int gw = lane >> 3, r4 = (lane >> 1) & 3, hh = lane & 1;
-    const uint4* aq16 = (const uint4*)aq;
+    const uint4* aq16 = (const uint4*)a_q;
     for (int g0 = warp * 4; g0 < Gt; g0 += kNW * 4) {
       const int g = g0 + gw;
       const bool valid = g < Gt;
@@ -483,7 +497,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       for (int i = 0; i < nb; i++) {
         const uint4 w = gq[i * 8 + (lane & 7)];
         const uint4 a = aq16[i * 2 + hh];
-        const float dxdy = __fmul_rn(__half2float(gd[i * 4 + r4]), ad[i]);
+        const float dxdy = __fmul_rn(__half2float(gd[i * 4 + r4]), a_d[i]);
         a0 = __fmaf_rn(__int2float_rn(__dp4a((int)w.x, (int)a.x, 0)), dxdy, a0);
         a1 = __fmaf_rn(__int2float_rn(__dp4a((int)w.y, (int)a.y, 0)), dxdy, a1);
         a2 = __fmaf_rn(__int2float_rn(__dp4a((int)w.z, (int)a.z, 0)), dxdy, a2);
@@ -516,7 +530,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
   };
 
   unsigned long long* const ctr = p.ctr;
-  const unsigned long long tH = (epoch + 1ull) * (unsigned long long)p.H;
+  const unsigned long long tA = (epoch + 1ull) * (unsigned long long)p.n_attn;
   const unsigned long long tW = (epoch + 1ull) * (unsigned long long)W;
 
   if (r.attn) {
@@ -572,6 +586,11 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
           }
         }
       };
+      // every head's output of this layer, into oq / od (phase l of bar_o;
+      // the previous phase completed before this CTA's O rows of layer l-1,
+      // and no head of layer l can finish before every attention CTA has
+      // stored its x2 rows of layer l-1)
+      if (tid == 0) mbar_arrive_expect_tx(bar_o, (uint32_t)(p.H * (D + 4 * (D / 32))));
       if (query) {
         if (tid == 0) mbar_arrive_expect_tx(bar_kv, (uint32_t)(2 * D * 4));
         load_kv(0, min(KT, n_kv), true, true);
@@ -581,13 +600,13 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       // ---- x of this layer: the embedding (layer 0) or the down output ----
       if (l > 0) wait_ctr(&ctr[(size_t)(l - 1) * 4 + 3], tW);
       if (tr_attn) pstamp(p, 2 * l, 1);
-      norm_quant(p.x, l == 0, nw, l == 0 && cta == 0 ? p.x : nullptr);
+      norm_quant(p.x, l == 0, nw);  // xs keeps x: the O rows' residual
       if (tr_attn) pstamp(p, 2 * l, 2);
       // ---- the CTA's q rows, or k and v rows ----
-      const ItemDesc d = item_desc(p, lay, r, l);
-      const uint8_t* wbase = wait_item(l);
-      rows_2t(wbase, d);  // ends with a CTA barrier: the item may be reused
-      free_item(l);
+      const ItemDesc d = item_desc(p, lay, r, 2 * l);
+      const uint8_t* wbase = wait_item(2 * l);
+      rows_2t(wbase, d, aq, ad);  // ends with a CTA barrier: the item may be reused
+      free_item(2 * l);
       if (tr_attn) pstamp(p, 2 * l, 3);
       // ---- bias, RoPE (ref src/ops_cpu.cpp:286-297), v ----
       if (tid < half) {
@@ -599,14 +618,16 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       if (r.kv && tid < D) vr[tid] = __fadd_rn(res[D + tid], b_v);
       __syncthreads();
       if (r.kv) {
-        // k / v into every query CTA of the cluster (st.async, counted on the
-        // receiver's bar_kv), then the KV-cache append
+        // k / v into the query CTAs of this KV head (cluster ranks
+        // kvh * (n_rep + 1) + c; st.async, counted on the receiver's bar_kv),
+        // then the KV-cache append
         if (!s_dead) {
           const int per = D >> 1;
           for (int e = tid; e < n_rep * per; e += kNT) {
             const int c = e / per, i4 = e - c * per;
+            const uint32_t rk = (uint32_t)(r.kvh * CK + c);
             const float* src = i4 < D / 4 ? kr + 4 * i4 : vr + 4 * (i4 - D / 4);
-            dsmem_store_async(dsmem_addr(src, (uint32_t)c), *(const float4*)src, dsmem_addr(bar_kv, (uint32_t)c));
+            dsmem_store_async(dsmem_addr(src, rk), *(const float4*)src, dsmem_addr(bar_kv, rk));
           }
         }
         if (tid < D) {
@@ -614,8 +635,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
           cache_v[((size_t)n_past * HKV + r.kvh) * D + tid] = vr[tid];
         }
         __syncthreads();
-        continue;
-      }
+      } else {
       // ---- query CTA: the decode attention of head h ----
       if (!s_dead && !mbar_wait_bounded(bar_kv, (uint32_t)(l & 1), p.err)) s_dead = 1;
       if (n_past < KT && tid < D) {
@@ -731,50 +751,56 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         }
       }
       // the O projection's quantize node (src/ops_cpu.cpp:462-479) for this
-      // head's outputs: warp w holds block h*D/32 + w
+      // head's outputs (warp w holds block h*D/32 + w), then the blocks into
+      // every attention CTA's oq / od: D/4 words of quants and D/32 scales
+      // per receiver, counted on its bar_o
       if (tid < D) {
         float dq;
-        const int8_t q = quantize_lane(acc, &dq);
-        uint8_t* blk = p.attn_q + ((size_t)r.h * (D / 32) + (tid >> 5)) * 36;
-        ((int8_t*)blk)[4 + lane] = q;
-        if (lane == 0) *(float*)blk = dq;
+        ostage_q[tid] = quantize_lane(acc, &dq);
+        if (lane == 0) ostage_d[tid >> 5] = dq;
       }
-      signal_ctr(&ctr[(size_t)l * 4 + 0]);
-      if (tr_attn) pstamp(p, 2 * l, 7);
+      __syncthreads();
+      if (!s_dead) {
+        const int nw = D / 4 + D / 32;
+        for (int e = tid; e < p.n_attn * nw; e += kNT) {
+          const int rk = e / nw, w = e - rk * nw;
+          const bool quant = w < D / 4;
+          const uint32_t v = quant ? ((const uint32_t*)ostage_q)[w] : __float_as_uint(ostage_d[w - D / 4]);
+          const void* dst = quant ? (const void*)(oq + r.h * D + 4 * w) : (const void*)(od + r.h * (D / 32) + (w - D / 4));
+          dsmem_store_async_u32(dsmem_addr(dst, (uint32_t)rk), v, dsmem_addr(bar_o, (uint32_t)rk));
+        }
+      }
+      }  // query CTA
+      // ---- O projection + residual on the cluster: x2 = x + W_o . attn ----
+      {
+        const ItemDesc dO = item_desc(p, lay, r, 2 * l + 1);
+        const int rows = 4 * dO.G[0], r0 = 4 * dO.g0[0];
+        if (!s_dead && !mbar_wait_bounded(bar_o, (uint32_t)(l & 1), p.err)) s_dead = 1;
+        const uint8_t* wb = wait_item(2 * l + 1);
+        if (rows > 0) rows_2t(wb, dO, oq, od);
+        for (int i = tid; i < rows; i += kNT) p.x2[r0 + i] = __fadd_rn(xs[r0 + i], res[i]);
+        signal_ctr(&ctr[(size_t)l * 4 + 1]);
+        free_item(2 * l + 1);
+        if (tr_attn) pstamp(p, 2 * l, 7);
+      }
     }
   } else {
     // ===================== projection CTAs =====================
     for (int l = 0; l < p.n_layer; l++) {
       const PersistLayer& Ly = lay[l];
-      // ---- O projection + residual: x2 = x + W_o . attn ----
-      {
-        const ItemDesc d = item_desc(p, lay, r, 3 * l);
-        const int rows = 4 * d.G[0], r0 = 4 * d.g0[0];
-        wait_ctr(&ctr[(size_t)l * 4 + 0], tH);
-        if (tr_gemv) pstamp(p, 2 * l + 1, 0);
-        load_act(p.attn_q, nbE);
-        const uint8_t* wb = wait_item(3 * l);
-        if (rows > 0) rows_2t(wb, d);
-        for (int i = tid; i < rows; i += kNT) {
-          const float v = __fadd_rn(l == 0 ? __ldcg(p.x + r0 + i) : xl[i], res[i]);
-          x2l[i] = v;
-          p.x2[r0 + i] = v;
-        }
-        signal_ctr(&ctr[(size_t)l * 4 + 1]);
-        free_item(3 * l);
-        if (tr_gemv) pstamp(p, 2 * l + 1, 1);
-      }
       // ---- gate/up: rms_norm(x2) * ffn_norm, quantize; silu(gate) * up, quantize ----
       {
-        const ItemDesc d = item_desc(p, lay, r, 3 * l + 1);
+        const ItemDesc d = item_desc(p, lay, r, 2 * l);
+        if (tr_gemv) pstamp(p, 2 * l + 1, 0);
         float nw[4];
         load_nw(Ly.ffn_norm, nw);
-        wait_ctr(&ctr[(size_t)l * 4 + 1], tW);
+        if (tr_gemv) pstamp(p, 2 * l + 1, 1);
+        wait_ctr(&ctr[(size_t)l * 4 + 1], tA);
         if (tr_gemv) pstamp(p, 2 * l + 1, 2);
-        norm_quant(p.x2, false, nw, nullptr);
+        norm_quant(p.x2, false, nw);  // xs keeps x2: the down rows' residual
         if (tr_gemv) pstamp(p, 2 * l + 1, 3);
-        const uint8_t* wb = wait_item(3 * l + 1);
-        if (d.G[0] > 0) rows_2t(wb, d);
+        const uint8_t* wb = wait_item(2 * l);
+        if (d.G[0] > 0) rows_2t(wb, d, aq, ad);
         // each 64 packed rows are the gate / up rows of one 32-element block:
         // act[a] = silu(gate) * up, then the down projection's quantize node
         for (int j = warp; j < r.gu_b1 - r.gu_b0; j += kNW) {
@@ -788,28 +814,24 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
           if (lane == 0) *(float*)blk = dq;
         }
         signal_ctr(&ctr[(size_t)l * 4 + 2]);
-        free_item(3 * l + 1);
+        free_item(2 * l);
         if (tr_gemv) pstamp(p, 2 * l + 1, 4);
       }
       // ---- down projection + residual: x = x2 + W_down . act ----
       {
-        const ItemDesc d = item_desc(p, lay, r, 3 * l + 2);
+        const ItemDesc d = item_desc(p, lay, r, 2 * l + 1);
         const int rows = 4 * d.G[0], r0 = 4 * d.g0[0];
         wait_ctr(&ctr[(size_t)l * 4 + 2], tW);
         if (tr_gemv) pstamp(p, 2 * l + 1, 5);
         load_act(p.act_q, nbF);
-        const uint8_t* wb = wait_item(3 * l + 2);
+        const uint8_t* wb = wait_item(2 * l + 1);
         if (rows > 0) {
           if (FAST && rows * kNW <= E) rows_8t_split(wb, d);
           else rows_8t(wb, d);
         }
-        for (int i = tid; i < rows; i += kNT) {
-          const float v = __fadd_rn(x2l[i], res[i]);
-          xl[i] = v;
-          p.x[r0 + i] = v;
-        }
+        for (int i = tid; i < rows; i += kNT) p.x[r0 + i] = __fadd_rn(xs[r0 + i], res[i]);
         signal_ctr(&ctr[(size_t)l * 4 + 3]);
-        free_item(3 * l + 2);
+        free_item(2 * l + 1);
         if (tr_gemv) pstamp(p, 2 * l + 1, 6);
       }
     }
@@ -819,7 +841,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       load_nw(p.out_norm, nw);
       wait_ctr(&ctr[(size_t)(p.n_layer - 1) * 4 + 3], tW);
       if (tr_gemv) pstamp(p, 2 * p.n_layer, 0);
-      norm_quant(p.x, false, nw, nullptr);
+      norm_quant(p.x, false, nw);
       if (tr_gemv) pstamp(p, 2 * p.n_layer, 1);
       float bv = -INFINITY;
       int32_t bi = 0x7fffffff;
@@ -833,7 +855,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
           t_wait += now - t_mark;
           t_mark = now;
         }
-        rows_2t(wb, d);  // ends with a CTA barrier: the item may be reused
+        rows_2t(wb, d, aq, ad);  // ends with a CTA barrier: the item may be reused
         if (tr_gemv) {
           const uint64_t now = globaltimer_ns();
           t_rows += now - t_mark;
@@ -959,16 +981,21 @@ PersistPlan plan_persist(int64_t E, int32_t D, int32_t H, int32_t HKV, int64_t F
   if (g_optin <= 0 || D < 32 || D > 128 || D % 32 != 0 || HKV <= 0 || H % HKV != 0 || E % 64 != 0 ||
       E > 1024 || E != (int64_t)H * D || FF % 64 != 0 || FF < 64 || V <= 0 || n_ctx <= 0)
     return pl;
-  const int32_t n_rep = H / HKV, C = n_rep + 1;
-  if (C > 8) return pl;
+  // one cluster for every head: n_kv_head * (n_rep + 1) CTAs, at most 16 (a
+  // non-portable cluster size on B200)
+  const int32_t n_rep = H / HKV, C = HKV * (n_rep + 1);
+  if (C > 16) return pl;
   if (n_layer <= 0 || n_layer > kMaxLayers) return pl;
   const PSmem L = persist_smem(E, FF, n_layer);
   const size_t avail = (size_t)g_optin;
   if (avail <= L.ring + 4096) return pl;
   const size_t ring_gemv = (avail - L.ring) / 128 * 128;
-  // query CTAs: a ring for one item of their q rows, then the K / V tiles
-  const size_t ring_attn = groups_bytes(D / 4, E);
-  const size_t kv_item = 2 * groups_bytes(D / 4, E);
+  // query CTAs: a ring for the item of their q rows and the item of their O
+  // rows, then the K / V tiles; k/v CTAs: the k and v rows and the O rows
+  const int OG = (int)((E / 4 + C - 1) / C);
+  if (OG * 4 > kMaxRes) return pl;
+  const size_t ring_attn = groups_bytes(D / 4, E) + groups_bytes(OG, E);
+  const size_t kv_item = 2 * groups_bytes(D / 4, E) + groups_bytes(OG, E);
   const size_t sc = n_ctx <= kScoresOnChipMax ? up16((size_t)n_ctx * 4) + kChainSlackBytes : 0;
   const size_t row = (size_t)(2 * D + 1) * 4;
   if (ring_gemv < kv_item || ring_gemv < ring_attn + sc + 32 * row) return pl;
@@ -999,11 +1026,11 @@ PersistPlan plan_persist(int64_t E, int32_t D, int32_t H, int32_t HKV, int64_t F
   }
   n_clusters = std::min(n_clusters, n_fast);
   n_clusters = std::min(n_clusters, num_sms / C);
-  const int32_t n_attn = HKV * C;
+  const int32_t n_attn = C;
   const int32_t grid = C * n_clusters;
   const int32_t n_gemv = grid - n_attn;
   // every projection CTA keeps at most two 32-element FFN blocks (the ring
-  // and kMaxRes hold 128 gate/up rows) and at least one LM-head row group
+  // and kMaxRes hold 128 gate/up rows)
   if (n_gemv < 8 || (FF / 32 + n_gemv - 1) / n_gemv > 2 || (E / 4 + n_gemv - 1) / n_gemv * 4 > kMaxRes)
     return pl;
   // the largest item of a projection CTA must fit its ring

@@ -161,6 +161,14 @@ __device__ __forceinline__ void dsmem_store_async(uint32_t addr, float4 v, uint3
                : "memory");
 }
 
+// One 32-bit word into another CTA's shared memory, counted (4 bytes) on its
+// mbarrier `bar` (shared::cluster addresses, as dsmem_store_async).
+__device__ __forceinline__ void dsmem_store_async_u32(uint32_t addr, uint32_t v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr), "r"(v),
+               "r"(bar)
+               : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // Tensor-parallel exchange words: value bits | tag << 32, written with one
 // 64-bit store (single-copy atomic), so a reader that sees the step's tag

@@ -239,7 +239,6 @@ struct PersistParams {
   const float2* rope;          // [pos][D/2]
   float* x;                    // residual stream (layer input / down output)
   float* x2;                   // residual stream after attention
-  uint8_t* attn_q;             // Q8_0_ACT: the O projection's input
   uint8_t* act_q;              // Q8_0_ACT: the down projection's input
   float* logits;
   float* scores;               // [H][n_ctx] when the scores do not fit on chip
@@ -254,10 +253,10 @@ struct PersistParams {
   int32_t* err;
   uint32_t* ticket;            // CTAs finished with the step (the last one closes it)
   unsigned long long* epoch;   // steps completed since the counters were zeroed
-  unsigned long long* ctr;     // [n_layer][4] hand-over counters
-  // schedule: CTAs [0, n_attn) run the attention of one head (clusters of
-  // n_rep + 1: n_rep query heads and one k/v CTA), the other n_gemv CTAs the
-  // O, gate/up and down projections; all of them share the LM head
+  unsigned long long* ctr;     // [n_layer][4] hand-over counters (1: x2, 2: act, 3: x stored)
+  // schedule: CTAs [0, n_attn) are one cluster (per KV head n_rep query
+  // CTAs and one k/v CTA) running the attention and the O projection; the
+  // other n_gemv CTAs the gate/up and down projections and the LM head
   int32_t n_attn, n_gemv;
   int32_t kv_tile, scores_in_smem;
   int32_t ring_gemv, ring_attn;  // weight-ring bytes of the two roles

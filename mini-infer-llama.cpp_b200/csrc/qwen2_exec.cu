@@ -576,7 +576,6 @@ int enqueue_step(mi_cuda_kv_cache* kv, bool with_head, int32_t* n_kernels) {
     q.rope = kv->rope;
     q.x = kv->x;
     q.x2 = kv->x2;
-    q.attn_q = kv->attn_q;
     q.act_q = kv->act_q;
     q.logits = kv->logits;
     q.scores = kv->scores;

@@ -449,9 +449,10 @@ class KVCache:
         prologue done, epilogue start, then the kernel's own phase marks
         (attention: scores, exp, sum, KV done). Persistent step (one kernel):
         two slots per layer -- attention CTA 0 (layer start, x ready, prologue
-        done, rows done, k/v received, exp done, sum done, head signalled) and
-        the first projection CTA (O wait done, O signalled, gate/up wait done,
-        its prologue done, gate/up signalled, down wait done, down signalled)
+        done, rows done, k/v received, exp done, sum done, O rows signalled)
+        and the first projection CTA (layer start, norm weights loaded,
+        gate/up wait done, its prologue done, gate/up signalled, down wait
+        done, down signalled)
         -- then the LM head (wait done, prologue done, rows done, step closed,
         then the first projection CTA's totals over its LM-head items: ns
         waiting for ring items, ns in the rows, ns issuing copies, items)."""

@@ -130,7 +130,7 @@ def test_step_trace(mc, model_path, qkv_attn_path):
         attn, proj = t[0:2 * L:2], t[1:2 * L:2]
         assert np.all(attn > 0) and np.all(proj[:, :7] > 0) and np.all(t[-1, :3] > 0)
         assert np.all(np.diff(attn, axis=1) >= 0) and np.all(np.diff(proj[:, :7], axis=1) >= 0)
-        assert np.all(proj[:, 0] >= attn[:, 7] - 2000)   # O starts after the heads are done
+        assert np.all(proj[:, 2] >= attn[:, 7] - 2000)   # gate/up starts after the cluster's O rows
         assert np.all(attn[1:, 1] >= proj[:-1, 6] - 2000)  # a layer starts after the previous down
         assert t[-1, 2] - attn[0, 0] < 10_000_000
     else:
