@@ -606,7 +606,6 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       const ItemDesc d = item_desc(p, lay, r, 2 * l);
       const uint8_t* wbase = wait_item(2 * l);
       rows_2t(wbase, d, aq, ad);  // ends with a CTA barrier: the item may be reused
-      free_item(2 * l);
       if (tr_attn) pstamp(p, 2 * l, 3);
       // ---- bias, RoPE (ref src/ops_cpu.cpp:286-297), v ----
       if (tid < half) {
@@ -771,6 +770,9 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         }
       }
       }  // query CTA
+      // the q (or k and v) rows' ring item is freed only now: issuing the
+      // next copy holds thread 0 for a while, here while the heads finish
+      free_item(2 * l);
       // ---- O projection + residual on the cluster: x2 = x + W_o . attn ----
       {
         const ItemDesc dO = item_desc(p, lay, r, 2 * l + 1);
