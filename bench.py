@@ -74,13 +74,11 @@ PERIOD = N_PREDICT - 1  # decode forwards per generated sequence
 METRIC = "decode tok/s (0.5B-shape Q8_0, ctx 2048)"
 PUBLISHED_BEST = 64.035  # reference Q8_0 decode tok/s, 4 threads (reference README.md:106)
 # DRAM bytes (read + write) of one decode step: dram__bytes_read.sum +
-# dram__bytes_write.sum summed over the 97 launches of one step at n_kv = 33,
-# from an ncu capture of this build's decode graph (ncu flushes the caches
-# before every replayed launch, so operands a real step finds in L2 count as
-# DRAM reads here); profiles/decode_step_qwen2_05b.md gives the command and the
-# per-kernel figures.
-TRAFFIC_PER_STEP = 564_573_440
-TRAFFIC_SOURCE = "ncu dram__bytes_read+write, 97 launches of one step at n_kv 33 (caches flushed per launch)"
+# dram__bytes_write.sum of one launch of the persistent step kernel (the whole
+# step) at n_kv = 34, from an ncu capture of this build;
+# profiles/decode_step_qwen2_05b.md gives the command and the figures.
+TRAFFIC_PER_STEP = 531_213_824
+TRAFFIC_SOURCE = "ncu dram__bytes_read+write of one persistent-step launch at n_kv 34 (527.6 MB read, 3.6 MB written)"
 
 
 def step_bytes(hp, n_kv: int) -> int:
@@ -986,7 +984,9 @@ def decode_measure(args, dist, rank: int, world: int, local: int) -> dict:
         "config": decode_config(), "parallelism": f"replicas x{world}",
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": TRAFFIC_PER_STEP, "traffic_source": TRAFFIC_SOURCE,
-                     "peak_kind": peak_kind, "kernel": f"decode step graph ({kernels} kernels)",
+                     "peak_kind": peak_kind,
+                     "kernel": ("persistent decode step (one launch per token)" if kernels == 1
+                                else f"decode step graph ({kernels} kernels)"),
                      "bytes_per_step": total_bytes / args.steps},
         "e2e": {"value": e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": 4 + 32, "d2h_bytes_per_step": 4 + 4,
                 "api": "mi_cuda_qwen2_forward (token in) + mi_cuda_qwen2_last_token (greedy token out)"},
