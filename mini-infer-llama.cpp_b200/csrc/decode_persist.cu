@@ -770,9 +770,6 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         }
       }
       }  // query CTA
-      // the q (or k and v) rows' ring item is freed only now: issuing the
-      // next copy holds thread 0 for a while, here while the heads finish
-      free_item(2 * l);
       // ---- O projection + residual on the cluster: x2 = x + W_o . attn ----
       {
         const ItemDesc dO = item_desc(p, lay, r, 2 * l + 1);
@@ -782,6 +779,10 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         if (rows > 0) rows_2t(wb, dO, oq, od);
         for (int i = tid; i < rows; i += kNT) p.x2[r0 + i] = __fadd_rn(xs[r0 + i], res[i]);
         signal_ctr(&ctr[(size_t)l * 4 + 1]);
+        // the layer's two ring items are freed only after its last signal:
+        // issuing a copy holds thread 0 for up to ~0.5 us, which on the
+        // slowest CTA would delay every consumer of its signal
+        free_item(2 * l);
         free_item(2 * l + 1);
         if (tr_attn) pstamp(p, 2 * l, 7);
       }
@@ -816,7 +817,6 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
           if (lane == 0) *(float*)blk = dq;
         }
         signal_ctr(&ctr[(size_t)l * 4 + 2]);
-        free_item(2 * l);
         if (tr_gemv) pstamp(p, 2 * l + 1, 4);
       }
       // ---- down projection + residual: x = x2 + W_down . act ----
@@ -833,6 +833,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         }
         for (int i = tid; i < rows; i += kNT) p.x[r0 + i] = __fadd_rn(xs[r0 + i], res[i]);
         signal_ctr(&ctr[(size_t)l * 4 + 3]);
+        free_item(2 * l);  // (after the layer's last signal, as above)
         free_item(2 * l + 1);
         if (tr_gemv) pstamp(p, 2 * l + 1, 6);
       }
