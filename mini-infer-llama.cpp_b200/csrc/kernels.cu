@@ -999,6 +999,7 @@ constexpr int kAttnSmemBudget = 140 * 1024;  // dynamic shared memory per CTA (o
 // loaded before the dependency wait (192 positions at head_dim 128).
 constexpr int kExecAttnSmemBudget = 210 * 1024;
 constexpr int kScoresSmemMax = 8192;         // scores kept on chip up to this many positions
+constexpr int kLongMin = 512;                // op mode, one query: attn_long.cu from this many positions
 }  // namespace
 
 namespace {
@@ -1015,7 +1016,10 @@ cudaError_t set_attn_smem(int optin) {
 }
 }  // namespace
 
+int g_attn_optin = 0;  // the device's opt-in shared memory per block (set once)
+
 cudaError_t prepare_attn_kernels(int optin) {
+  g_attn_optin = optin;
   cudaError_t e = set_attn_smem<true, false, false>(optin);
   if (e == cudaSuccess) e = set_attn_smem<true, false, true>(optin);
   if (e == cudaSuccess) e = set_attn_smem<false, false, false>(optin);
@@ -1053,6 +1057,14 @@ cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t
   cfg.numAttrs = pdl ? 1 : 0;
   if (exec_mode && tp) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<true, false, true>, q);
   if (exec_mode) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<true, false, false>, q);
+  // one query of at least kLongMin positions: the kernels that spread the
+  // independent parts over the GPU (attn_long.cu), same order of every sum
+  // (one CTA per head walks every position itself: 55 us at 1024 positions,
+  // 3 ms at 32768)
+  if (n_queries <= 1 && p.n_kv_fixed >= kLongMin && p.out && !p.act_out && !p.act_qs &&
+      ((uintptr_t)p.cache_k % 16 == 0) && ((uintptr_t)p.cache_v % 16 == 0) &&
+      attn_long_fits(p.head_dim, p.n_head, p.n_head_kv, p.n_kv_fixed, g_attn_optin))
+    return launch_attn_decode_long(q, s);
   if (q.scores_in_smem && max_kv >= kSpecSumMin)
     return cudaLaunchKernelEx(&cfg, attn_decode_kernel<false, true, false>, q);
   return cudaLaunchKernelEx(&cfg, attn_decode_kernel<false, false, false>, q);

@@ -141,6 +141,12 @@ struct AttnParams {
 };
 cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t s, bool pdl,
                                bool tp = false, int32_t n_queries = 1);
+// Exact decode attention for one query past the on-chip score limit, spread
+// over the GPU (attn_long.cu): scores, softmax (ordered denominator by
+// spec_ordered_sum) and the ordered value chains as three kernels; uses
+// p.scores [n_head][scores_stride] for the scores and then the probabilities.
+bool attn_long_fits(int64_t head_dim, int64_t n_head, int64_t n_head_kv, int64_t n_kv, int optin);
+cudaError_t launch_attn_decode_long(const AttnParams& p, cudaStream_t s);
 
 // Decode attention split over positions (attn_split.cu): a fast mode that
 // regroups the softmax and value sums (not bit-exact). part holds

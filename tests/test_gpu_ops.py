@@ -220,7 +220,7 @@ def test_attention_ops_separately(mc, S, torch_cuda, n_kv, n_tokens):
     assert np.array_equal(bits(o.cpu()), bits(o_w))
 
 
-@pytest.mark.parametrize("n_kv", [1, 128, 300, 1024, 4096, 8192, 32768])
+@pytest.mark.parametrize("n_kv", [1, 128, 300, 1024, 4096, 8192, 8193, 20001, 32768])
 def test_attention_decode_config2(mc, S, torch_cuda, n_kv):
     torch = torch_cuda
     rng = np.random.default_rng(n_kv)
@@ -230,6 +230,23 @@ def test_attention_decode_config2(mc, S, torch_cuda, n_kv):
     v = rng.standard_normal((n_kv, HKV, D), dtype=np.float32)
     _, _, want = S.attention(q, k, v, HKV, n_kv - 1, 1, 0.125)
     got = mc.attention_decode(dev(torch, q[0]), dev(torch, k), dev(torch, v), HKV, n_kv, 0.125).cpu().numpy()
+    assert np.array_equal(bits(got), bits(want[0]))
+
+
+@pytest.mark.parametrize("n_kv,H,HKV,D", [(9001, 28, 4, 128), (12000, 16, 16, 32)])
+def test_attention_decode_long_context_shapes(mc, S, torch_cuda, n_kv, H, HKV, D):
+    """Past 8192 positions one query's exact attention runs as three kernels
+    (scores over many CTAs, the ordered denominator by the speculative sum,
+    the ordered value chains): bit-identical to the reference order for other
+    head shapes too (7B widths; one query head per KV head, head_dim 32)."""
+    torch = torch_cuda
+    rng = np.random.default_rng(n_kv + D)
+    q = rng.standard_normal((1, H, D), dtype=np.float32)
+    k = rng.standard_normal((n_kv, HKV, D), dtype=np.float32)
+    v = rng.standard_normal((n_kv, HKV, D), dtype=np.float32)
+    scale = float(np.float32(1.0 / np.sqrt(D)))
+    _, _, want = S.attention(q, k, v, HKV, n_kv - 1, 1, scale)
+    got = mc.attention_decode(dev(torch, q[0]), dev(torch, k), dev(torch, v), HKV, n_kv, scale).cpu().numpy()
     assert np.array_equal(bits(got), bits(want[0]))
 
 
