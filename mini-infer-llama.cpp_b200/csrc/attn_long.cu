@@ -31,7 +31,7 @@ namespace {
 constexpr int kLongNT = 256;
 constexpr int kSoftNT = 1024;   // softmax CTA: the exponentials and 32 speculative segments
 constexpr int kScoreTile = 128;   // positions per score CTA
-constexpr int kValChunk = 1024;   // positions per value chunk (double-buffered)
+constexpr int kValChunk = 2048;   // positions per value chunk (double-buffered; a multiple of 32)
 constexpr int kValOut = 8;        // output chains per value CTA
 
 // ---- 1. scores ----
@@ -161,18 +161,47 @@ __global__ void __launch_bounds__(kLongNT) attn_long_values_kernel(const float* 
       // out[o] = sum_t V[t][o] * p[t], t ascending (src/ops_cpu.cpp:402-406)
       const float* v = vbuf(b) + tid;
       const float* pp = pbuf(b);
-      int t = 0;
-      for (; t + 16 <= rows; t += 16) {
-        float a[16], w[16];
+      if (rows == kValChunk) {
+        // two register batches of 16 positions, ping-pong: the loads of the
+        // next batch are in flight while the current batch's adds run
+        float a0[16], w0[16], a1[16], w1[16];
 #pragma unroll
         for (int u = 0; u < 16; u++) {
-          a[u] = v[(t + u) * kValOut];
-          w[u] = pp[t + u];
+          a0[u] = v[u * kValOut];
+          w0[u] = pp[u];
         }
+        for (int t = 0; t < kValChunk; t += 32) {
 #pragma unroll
-        for (int u = 0; u < 16; u++) acc = __fadd_rn(acc, __fmul_rn(a[u], w[u]));
+          for (int u = 0; u < 16; u++) {
+            a1[u] = v[(t + 16 + u) * kValOut];
+            w1[u] = pp[t + 16 + u];
+          }
+#pragma unroll
+          for (int u = 0; u < 16; u++) acc = __fadd_rn(acc, __fmul_rn(a0[u], w0[u]));
+          if (t + 32 < kValChunk) {
+#pragma unroll
+            for (int u = 0; u < 16; u++) {
+              a0[u] = v[(t + 32 + u) * kValOut];
+              w0[u] = pp[t + 32 + u];
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 16; u++) acc = __fadd_rn(acc, __fmul_rn(a1[u], w1[u]));
+        }
+      } else {
+        int t = 0;
+        for (; t + 16 <= rows; t += 16) {
+          float a[16], w[16];
+#pragma unroll
+          for (int u = 0; u < 16; u++) {
+            a[u] = v[(t + u) * kValOut];
+            w[u] = pp[t + u];
+          }
+#pragma unroll
+          for (int u = 0; u < 16; u++) acc = __fadd_rn(acc, __fmul_rn(a[u], w[u]));
+        }
+        for (; t < rows; t++) acc = __fadd_rn(acc, __fmul_rn(v[t * kValOut], pp[t]));
       }
-      for (; t < rows; t++) acc = __fadd_rn(acc, __fmul_rn(v[t * kValOut], pp[t]));
     }
     __syncthreads();  // buffer b is refilled by the next iteration's issue
   }
