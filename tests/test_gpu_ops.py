@@ -220,7 +220,7 @@ def test_attention_ops_separately(mc, S, torch_cuda, n_kv, n_tokens):
     assert np.array_equal(bits(o.cpu()), bits(o_w))
 
 
-@pytest.mark.parametrize("n_kv", [1, 128, 300, 1024, 4096, 8192, 8193, 20001, 32768])
+@pytest.mark.parametrize("n_kv", [1, 128, 300, 511, 512, 1024, 4096, 8192, 8193, 20001, 32768, 60001])
 def test_attention_decode_config2(mc, S, torch_cuda, n_kv):
     torch = torch_cuda
     rng = np.random.default_rng(n_kv)
