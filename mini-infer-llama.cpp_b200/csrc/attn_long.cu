@@ -217,6 +217,19 @@ size_t softmax_smem(int n_kv) {
 
 }  // namespace
 
+// The kernels' shared-memory attributes, once per device (at its init): the
+// largest sizes attn_long_fits admits.
+cudaError_t prepare_attn_long_kernels(int optin) {
+  cudaError_t e = cudaFuncSetAttribute(attn_long_values_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kValSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attn_long_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(((size_t)16 * 256 + (size_t)kScoreTile * 257) * 4));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attn_long_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - 1024);
+  return e;
+}
+
 bool attn_long_fits(int64_t head_dim, int64_t n_head, int64_t n_head_kv, int64_t n_kv, int optin) {
   return head_dim % kValOut == 0 && head_dim <= 256 && n_head_kv > 0 && n_head % n_head_kv == 0 &&
          n_head / n_head_kv <= 16 && n_kv > 0 && (int64_t)softmax_smem((int)n_kv) <= (int64_t)optin - 1024;
@@ -227,24 +240,7 @@ cudaError_t launch_attn_decode_long(const AttnParams& p, cudaStream_t s) {
   const int n_rep = H / HKV;
   const size_t sc_smem = ((size_t)n_rep * D + (size_t)kScoreTile * (D + 1)) * 4;
   const size_t sm_smem = softmax_smem(n_kv);
-  static size_t set_sc = 0, set_sm = 0;  // (attributes once per larger size; a host call costs microseconds)
-  static bool set_val = false;
   cudaError_t e = cudaSuccess;
-  if (!set_val) {
-    e = cudaFuncSetAttribute(attn_long_values_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kValSmem);
-    if (e != cudaSuccess) return e;
-    set_val = true;
-  }
-  if (sc_smem > set_sc) {
-    e = cudaFuncSetAttribute(attn_long_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sc_smem);
-    if (e != cudaSuccess) return e;
-    set_sc = sc_smem;
-  }
-  if (sm_smem > set_sm) {
-    e = cudaFuncSetAttribute(attn_long_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_smem);
-    if (e != cudaSuccess) return e;
-    set_sm = sm_smem;
-  }
   attn_long_scores_kernel<<<dim3((unsigned)((n_kv + kScoreTile - 1) / kScoreTile), (unsigned)HKV), kLongNT, sc_smem,
                             s>>>(p.q_rot, p.cache_k, D, H, HKV, n_kv, p.scale, p.scores, p.scores_stride);
   e = cudaGetLastError();

@@ -259,6 +259,19 @@ __global__ void __launch_bounds__(kCombineNT) attn_split_combine_kernel(const fl
 
 }  // namespace
 
+// The split kernels' shared-memory attribute, once per device (at its init).
+cudaError_t prepare_attn_split_kernels() {
+  const int most = (int)split_smem_bytes(kSplitMaxD, kSplitMaxRep);
+  const void* fns[] = {(const void*)attn_split_kernel<4>,  (const void*)attn_split_kernel<8>,
+                       (const void*)attn_split_kernel<16>, (const void*)attn_split_kernel<32>,
+                       (const void*)attn_split_kernel<64>, (const void*)attn_split_kernel<128>};
+  for (const void* f : fns) {
+    const cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
 bool attn_split_fits(int64_t head_dim, int64_t n_head, int64_t n_head_kv) {
   return head_dim >= 4 && head_dim <= kSplitMaxD && (head_dim & (head_dim - 1)) == 0 && n_head > 0 &&
          n_head < (1ll << 31) && n_head_kv > 0 && n_head % n_head_kv == 0 &&
@@ -290,19 +303,7 @@ cudaError_t launch_attn_split(const float* q, const float* ck, const float* cv, 
   (void)et;   // (this mode uses CUDA's expf: its sums are regrouped anyway)
   if (S > kMaxSplits) return cudaErrorInvalidValue;
   const size_t smem = split_smem_bytes((int)D, (int)(H / HKV));
-  static bool smem_set = false;  // (the attributes once; a host call per launch costs microseconds)
   cudaError_t e = cudaSuccess;
-  if (!smem_set) {
-    const int most = (int)split_smem_bytes(kSplitMaxD, kSplitMaxRep);
-    const void* fns[] = {(const void*)attn_split_kernel<4>,  (const void*)attn_split_kernel<8>,
-                         (const void*)attn_split_kernel<16>, (const void*)attn_split_kernel<32>,
-                         (const void*)attn_split_kernel<64>, (const void*)attn_split_kernel<128>};
-    for (const void* f : fns) {
-      e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
-      if (e != cudaSuccess) return e;
-    }
-    smem_set = true;
-  }
   const dim3 grid((unsigned)S, (unsigned)HKV);
   switch (D) {
 #define MI_SPLIT_CASE(DD)                                                                                     \

@@ -717,6 +717,8 @@ cudaError_t prepare_kernels() {
   if (e == cudaSuccess) e = prepare_gemm_tc_kernel();
   if (e == cudaSuccess) e = prepare_qkv_attn_kernel(optin);
   if (e == cudaSuccess) e = prepare_persist_kernel(optin);
+  if (e == cudaSuccess) e = prepare_attn_split_kernels();
+  if (e == cudaSuccess) e = prepare_attn_long_kernels(optin);
   return e;
 }
 

@@ -146,6 +146,8 @@ cudaError_t launch_attn_decode(const AttnParams& p, bool exec_mode, cudaStream_t
 // spec_ordered_sum) and the ordered value chains as three kernels; uses
 // p.scores [n_head][scores_stride] for the scores and then the probabilities.
 bool attn_long_fits(int64_t head_dim, int64_t n_head, int64_t n_head_kv, int64_t n_kv, int optin);
+cudaError_t prepare_attn_long_kernels(int optin);  // per device, at init
+cudaError_t prepare_attn_split_kernels();          // per device, at init
 cudaError_t launch_attn_decode_long(const AttnParams& p, cudaStream_t s);
 
 // Decode attention split over positions (attn_split.cu): a fast mode that
