@@ -259,6 +259,32 @@ def step_trace_summary(kv) -> dict:
 
 
 
+def argmax_agreement(fast: np.ndarray, exact: np.ndarray) -> dict:
+    """Teacher-forced agreement of two [positions, vocab] logit arrays: the
+    share of positions whose greedy argmax matches, the logit error, and the
+    gap-aware check. A flip always needs the two logits involved to move by
+    half the exact gap between them, so the check compares each
+    disagreement's exact gap (exact top logit minus the exact logit of the
+    fast mode's pick) with the TYPICAL error, twice the 99.9th percentile of
+    |fast - exact| over all logits: a disagreement passes only at a near tie,
+    not where a few outlying errors overturned a clear winner. The median
+    exact top-two gap gives the scale of a clear winner."""
+    fa, ea = np.argmax(fast, axis=1), np.argmax(exact, axis=1)
+    rows = np.arange(fast.shape[0])
+    diff = np.abs(fast.astype(np.float64) - exact)
+    mad = float(np.max(diff))
+    typ = float(np.quantile(diff, 0.999))
+    a, b = fast.astype(np.float64).ravel(), exact.astype(np.float64).ravel()
+    cos = float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
+    gaps = (exact[rows, ea] - exact[rows, fa])[fa != ea]
+    top2 = np.sort(exact, axis=1)[:, -2:]
+    return {"teacher_forced": float(np.mean(fa == ea)), "n_positions": int(fast.shape[0]),
+            "disagreements": int(gaps.size), "max_abs_logit_diff": mad, "p999_abs_logit_diff": typ, "cos": cos,
+            "disagree_max_exact_gap": float(gaps.max()) if gaps.size else None,
+            "exact_top2_gap_median": float(np.median(top2[:, 1] - top2[:, 0])),
+            "gap_check": bool(np.all(gaps <= 2 * typ))}
+
+
 def fast_mode_measure(args, kv, seed_tokens, exact_gen, stream, dist, local: int, world: int, hp,
                       peak: float, peak_kind: str) -> dict:
     """The labelled fast mode of the decode step (mi_cuda_qwen2_set_fast_mode:
@@ -305,12 +331,6 @@ def fast_mode_measure(args, kv, seed_tokens, exact_gen, stream, dist, local: int
     fast = teacher_forced()
     kv.set_fast_mode(False)
     exact = teacher_forced()
-    fa, ea = np.argmax(fast, axis=1), np.argmax(exact, axis=1)
-    rows = np.arange(PERIOD)
-    mad = float(np.max(np.abs(fast.astype(np.float64) - exact)))
-    a, b = fast.astype(np.float64).ravel(), exact.astype(np.float64).ravel()
-    cos = float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
-    gaps = (exact[rows, ea] - exact[rows, fa])[fa != ea]
     n_kvs = [N_PROMPT + (i % PERIOD) + 1 for i in range(args.steps)]
     achieved = sum(step_bytes(hp, n) for n in n_kvs) / (ms / 1e3) / 1e9
     out = {
@@ -321,10 +341,7 @@ def fast_mode_measure(args, kv, seed_tokens, exact_gen, stream, dist, local: int
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind},
         "argmax_agreement": {
-            "teacher_forced": float(np.mean(fa == ea)), "n_positions": PERIOD, "disagreements": int(gaps.size),
-            "max_abs_logit_diff": mad, "cos": cos,
-            "disagree_max_exact_gap": float(gaps.max()) if gaps.size else None,
-            "gap_check": bool(np.all(gaps <= 2 * mad)),
+            **argmax_agreement(fast, exact),
             "run": "exact run's tokens fed back (positions 32..158), fast vs exact step argmax"},
         "free_run": {"tokens_identical_prefix": prefix, "n_tokens": int(exact_gen.size)},
     }

@@ -70,3 +70,28 @@ def test_decode_config_is_the_same_on_both_arms():
     c = b.decode_config()
     assert c == b.decode_config()
     assert c["n_ctx"] == 2048 and c["prompt"] == 32 and c["n_predict"] == 128
+
+
+def test_fast_mode_argmax_agreement():
+    """The fast-mode object's statistics on crafted logits: a flip at a near
+    tie (gap inside the typical error) passes the gap check; a flip of a clear
+    winner by one outlying error fails it."""
+    import numpy as np
+    b = _bench()
+    rng = np.random.default_rng(0)
+    exact = rng.standard_normal((8, 4000)).astype(np.float32)
+    exact[:, 0] = 10.0                                    # a clear winner at every position
+    noise = (rng.standard_normal(exact.shape) * 1e-3).astype(np.float32)
+    fast = exact + noise                                  # typical error ~3e-3 at the 99.9th percentile
+    exact[3, 1] = 10.0 - 1e-3                             # position 3: a near tie...
+    fast[3, 1] = 10.0 + 1e-3                              # ...that the fast mode resolves the other way
+    fast[3, 0] = 10.0 - 1e-3
+    r = b.argmax_agreement(fast, exact)
+    assert r["n_positions"] == 8 and r["disagreements"] == 1 and r["teacher_forced"] == 7 / 8
+    assert r["gap_check"] and r["disagree_max_exact_gap"] < 2e-3
+    assert r["exact_top2_gap_median"] > 5.0
+    bad = fast.copy()
+    bad[5, 7] = 12.0                                      # one outlier overturns position 5's winner (gap ~10)
+    r2 = b.argmax_agreement(bad, exact)
+    assert r2["disagreements"] == 2 and not r2["gap_check"]
+    assert r2["max_abs_logit_diff"] > 10.0 and r2["p999_abs_logit_diff"] < 0.01
