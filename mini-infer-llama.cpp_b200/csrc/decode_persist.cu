@@ -391,9 +391,17 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
         const float v = __fmul_rn((float)packed_qs(p.embed, E, tok, k >> 5)[k & 31],
                                   packed_scale(p.embed, E, p.embed_npad, tok, k >> 5));
         xs[k] = v;
+        if (!FAST) sq[k] = __fmul_rn(v, v);
       }
     } else {
-      for (int k = tid; k < E / 4; k += kNT) ((float4*)xs)[k] = __ldcg((const float4*)x + k);
+      // x, and (exact mode) its squares for the ordered sum, from the same registers
+      for (int k = tid; k < E / 4; k += kNT) {
+        const float4 v = __ldcg((const float4*)x + k);
+        ((float4*)xs)[k] = v;
+        if (!FAST)
+          ((float4*)sq)[k] = make_float4(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y), __fmul_rn(v.z, v.z),
+                                         __fmul_rn(v.w, v.w));
+      }
     }
     __syncthreads();
     float scale;
@@ -409,8 +417,6 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
       for (int w = 0; w < kNW; w++) ss += red_s[w];
       scale = rsqrtf(ss / (float)E + p.eps);
     } else {
-      for (int k = tid; k < E; k += kNT) sq[k] = __fmul_rn(xs[k], xs[k]);
-      __syncthreads();
       const float ss = spec_ordered_sum<kNT, 2>(sq, E, smem + L.spec);
       if (tid == 0) misc[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)E), p.eps)));
       __syncthreads();
@@ -752,7 +758,7 @@ __global__ void __launch_bounds__(kNT, 1) persist_step_kernel(const PersistParam
           if (grp < NG)
             for (int i = grp; i < rows; i += NG) acc = fmaf(Vs[(size_t)i * D + o_el], sc[c0 + i], acc);
         } else {
-          if (tid < D) acc = ordered_dot_scaled(acc, Vs + tid, D, sc + c0, inv, rows);
+          if (tid < D) acc = ordered_dot_scaled_pp(acc, Vs + tid, D, sc + c0, inv, rows);
         }
       }
       if constexpr (FAST) {

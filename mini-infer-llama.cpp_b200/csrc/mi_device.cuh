@@ -346,6 +346,41 @@ __device__ __forceinline__ float ordered_dot_scaled(float acc, const float* v, i
   return acc;
 }
 
+// ordered_dot_scaled with two 16-term register batches in ping-pong: the
+// loads of the next batch are in flight while the current batch's dependent
+// adds run. Same terms, same order, same roundings.
+__device__ __forceinline__ float ordered_dot_scaled_pp(float acc, const float* v, int vs, const float* p, float s,
+                                                      int n) {
+  int t = 0;
+  if (n >= 32) {
+    float a0[16], b0[16], a1[16], b1[16];
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+      a0[u] = v[(size_t)u * vs];
+      b0[u] = __fmul_rn(p[u], s);
+    }
+    for (; t + 32 <= n; t += 32) {
+#pragma unroll
+      for (int u = 0; u < 16; u++) {
+        a1[u] = v[(size_t)(t + 16 + u) * vs];
+        b1[u] = __fmul_rn(p[t + 16 + u], s);
+      }
+#pragma unroll
+      for (int u = 0; u < 16; u++) acc = __fadd_rn(acc, __fmul_rn(a0[u], b0[u]));
+      if (t + 48 <= n) {
+#pragma unroll
+        for (int u = 0; u < 16; u++) {
+          a0[u] = v[(size_t)(t + 32 + u) * vs];
+          b0[u] = __fmul_rn(p[t + 32 + u], s);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 16; u++) acc = __fadd_rn(acc, __fmul_rn(a1[u], b1[u]));
+    }
+  }
+  return ordered_dot_scaled(acc, v + (size_t)t * vs, vs, p + t, s, n - t);
+}
+
 // One lane's accumulator chain of the Q8_0 dot over n blocks of a 4-row group
 // held in shared memory in the packed layout (block i: quants gq[i*32 + lane],
 // scales gd[i*4 + rr]) against the quantized activation (aq4 words, ad scales,
