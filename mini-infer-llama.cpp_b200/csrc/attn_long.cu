@@ -20,8 +20,6 @@
 // K and V must be 16-byte aligned (the router checks).
 // The chains of step 3 (n_kv dependent adds each) set the floor: ~4-5 cycles
 // per position.
-#include <algorithm>
-
 #include "mi_device.cuh"
 
 namespace mi {
