@@ -57,6 +57,9 @@ def test_errors_are_status_codes_not_aborts():
     assert b"null" in L.mi_cuda_last_error()
     rc = L.mi_cuda_kv_cache_init(None, 16, None)
     assert rc == mi_cuda.ERR_ARG
+    # the fast-mode switch: no KV cache, or a value other than 0 / 1
+    assert L.mi_cuda_qwen2_set_fast_mode(None, 1) == mi_cuda.ERR_ARG
+    assert L.mi_cuda_qwen2_fast_mode(None) == 0
 
 
 def test_device_required_for_compute():
