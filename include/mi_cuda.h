@@ -151,8 +151,11 @@ int mi_cuda_attn_kqv(const float* d_probs, const float* d_cache_v, int64_t head_
                      float* d_dst, mi_cuda_stream s);
 
 /* The three attention nodes of one decode step (ref src/model_qwen2.cpp:170-172,
- * n_tokens = 1, n_past = n_kv - 1) fused in one launch: q [n_head][hd] already
- * rotated, caches hold positions [0, n_kv). d_scratch holds
+ * n_tokens = 1, n_past = n_kv - 1), every sum in the reference's order: q
+ * [n_head][hd] already rotated, caches hold positions [0, n_kv). One launch;
+ * from 512 positions (with 16-byte aligned caches and hd a multiple of 4)
+ * three launches that spread the scores, the softmax and the ordered value
+ * chains over the GPU -- same results. d_scratch holds
  * mi_cuda_attention_decode_scratch_bytes() bytes; dst [n_head][hd]. */
 size_t mi_cuda_attention_decode_scratch_bytes(int64_t n_head, int64_t n_kv);
 int mi_cuda_attention_decode(const float* d_q, const float* d_cache_k, const float* d_cache_v,
@@ -161,11 +164,12 @@ int mi_cuda_attention_decode(const float* d_q, const float* d_cache_k, const flo
 
 /* No counterpart in the reference: a fast mode of mi_cuda_attention_decode
  * (same inputs and output layout) that splits the positions over many CTAs and
- * combines their partial softmax sums. Each score and exponential is the
- * reference's, but the denominator and value sums are regrouped, so results
- * differ from the reference's in the last bits (|error| ~1e-7 relative on
- * N(0,1) data). head_dim <= 128 and a multiple of 4, n_head / n_head_kv <= 16.
- * d_scratch holds mi_cuda_attention_decode_split_scratch_bytes() bytes. */
+ * combines their partial softmax sums. The scores are fused dot products, the
+ * exponentials CUDA's expf, the denominator and value sums regrouped, so
+ * results differ from the reference's in the last bits (within max-abs 1e-5
+ * on N(0,1) data). head_dim a power of two <= 128, n_head / n_head_kv <= 16,
+ * caches and scratch 16-byte aligned. d_scratch holds
+ * mi_cuda_attention_decode_split_scratch_bytes() bytes. */
 size_t mi_cuda_attention_decode_split_scratch_bytes(int64_t n_head, int64_t n_head_kv, int64_t n_kv,
                                                     int64_t head_dim);
 int mi_cuda_attention_decode_split(const float* d_q, const float* d_cache_k, const float* d_cache_v,
