@@ -77,8 +77,8 @@ PUBLISHED_BEST = 64.035  # reference Q8_0 decode tok/s, 4 threads (reference REA
 # dram__bytes_write.sum of one launch of the persistent step kernel (the whole
 # step) at n_kv = 34, from an ncu capture of this build;
 # profiles/decode_step_qwen2_05b.md gives the command and the figures.
-TRAFFIC_PER_STEP = 531_213_824
-TRAFFIC_SOURCE = "ncu dram__bytes_read+write of one persistent-step launch at n_kv 34 (527.6 MB read, 3.6 MB written)"
+TRAFFIC_PER_STEP = 531_855_872
+TRAFFIC_SOURCE = "ncu dram__bytes_read+write of one persistent-step launch at n_kv 34 (527.1 MB read, 4.7 MB written)"
 
 
 def step_bytes(hp, n_kv: int) -> int:
